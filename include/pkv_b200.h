@@ -1,0 +1,275 @@
+/*
+ * pkv_b200.h -- C ABI of the B200 (sm_100a) paged GQA decode-attention engine.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (passed as void*, i.e. a cudaStream_t / CUstream handle; NULL = legacy
+ * default stream).  Nothing here allocates device memory: q, the paged K/V
+ * cache, metadata, output and workspace all belong to the caller, exactly as
+ * in the reference's PyTorch operator surface.  Calls are asynchronous on the
+ * given stream and return a status instead of raising or exiting.
+ *
+ * Layouts (identical to the reference, tests/persistentkv_torch_extension.cu):
+ *   q / q_source   [rows, Hq, 128]            fp16 or bf16, contiguous
+ *   k_pages/v_pages[physical_pages, Hkv, page_size, 128]
+ *   block_table    [B, max_pages] int32       physical page per logical page
+ *   seq_lens       [B] int32                  tokens per row (masked routes)
+ *   q_indices      [B] int32                  row of q_source read by row b
+ *   out_indices    [B] int32                  row of output written by row b
+ *   work_items     [T, 5] int32               {row, kvh, split, tile_begin,
+ *                                              tile_end}, tiles of 32 tokens
+ *   split_offsets  [B + 1] int32              partial slots of row b are
+ *                                              split_offsets[b] + split
+ *   merge_counters [B, Hkv] int32             zero on entry, zero on return
+ *   workspace      fp32 partial states: m[slots*Hq] | l[slots*Hq] |
+ *                  acc[slots*Hq*128]   (slots = B*num_splits, or
+ *                  total_partial_slots on the work-queue route)
+ */
+#ifndef PKV_B200_H
+#define PKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Only the entry points below are exported from libpkv_b200.so. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define PKV_HEAD_DIM 128   /* reference: kernels/persistentkv_attention.cuh:26 */
+#define PKV_TILE_TOKENS 32 /* work-item tile unit, reference cuh:28          */
+#define PKV_ABI_VERSION 1
+
+typedef enum pkv_status {
+    PKV_OK = 0,
+    PKV_ERR_INVALID_ARGUMENT = 1, /* bad shape / size / null pointer          */
+    PKV_ERR_UNSUPPORTED = 2,      /* head_dim != 128, G not in {1,2,4,8}, ...  */
+    PKV_ERR_MISALIGNED = 3,       /* K/V pool or q not 16-byte aligned         */
+    PKV_ERR_WORKSPACE = 4,        /* workspace missing or too small            */
+    PKV_ERR_CUDA = 5,             /* CUDA runtime / launch error               */
+    PKV_ERR_NO_DEVICE = 6,        /* no sm_100 device current                  */
+    PKV_ERR_CAPACITY = 7          /* output buffer too small (host helpers)    */
+} pkv_status;
+
+typedef enum pkv_dtype {
+    PKV_DTYPE_F16 = 0,
+    PKV_DTYPE_BF16 = 1
+} pkv_dtype;
+
+/* Human-readable name of a status code (static string). */
+const char* pkv_status_string(pkv_status status);
+int pkv_abi_version(void);
+
+/* Thread-local text of the last argument error raised by this library in the
+ * calling thread (mirrors the TORCH_CHECK messages of the reference). */
+const char* pkv_last_error_message(void);
+
+/* ---------------------------------------------------------------------------
+ * Paged decode attention, the four reference operator entry points.
+ * ------------------------------------------------------------------------- */
+
+/* Replaces persistentkv_paged_attention
+ * (reference tests/persistentkv_torch_extension.cu:35-93): every row attends
+ * to exactly `context` tokens.  num_splits > 1 needs
+ * workspace_bytes >= pkv_workspace_bytes(B, Hq, num_splits). */
+pkv_status pkv_paged_attention(
+    const void* q, const void* k_pages, const void* v_pages,
+    const int32_t* block_table, void* output,
+    void* workspace, size_t workspace_bytes,
+    int B, int Hq, int Hkv, int head_dim,
+    int physical_pages, int page_size, int max_pages,
+    int context, int num_splits, pkv_dtype dtype, void* stream);
+
+/* Replaces persistentkv_paged_attention_masked (extension :95-157): row b
+ * attends to seq_lens[b] tokens; split bounds are row-local. */
+pkv_status pkv_paged_attention_masked(
+    const void* q, const void* k_pages, const void* v_pages,
+    const int32_t* block_table, const int32_t* seq_lens, void* output,
+    void* workspace, size_t workspace_bytes,
+    int B, int Hq, int Hkv, int head_dim,
+    int physical_pages, int page_size, int max_pages,
+    int bucket_context, int num_splits, pkv_dtype dtype, void* stream);
+
+/* Replaces persistentkv_paged_attention_indexed (extension :159-228): row b
+ * reads q_source[q_indices[b]] and writes output[out_indices[b]].
+ * q_rows / out_rows are the leading extents of q_source / output. */
+pkv_status pkv_paged_attention_indexed(
+    const void* q_source, const void* k_pages, const void* v_pages,
+    const int32_t* block_table, const int32_t* seq_lens,
+    const int32_t* q_indices, const int32_t* out_indices, void* output,
+    void* workspace, size_t workspace_bytes,
+    int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim,
+    int physical_pages, int page_size, int max_pages,
+    int bucket_context, int num_splits, pkv_dtype dtype, void* stream);
+
+/* Replaces persistentkv_paged_attention_workqueue (extension :230-317): one
+ * task per work item; partial states go to slot split_offsets[row] + split.
+ * fused_merge != 0 merges inside the decode kernel through merge_counters
+ * (the last task of each (row, kvh) merges and resets its counter);
+ * fused_merge == 0 runs the segmented merge kernel afterwards. */
+pkv_status pkv_paged_attention_workqueue(
+    const void* q_source, const void* k_pages, const void* v_pages,
+    const int32_t* block_table, const int32_t* seq_lens,
+    const int32_t* work_items, const int32_t* split_offsets,
+    int32_t* merge_counters,
+    const int32_t* q_indices, const int32_t* out_indices, void* output,
+    void* workspace, size_t workspace_bytes,
+    int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim,
+    int physical_pages, int page_size, int max_pages,
+    int bucket_context, int num_tasks, int total_partial_slots,
+    int fused_merge, pkv_dtype dtype, void* stream);
+
+/* Same as pkv_paged_attention_workqueue, but instead of the normalised
+ * output it writes, per row b and query head h, the combined log-sum-exp
+ * state of all of the row's splits to
+ *   state_out[(b * Hq + h) * 130 + {0: m, 1: l, 2..129: acc}]
+ * (m in natural-log units of the scaled scores, l = sum exp(s - m),
+ * acc = sum exp(s - m) v).  Used by sequence sharding across GPUs: each GPU
+ * produces the state of its token range, and pkv_combine_states merges them.
+ * Has no counterpart in the reference (which never crosses a GPU). */
+pkv_status pkv_paged_attention_workqueue_state(
+    const void* q_source, const void* k_pages, const void* v_pages,
+    const int32_t* block_table, const int32_t* seq_lens,
+    const int32_t* work_items, const int32_t* split_offsets,
+    int32_t* merge_counters,
+    const int32_t* q_indices, float* state_out,
+    void* workspace, size_t workspace_bytes,
+    int B, int q_rows, int Hq, int Hkv, int head_dim,
+    int physical_pages, int page_size, int max_pages,
+    int num_tasks, int total_partial_slots,
+    pkv_dtype dtype, void* stream);
+
+/* Merge n_parts state blocks states[part][B][Hq][130] (layout of
+ * pkv_paged_attention_workqueue_state) into output[out_indices[b] or b][Hq][128].
+ * Same arithmetic as the reference's split merge (cuh:719-784). */
+pkv_status pkv_combine_states(
+    const float* states, int n_parts, const int32_t* out_indices,
+    void* output, int B, int out_rows, int Hq, int head_dim,
+    pkv_dtype dtype, void* stream);
+
+/* Bytes of workspace the rectangular routes need: 0 when num_splits <= 1,
+ * else B*Hq*num_splits*(128+2)*4 (reference cuh:891-898). */
+size_t pkv_workspace_bytes(int B, int Hq, int num_splits);
+
+/* Bytes of workspace the work-queue route needs for total_partial_slots
+ * partial states (reference cuh:916-927 layout). */
+size_t pkv_workqueue_workspace_bytes(int total_partial_slots, int Hq);
+
+/* Reads (and optionally clears) the device-side error word of the current
+ * device.  Kernels never trap: an out-of-range page id, row, slot or index,
+ * or a pipeline wait that exceeded its time limit, sets a bit here and the
+ * affected loads/stores are skipped.  Synchronises the device. */
+pkv_status pkv_device_error(uint32_t* code, int clear);
+
+#define PKV_DEVERR_PAGE_ID     0x1u  /* block_table entry outside [0, P)     */
+#define PKV_DEVERR_LOGICAL_PAGE 0x2u /* token beyond max_pages * page_size   */
+#define PKV_DEVERR_WORK_ITEM   0x4u  /* row/kvh/tile range out of range      */
+#define PKV_DEVERR_SLOT        0x8u  /* partial slot >= total_partial_slots  */
+#define PKV_DEVERR_INDEX       0x10u /* q_indices / out_indices out of range */
+#define PKV_DEVERR_TIMEOUT     0x20u /* bounded pipeline wait expired        */
+
+/* ---------------------------------------------------------------------------
+ * Host-side scheduler: work-queue builder and split-count router.
+ * ------------------------------------------------------------------------- */
+
+typedef enum pkv_split_policy {
+    /* choose_workqueue_row_splits of the reference
+     * (tests/benchmark_serving_trace.py:370-393), clamped so that no split is
+     * empty (the reference can leave partial slots unwritten). */
+    PKV_SPLITS_REFERENCE = 0,
+    /* B200 policy: split rows so the tasks fill sm_count * ctas_per_sm
+     * evenly-sized tasks (see pkv_router_params). */
+    PKV_SPLITS_BALANCED = 1,
+    /* every row uses exactly `requested_splits` splits (clamped to tiles). */
+    PKV_SPLITS_FIXED = 2
+} pkv_split_policy;
+
+typedef struct pkv_router_params {
+    int hq;                 /* query heads (reference HQ = 32)                 */
+    int hkv;                /* KV heads (reference HKV = 8)                    */
+    int head_dim;           /* 128                                             */
+    int elem_bytes;         /* 2 for fp16 / bf16                               */
+    int sm_count;           /* reference SM_COUNT = 28; B200: 148              */
+    double read_gbps;       /* reference ROOFLINE_READ_GBPS = 302              */
+    double launch_us;       /* reference LAUNCH_OVERHEAD_US = 8                */
+    double min_ctas_per_sm; /* reference MIN_CTAS_PER_SM = 4                   */
+    int supported_g;        /* router GQA gate: only this G takes the split
+                               routes (reference SUPPORTED_PERSISTENTKV_GQA=4);
+                               0 = every G                                      */
+    int min_split_len;      /* below this max length the router keeps the
+                               single-pass route (reference: 16384)             */
+    int ctas_per_sm;        /* resident decode CTAs per SM (balanced policy)   */
+    int tasks_per_cta;      /* tasks per resident CTA slot (balanced policy)   */
+    int max_splits;         /* cap on splits per row (balanced policy)         */
+    int min_tiles_per_task; /* lower bound on task size (balanced policy)      */
+} pkv_router_params;
+
+/* Fills p with the reference constants (benchmark_serving_trace.py:33-43). */
+void pkv_router_params_reference(pkv_router_params* p);
+/* Fills p with constants calibrated for one B200 (148 SMs). */
+void pkv_router_params_b200(pkv_router_params* p);
+
+/* reference choose_workqueue_row_splits (benchmark_serving_trace.py:370-393),
+ * unclamped (may exceed the row's tile count, exactly as the reference). */
+int pkv_choose_workqueue_row_splits(const pkv_router_params* p, int length,
+                                    int active_count, int requested_splits,
+                                    int auto_splits);
+
+/* reference choose_splits (benchmark_serving_trace.py:328-367). */
+int pkv_choose_splits(const pkv_router_params* p, const int32_t* lengths,
+                      int n, int requested_splits, int auto_splits,
+                      int single_bucket);
+
+/* reference model_bucket_splits (:396-402) and model_workqueue_splits
+ * (:405-415). */
+int pkv_model_bucket_splits(const pkv_router_params* p, const int32_t* lengths,
+                            int n);
+int pkv_model_workqueue_splits(const pkv_router_params* p,
+                               const int32_t* lengths, int n);
+
+typedef enum pkv_route {
+    PKV_ROUTE_SINGLE_PASS = 0, /* one task per (row, kvh); the reference's
+                                  "flashinfer" baseline route of the router */
+    PKV_ROUTE_BUCKET = 1,      /* rectangular split grid per length bucket   */
+    PKV_ROUTE_WORKQUEUE = 2    /* compact work queue                          */
+} pkv_route;
+
+/* reference estimate_route_ms (:418-442). */
+double pkv_estimate_route_ms(const pkv_router_params* p, const int32_t* lengths,
+                             int n, pkv_route route, int splits);
+
+/* reference choose_adaptive_route_cost_model (:445-488), with the
+ * "flashinfer" route of the reference mapped to PKV_ROUTE_SINGLE_PASS.
+ * Writes the chosen splits and estimated milliseconds if non-NULL. */
+pkv_route pkv_choose_route(const pkv_router_params* p, const int32_t* lengths,
+                           int n, int* splits_out, double* est_ms_out);
+
+/* Builds the compact work queue of one decode step, following
+ * compile_persistentkv_metadata (benchmark_serving_trace.py:686-703):
+ * for each row, splits = policy(...), and one item per (non-empty split, kvh)
+ * of {row, kvh, split, tile_begin, tile_end}.  Unlike the reference, splits
+ * are clamped to the row's tile count so every partial slot is written, and a
+ * row with zero tokens gets one empty split (its output becomes zeros).
+ * work_items needs room for max_items * 5 int32, split_offsets for B + 1.
+ * Returns PKV_ERR_CAPACITY if max_items is too small (num_items_out then
+ * holds the required count). */
+pkv_status pkv_build_workqueue(const pkv_router_params* p,
+                               const int32_t* seq_lens, int B,
+                               int active_count, pkv_split_policy policy,
+                               int requested_splits,
+                               int32_t* work_items, int max_items,
+                               int32_t* split_offsets,
+                               int* num_items_out, int* total_slots_out);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PKV_B200_H */

@@ -1,0 +1,168 @@
+"""ctypes binding of ``libpkv_b200.so`` (the C ABI of ``include/pkv_b200.h``).
+
+No torch types cross this boundary: tensors are passed as device pointers plus
+sizes, streams as raw ``cudaStream_t`` handles.  The library must exist; there
+is no fallback path (build it with ``python -m persistentkv_attention_b200.build``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_char_p, c_double, c_int, c_int32, c_size_t, c_uint32, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libpkv_b200.so"
+
+PKV_OK = 0
+PKV_ERR_INVALID_ARGUMENT = 1
+PKV_ERR_UNSUPPORTED = 2
+PKV_ERR_MISALIGNED = 3
+PKV_ERR_WORKSPACE = 4
+PKV_ERR_CUDA = 5
+PKV_ERR_NO_DEVICE = 6
+PKV_ERR_CAPACITY = 7
+
+PKV_DTYPE_F16 = 0
+PKV_DTYPE_BF16 = 1
+
+PKV_SPLITS_REFERENCE = 0
+PKV_SPLITS_BALANCED = 1
+PKV_SPLITS_FIXED = 2
+
+PKV_ROUTE_SINGLE_PASS = 0
+PKV_ROUTE_BUCKET = 1
+PKV_ROUTE_WORKQUEUE = 2
+
+DEVERR_BITS = {
+    0x1: "page id outside the pool",
+    0x2: "token beyond max_pages * page_size",
+    0x4: "work item out of range",
+    0x8: "partial slot out of range",
+    0x10: "q/out index out of range",
+    0x20: "pipeline wait timed out",
+}
+
+
+class RouterParams(ctypes.Structure):
+    """Mirror of ``pkv_router_params``."""
+
+    _fields_ = [
+        ("hq", c_int),
+        ("hkv", c_int),
+        ("head_dim", c_int),
+        ("elem_bytes", c_int),
+        ("sm_count", c_int),
+        ("read_gbps", c_double),
+        ("launch_us", c_double),
+        ("min_ctas_per_sm", c_double),
+        ("supported_g", c_int),
+        ("min_split_len", c_int),
+        ("ctas_per_sm", c_int),
+        ("tasks_per_cta", c_int),
+        ("max_splits", c_int),
+        ("min_tiles_per_task", c_int),
+    ]
+
+
+_P = c_void_p
+_I32P = POINTER(c_int32)
+
+# name -> (restype, argtypes); every function declared in include/pkv_b200.h
+SIGNATURES = {
+    "pkv_status_string": (c_char_p, [c_int]),
+    "pkv_abi_version": (c_int, []),
+    "pkv_last_error_message": (c_char_p, []),
+    "pkv_paged_attention": (
+        c_int,
+        [_P, _P, _P, _P, _P, _P, c_size_t, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+         c_int, c_int, c_int, _P],
+    ),
+    "pkv_paged_attention_masked": (
+        c_int,
+        [_P, _P, _P, _P, _P, _P, _P, c_size_t, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+         c_int, c_int, c_int, _P],
+    ),
+    "pkv_paged_attention_indexed": (
+        c_int,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, c_size_t, c_int, c_int, c_int, c_int, c_int, c_int,
+         c_int, c_int, c_int, c_int, c_int, c_int, _P],
+    ),
+    "pkv_paged_attention_workqueue": (
+        c_int,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, c_size_t, c_int, c_int, c_int, c_int,
+         c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, _P],
+    ),
+    "pkv_paged_attention_workqueue_state": (
+        c_int,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, c_size_t, c_int, c_int, c_int, c_int,
+         c_int, c_int, c_int, c_int, c_int, c_int, c_int, _P],
+    ),
+    "pkv_combine_states": (
+        c_int, [_P, c_int, _P, _P, c_int, c_int, c_int, c_int, c_int, _P]),
+    "pkv_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "pkv_workqueue_workspace_bytes": (c_size_t, [c_int, c_int]),
+    "pkv_device_error": (c_int, [POINTER(c_uint32), c_int]),
+    "pkv_router_params_reference": (None, [POINTER(RouterParams)]),
+    "pkv_router_params_b200": (None, [POINTER(RouterParams)]),
+    "pkv_choose_workqueue_row_splits": (c_int, [POINTER(RouterParams), c_int, c_int, c_int, c_int]),
+    "pkv_choose_splits": (c_int, [POINTER(RouterParams), _I32P, c_int, c_int, c_int, c_int]),
+    "pkv_model_bucket_splits": (c_int, [POINTER(RouterParams), _I32P, c_int]),
+    "pkv_model_workqueue_splits": (c_int, [POINTER(RouterParams), _I32P, c_int]),
+    "pkv_estimate_route_ms": (c_double, [POINTER(RouterParams), _I32P, c_int, c_int, c_int]),
+    "pkv_choose_route": (
+        c_int, [POINTER(RouterParams), _I32P, c_int, POINTER(c_int), POINTER(c_double)]),
+    "pkv_build_workqueue": (
+        c_int,
+        [POINTER(RouterParams), _I32P, c_int, c_int, c_int, c_int, _I32P, c_int, _I32P,
+         POINTER(c_int), POINTER(c_int)],
+    ),
+}
+
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Loads the library once and declares every exported signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python -m persistentkv_attention_b200.build`"
+        )
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (restype, argtypes) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    if lib.pkv_abi_version() != 1:
+        raise ImportError("libpkv_b200.so has an unexpected ABI version")
+    _lib = lib
+    return lib
+
+
+class PkvError(RuntimeError):
+    """Raised for a non-OK status; carries the status code."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+def check(status: int) -> None:
+    if status != PKV_OK:
+        lib = load()
+        msg = lib.pkv_last_error_message().decode() or lib.pkv_status_string(status).decode()
+        raise PkvError(status, msg)
+
+
+def device_error(clear: bool = True) -> int:
+    """Returns (and by default clears) the device error word of the current device."""
+    lib = load()
+    code = c_uint32(0)
+    check(lib.pkv_device_error(ctypes.byref(code), 1 if clear else 0))
+    return int(code.value)
+
+
+def describe_device_error(code: int) -> str:
+    return ", ".join(text for bit, text in DEVERR_BITS.items() if code & bit) or "none"

@@ -1,0 +1,621 @@
+// pkv_api.cu -- C ABI of the B200 paged decode engine (declared in
+// include/pkv_b200.h): argument validation, TMA tensor maps, kernel dispatch.
+//
+// Validation mirrors the reference's operator checks
+// (tests/persistentkv_torch_extension.cu:9-31 and the per-entry TORCH_CHECKs)
+// and the dispatch asserts (kernels/persistentkv_attention.cuh:1036-1045,
+// :1131, :1215-1223), but returns a status plus a thread-local message instead
+// of raising, asserting or exiting.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/pkv_b200.h"
+#include "pkv_kernels.cuh"
+
+using namespace pkv;
+
+// Device-side error word (one per device that loads the library).
+__device__ unsigned int g_pkv_error_word = 0u;
+
+namespace {
+
+constexpr int kSlots = 8;        // ring depth (8 KB per slot)
+constexpr int kCtasPerSm = 2;    // resident decode CTAs per SM
+constexpr int kMaxDevices = 64;
+
+thread_local char t_last_error[512] = "";
+
+pkv_status fail(pkv_status st, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+    va_end(ap);
+    return st;
+}
+
+pkv_status ok_status() {
+    t_last_error[0] = '\0';
+    return PKV_OK;
+}
+
+// ------------------------------------------------------------ device state
+struct DeviceState {
+    std::atomic<int> ready{0};
+    int sm_count = 0;
+    int cc_major = 0;
+    unsigned* error_word = nullptr;
+};
+DeviceState g_devices[kMaxDevices];
+std::mutex g_device_mutex;
+
+pkv_status current_device(DeviceState** out) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        cudaGetLastError();
+        return fail(PKV_ERR_NO_DEVICE, "no CUDA device is available (%s)", cudaGetErrorString(e));
+    }
+    DeviceState& ds = g_devices[dev];
+    if (!ds.ready.load(std::memory_order_acquire)) {
+        std::lock_guard<std::mutex> lock(g_device_mutex);
+        if (!ds.ready.load(std::memory_order_relaxed)) {
+            int sms = 0, major = 0;
+            if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+                cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) !=
+                    cudaSuccess) {
+                cudaGetLastError();
+                return fail(PKV_ERR_NO_DEVICE, "cannot query device %d", dev);
+            }
+            if (major != 10) {
+                return fail(PKV_ERR_NO_DEVICE,
+                            "device %d has compute capability %d.x; this library is built for "
+                            "sm_100a (B200) only",
+                            dev, major);
+            }
+            void* ptr = nullptr;
+            e = cudaGetSymbolAddress(&ptr, g_pkv_error_word);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                return fail(PKV_ERR_CUDA, "cudaGetSymbolAddress(error word) failed: %s",
+                            cudaGetErrorString(e));
+            }
+            ds.sm_count = sms;
+            ds.cc_major = major;
+            ds.error_word = static_cast<unsigned*>(ptr);
+            ds.ready.store(1, std::memory_order_release);
+        }
+    }
+    *out = &ds;
+    return PKV_OK;
+}
+
+// ------------------------------------------------------------ tensor maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        } else {
+            cudaGetLastError();
+        }
+    });
+    return fn;
+}
+
+struct MapCacheEntry {
+    const void* base = nullptr;
+    long long rows = 0;
+    int dtype = -1;
+    int box_rows = 0;
+    CUtensorMap map;
+};
+thread_local MapCacheEntry t_map_cache[8];
+thread_local int t_map_next = 0;
+
+// The pool [P, Hkv, page, 128] is viewed as a 2-D tensor of P*Hkv*page rows of
+// 128 elements; one box is 64 elements (one 128-byte SW128 line) x box_rows.
+pkv_status kv_tensor_map(const void* base, long long rows, pkv_dtype dtype, int box_rows,
+                         CUtensorMap* out) {
+    for (auto& e : t_map_cache) {
+        if (e.base == base && e.rows == rows && e.dtype == (int)dtype && e.box_rows == box_rows) {
+            *out = e.map;
+            return PKV_OK;
+        }
+    }
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return fail(PKV_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    MapCacheEntry& e = t_map_cache[t_map_next];
+    t_map_next = (t_map_next + 1) % 8;
+    cuuint64_t dims[2] = {(cuuint64_t)kHeadDim, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)kRowBytes};
+    cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1u, 1u};
+    CUresult r = fn(&e.map,
+                    dtype == PKV_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                           : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                    2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        e.base = nullptr;
+        return fail(PKV_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+    }
+    e.base = base;
+    e.rows = rows;
+    e.dtype = (int)dtype;
+    e.box_rows = box_rows;
+    *out = e.map;
+    return PKV_OK;
+}
+
+// ------------------------------------------------------------ validation
+struct Common {
+    const void* q;
+    const void* k;
+    const void* v;
+    const int32_t* block_table;
+    int B, Hq, Hkv, head_dim, physical_pages, page_size, max_pages;
+    pkv_dtype dtype;
+};
+
+pkv_status check_common(const Common& c) {
+    if (c.q == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "q must be a CUDA tensor");
+    if (c.k == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "k_pages must be a CUDA tensor");
+    if (c.v == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "v_pages must be a CUDA tensor");
+    if (c.block_table == nullptr)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "block_table must be a CUDA tensor");
+    if (c.dtype != PKV_DTYPE_F16 && c.dtype != PKV_DTYPE_BF16)
+        return fail(PKV_ERR_UNSUPPORTED, "q has wrong dtype");
+    if (c.head_dim != kHeadDim)
+        return fail(PKV_ERR_UNSUPPORTED, "PersistentKV extension currently requires d=128");
+    if (c.Hkv <= 0) return fail(PKV_ERR_INVALID_ARGUMENT, "Hkv must be positive");
+    if (c.Hq % c.Hkv != 0) return fail(PKV_ERR_INVALID_ARGUMENT, "Hq must be divisible by Hkv");
+    const int G = c.Hq / c.Hkv;
+    if (!(G == 1 || G == 2 || G == 4 || G == 8)) {
+        return fail(PKV_ERR_UNSUPPORTED,
+                    "PersistentKV supports G=Hq/Hkv in {1,2,4,8}; got G=%d from Hq=%d Hkv=%d", G,
+                    c.Hq, c.Hkv);
+    }
+    if (c.B < 0) return fail(PKV_ERR_INVALID_ARGUMENT, "batch must be non-negative");
+    if (c.page_size <= 0) return fail(PKV_ERR_INVALID_ARGUMENT, "page_size must be positive");
+    if (c.page_size % 8 != 0) {
+        return fail(PKV_ERR_UNSUPPORTED,
+                    "page_size must be a multiple of 8 tokens on the B200 engine; got %d",
+                    c.page_size);
+    }
+    if (c.physical_pages <= 0)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "k_pages must hold at least one page");
+    if (c.max_pages <= 0)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "block_table must have at least one column");
+    const long long rows = (long long)c.physical_pages * c.Hkv * c.page_size;
+    if (rows >= (1ll << 31)) {
+        return fail(PKV_ERR_UNSUPPORTED,
+                    "K/V pool of %lld token rows exceeds the 2^31 rows one tensor map addresses",
+                    rows);
+    }
+    if ((reinterpret_cast<uintptr_t>(c.k) & 15u) || (reinterpret_cast<uintptr_t>(c.v) & 15u))
+        return fail(PKV_ERR_MISALIGNED, "k_pages and v_pages must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(c.q) & 3u)
+        return fail(PKV_ERR_MISALIGNED, "q must be 4-byte aligned");
+    return PKV_OK;
+}
+
+int box_rows_for(int page_size) { return page_size % 16 == 0 ? 16 : 8; }
+
+// ------------------------------------------------------------ launch
+struct LaunchSpec {
+    DecodeParams dp;
+    bool merge;       // run the separate merge kernel after decode
+    int G;
+    int box_rows;
+    pkv_dtype dtype;
+    const void* k;
+    const void* v;
+    long long rows;
+};
+
+template <int G, typename T, int BR>
+pkv_status launch_typed(const LaunchSpec& ls, const CUtensorMap& tk, const CUtensorMap& tv,
+                        cudaStream_t stream, DeviceState* ds) {
+    auto kern = pkv_decode_kernel<G, T, BR, kSlots>;
+    const size_t smem = decode_smem_bytes<G, kSlots>();
+    static std::atomic<unsigned long long> attr_done{0ull};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (!(attr_done.load(std::memory_order_acquire) & bit)) {
+        cudaError_t e =
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return fail(PKV_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+        }
+        attr_done.fetch_or(bit, std::memory_order_acq_rel);
+    }
+    const int resident = kCtasPerSm * ds->sm_count;
+    const int grid = ls.dp.num_items < resident ? ls.dp.num_items : resident;
+    kern<<<grid, kThreads, smem, stream>>>(ls.dp, tk, tv);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess)
+        return fail(PKV_ERR_CUDA, "decode launch failed: %s", cudaGetErrorString(e));
+    if (ls.merge) {
+        MergeParams mp;
+        mp.part_m = ls.dp.part_m;
+        mp.part_l = ls.dp.part_l;
+        mp.part_acc = ls.dp.part_acc;
+        mp.split_offsets = ls.dp.work_items != nullptr ? ls.dp.split_offsets : nullptr;
+        mp.out_indices = ls.dp.out_indices;
+        mp.out = ls.dp.out;
+        mp.state_out = ls.dp.state_out;
+        mp.error = ls.dp.error;
+        mp.B = ls.dp.B;
+        mp.Hq = ls.dp.Hq;
+        mp.Hkv = ls.dp.Hkv;
+        mp.out_rows = ls.dp.out_rows;
+        mp.num_splits = ls.dp.num_splits;
+        mp.total_slots = ls.dp.total_slots;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(ls.dp.Hkv, ls.dp.B);
+        cfg.blockDim = dim3(kHeadDim);
+        cfg.dynamicSmemBytes = 0;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, pkv_merge_kernel<G, T>, mp);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return fail(PKV_ERR_CUDA, "merge launch failed: %s", cudaGetErrorString(e));
+        }
+    }
+    return ok_status();
+}
+
+template <typename T, int BR>
+pkv_status launch_g(const LaunchSpec& ls, const CUtensorMap& tk, const CUtensorMap& tv,
+                    cudaStream_t s, DeviceState* ds) {
+    switch (ls.G) {
+        case 1: return launch_typed<1, T, BR>(ls, tk, tv, s, ds);
+        case 2: return launch_typed<2, T, BR>(ls, tk, tv, s, ds);
+        case 4: return launch_typed<4, T, BR>(ls, tk, tv, s, ds);
+        case 8: return launch_typed<8, T, BR>(ls, tk, tv, s, ds);
+        default: return fail(PKV_ERR_UNSUPPORTED, "unsupported G=%d", ls.G);
+    }
+}
+
+pkv_status launch(LaunchSpec& ls, void* stream_ptr) {
+    if (ls.dp.num_items <= 0) return ok_status();
+    DeviceState* ds = nullptr;
+    pkv_status st = current_device(&ds);
+    if (st != PKV_OK) return st;
+    ls.dp.error = ds->error_word;
+    CUtensorMap tk, tv;
+    st = kv_tensor_map(ls.k, ls.rows, ls.dtype, ls.box_rows, &tk);
+    if (st != PKV_OK) return st;
+    st = kv_tensor_map(ls.v, ls.rows, ls.dtype, ls.box_rows, &tv);
+    if (st != PKV_OK) return st;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    if (ls.dtype == PKV_DTYPE_F16) {
+        return ls.box_rows == 16 ? launch_g<__half, 16>(ls, tk, tv, stream, ds)
+                                 : launch_g<__half, 8>(ls, tk, tv, stream, ds);
+    }
+    return ls.box_rows == 16 ? launch_g<__nv_bfloat16, 16>(ls, tk, tv, stream, ds)
+                             : launch_g<__nv_bfloat16, 8>(ls, tk, tv, stream, ds);
+}
+
+void fill_common(LaunchSpec& ls, const Common& c) {
+    std::memset(&ls.dp, 0, sizeof(ls.dp));
+    ls.dp.q = c.q;
+    ls.dp.block_table = c.block_table;
+    ls.dp.B = c.B;
+    ls.dp.Hq = c.Hq;
+    ls.dp.Hkv = c.Hkv;
+    ls.dp.num_pages = c.physical_pages;
+    ls.dp.page_size = c.page_size;
+    ls.dp.max_pages = c.max_pages;
+    ls.dp.scale_log2 = (1.0f / sqrtf((float)kHeadDim)) * kLog2e;
+    ls.G = c.Hq / c.Hkv;
+    ls.box_rows = box_rows_for(c.page_size);
+    ls.dtype = c.dtype;
+    ls.k = c.k;
+    ls.v = c.v;
+    ls.rows = (long long)c.physical_pages * c.Hkv * c.page_size;
+    ls.merge = false;
+}
+
+void partition_workspace(DecodeParams& dp, void* ws, long long slots) {
+    float* base = static_cast<float*>(ws);
+    dp.part_m = base;
+    dp.part_l = base + slots * dp.Hq;
+    dp.part_acc = base + 2 * slots * dp.Hq;
+}
+
+// Shared body of the three rectangular entry points.
+pkv_status rectangular(const Common& c, const int32_t* seq_lens, const int32_t* q_indices,
+                       const int32_t* out_indices, void* output, void* workspace,
+                       size_t workspace_bytes, int q_rows, int out_rows, int context,
+                       const char* context_name, int num_splits, void* stream) {
+    pkv_status st = check_common(c);
+    if (st != PKV_OK) return st;
+    if (output == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "output must be a CUDA tensor");
+    if (context <= 0) return fail(PKV_ERR_INVALID_ARGUMENT, "%s must be positive", context_name);
+    if (num_splits <= 0) return fail(PKV_ERR_INVALID_ARGUMENT, "num_splits must be positive");
+    const long long pages_needed = ((long long)context + c.page_size - 1) / c.page_size;
+    if (c.max_pages < pages_needed) {
+        return fail(PKV_ERR_INVALID_ARGUMENT,
+                    "block_table has %d pages per row but %s=%d needs %lld", c.max_pages,
+                    context_name, context, pages_needed);
+    }
+    const int total_tiles = (context + kTileTokens - 1) / kTileTokens;
+    if (num_splits > total_tiles) {
+        return fail(PKV_ERR_INVALID_ARGUMENT,
+                    "num_splits=%d exceeds the %d tiles of %s=%d", num_splits, total_tiles,
+                    context_name, context);
+    }
+    if (num_splits > 1) {
+        const size_t need = pkv_workspace_bytes(c.B, c.Hq, num_splits);
+        if (workspace == nullptr)
+            return fail(PKV_ERR_WORKSPACE, "Split dispatch requires workspace");
+        if (workspace_bytes < need) {
+            return fail(PKV_ERR_WORKSPACE, "workspace holds %zu bytes but %zu are needed",
+                        workspace_bytes, need);
+        }
+        if (reinterpret_cast<uintptr_t>(workspace) & 3u)
+            return fail(PKV_ERR_MISALIGNED, "workspace must be 4-byte aligned");
+    }
+    if (q_rows <= 0 || out_rows <= 0) {
+        if (c.B == 0) return ok_status();
+        return fail(PKV_ERR_INVALID_ARGUMENT, "q and output must have at least one row");
+    }
+    if (c.B == 0) return ok_status();
+    LaunchSpec ls;
+    fill_common(ls, c);
+    ls.dp.out = output;
+    ls.dp.seq_lens = seq_lens;
+    ls.dp.q_indices = q_indices;
+    ls.dp.out_indices = out_indices;
+    ls.dp.q_rows = q_rows;
+    ls.dp.out_rows = out_rows;
+    ls.dp.context = context;
+    ls.dp.num_splits = num_splits;
+    ls.dp.num_items = c.B * c.Hkv * num_splits;
+    ls.dp.total_slots = c.B * num_splits;
+    if (num_splits > 1) {
+        partition_workspace(ls.dp, workspace, (long long)c.B * num_splits);
+        ls.merge = true;
+    }
+    return launch(ls, stream);
+}
+
+pkv_status workqueue_common(const Common& c, const int32_t* seq_lens, const int32_t* work_items,
+                            const int32_t* split_offsets, int32_t* merge_counters,
+                            const int32_t* q_indices, const int32_t* out_indices, void* output,
+                            float* state_out, void* workspace, size_t workspace_bytes,
+                            int q_rows, int out_rows, int bucket_context, int num_tasks,
+                            int total_partial_slots, int fused_merge, void* stream) {
+    pkv_status st = check_common(c);
+    if (st != PKV_OK) return st;
+    if (seq_lens == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "seq_lens must be a CUDA tensor");
+    if (work_items == nullptr)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "work_items must be a CUDA tensor");
+    if (split_offsets == nullptr)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "split_offsets must be a CUDA tensor");
+    if (q_indices == nullptr)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "q_indices must be a CUDA tensor");
+    if (output == nullptr && state_out == nullptr)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "output must be a CUDA tensor");
+    if (state_out == nullptr && out_indices == nullptr)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "out_indices must be a CUDA tensor");
+    if (fused_merge && merge_counters == nullptr)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "merge_counters must be a CUDA tensor");
+    if (bucket_context <= 0)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "bucket_context must be positive");
+    if (num_tasks <= 0) return fail(PKV_ERR_INVALID_ARGUMENT, "work_items must not be empty");
+    if (total_partial_slots <= 0)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "total_partial_slots must be positive");
+    if (workspace == nullptr)
+        return fail(PKV_ERR_WORKSPACE, "Workqueue dispatch requires workspace");
+    const size_t need = pkv_workqueue_workspace_bytes(total_partial_slots, c.Hq);
+    if (workspace_bytes < need) {
+        return fail(PKV_ERR_WORKSPACE, "workspace holds %zu bytes but %zu are needed",
+                    workspace_bytes, need);
+    }
+    if (reinterpret_cast<uintptr_t>(workspace) & 3u)
+        return fail(PKV_ERR_MISALIGNED, "workspace must be 4-byte aligned");
+    if (q_rows <= 0) return fail(PKV_ERR_INVALID_ARGUMENT, "q_source must have at least one row");
+    if (state_out == nullptr && out_rows <= 0)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "output must have at least one row");
+    if (c.B <= 0) return fail(PKV_ERR_INVALID_ARGUMENT, "block_table batch must be positive");
+    LaunchSpec ls;
+    fill_common(ls, c);
+    ls.dp.out = state_out == nullptr ? output : nullptr;
+    ls.dp.state_out = state_out;
+    ls.dp.seq_lens = seq_lens;
+    ls.dp.q_indices = q_indices;
+    ls.dp.out_indices = state_out == nullptr ? out_indices : nullptr;
+    ls.dp.work_items = work_items;
+    ls.dp.split_offsets = split_offsets;
+    ls.dp.merge_counters = fused_merge ? merge_counters : nullptr;
+    ls.dp.q_rows = q_rows;
+    ls.dp.out_rows = state_out == nullptr ? out_rows : c.B;
+    ls.dp.context = bucket_context;
+    ls.dp.num_splits = 1;
+    ls.dp.num_items = num_tasks;
+    ls.dp.total_slots = total_partial_slots;
+    partition_workspace(ls.dp, workspace, total_partial_slots);
+    ls.merge = !fused_merge;
+    return launch(ls, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* pkv_status_string(pkv_status status) {
+    switch (status) {
+        case PKV_OK: return "PKV_OK";
+        case PKV_ERR_INVALID_ARGUMENT: return "PKV_ERR_INVALID_ARGUMENT";
+        case PKV_ERR_UNSUPPORTED: return "PKV_ERR_UNSUPPORTED";
+        case PKV_ERR_MISALIGNED: return "PKV_ERR_MISALIGNED";
+        case PKV_ERR_WORKSPACE: return "PKV_ERR_WORKSPACE";
+        case PKV_ERR_CUDA: return "PKV_ERR_CUDA";
+        case PKV_ERR_NO_DEVICE: return "PKV_ERR_NO_DEVICE";
+        case PKV_ERR_CAPACITY: return "PKV_ERR_CAPACITY";
+    }
+    return "PKV_ERR_UNKNOWN";
+}
+
+int pkv_abi_version(void) { return PKV_ABI_VERSION; }
+
+const char* pkv_last_error_message(void) { return t_last_error; }
+
+size_t pkv_workspace_bytes(int B, int Hq, int num_splits) {
+    if (num_splits <= 1 || B <= 0 || Hq <= 0) return 0;
+    return (size_t)B * Hq * num_splits * (kHeadDim + 2) * sizeof(float);
+}
+
+size_t pkv_workqueue_workspace_bytes(int total_partial_slots, int Hq) {
+    if (total_partial_slots <= 0 || Hq <= 0) return 0;
+    return (size_t)total_partial_slots * Hq * (kHeadDim + 2) * sizeof(float);
+}
+
+pkv_status pkv_paged_attention(const void* q, const void* k_pages, const void* v_pages,
+                               const int32_t* block_table, void* output, void* workspace,
+                               size_t workspace_bytes, int B, int Hq, int Hkv, int head_dim,
+                               int physical_pages, int page_size, int max_pages, int context,
+                               int num_splits, pkv_dtype dtype, void* stream) {
+    Common c{q, k_pages, v_pages, block_table, B, Hq, Hkv, head_dim,
+             physical_pages, page_size, max_pages, dtype};
+    return rectangular(c, nullptr, nullptr, nullptr, output, workspace, workspace_bytes, B, B,
+                       context, "context", num_splits, stream);
+}
+
+pkv_status pkv_paged_attention_masked(const void* q, const void* k_pages, const void* v_pages,
+                                      const int32_t* block_table, const int32_t* seq_lens,
+                                      void* output, void* workspace, size_t workspace_bytes,
+                                      int B, int Hq, int Hkv, int head_dim, int physical_pages,
+                                      int page_size, int max_pages, int bucket_context,
+                                      int num_splits, pkv_dtype dtype, void* stream) {
+    if (seq_lens == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "seq_lens must be a CUDA tensor");
+    Common c{q, k_pages, v_pages, block_table, B, Hq, Hkv, head_dim,
+             physical_pages, page_size, max_pages, dtype};
+    return rectangular(c, seq_lens, nullptr, nullptr, output, workspace, workspace_bytes, B, B,
+                       bucket_context, "bucket_context", num_splits, stream);
+}
+
+pkv_status pkv_paged_attention_indexed(const void* q_source, const void* k_pages,
+                                       const void* v_pages, const int32_t* block_table,
+                                       const int32_t* seq_lens, const int32_t* q_indices,
+                                       const int32_t* out_indices, void* output, void* workspace,
+                                       size_t workspace_bytes, int B, int q_rows, int out_rows,
+                                       int Hq, int Hkv, int head_dim, int physical_pages,
+                                       int page_size, int max_pages, int bucket_context,
+                                       int num_splits, pkv_dtype dtype, void* stream) {
+    if (seq_lens == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "seq_lens must be a CUDA tensor");
+    if (q_indices == nullptr)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "q_indices must be a CUDA tensor");
+    if (out_indices == nullptr)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "out_indices must be a CUDA tensor");
+    Common c{q_source, k_pages, v_pages, block_table, B, Hq, Hkv, head_dim,
+             physical_pages, page_size, max_pages, dtype};
+    return rectangular(c, seq_lens, q_indices, out_indices, output, workspace, workspace_bytes,
+                       q_rows, out_rows, bucket_context, "bucket_context", num_splits, stream);
+}
+
+pkv_status pkv_paged_attention_workqueue(
+    const void* q_source, const void* k_pages, const void* v_pages, const int32_t* block_table,
+    const int32_t* seq_lens, const int32_t* work_items, const int32_t* split_offsets,
+    int32_t* merge_counters, const int32_t* q_indices, const int32_t* out_indices, void* output,
+    void* workspace, size_t workspace_bytes, int B, int q_rows, int out_rows, int Hq, int Hkv,
+    int head_dim, int physical_pages, int page_size, int max_pages, int bucket_context,
+    int num_tasks, int total_partial_slots, int fused_merge, pkv_dtype dtype, void* stream) {
+    Common c{q_source, k_pages, v_pages, block_table, B, Hq, Hkv, head_dim,
+             physical_pages, page_size, max_pages, dtype};
+    return workqueue_common(c, seq_lens, work_items, split_offsets, merge_counters, q_indices,
+                            out_indices, output, nullptr, workspace, workspace_bytes, q_rows,
+                            out_rows, bucket_context, num_tasks, total_partial_slots, fused_merge,
+                            stream);
+}
+
+pkv_status pkv_paged_attention_workqueue_state(
+    const void* q_source, const void* k_pages, const void* v_pages, const int32_t* block_table,
+    const int32_t* seq_lens, const int32_t* work_items, const int32_t* split_offsets,
+    int32_t* merge_counters, const int32_t* q_indices, float* state_out, void* workspace,
+    size_t workspace_bytes, int B, int q_rows, int Hq, int Hkv, int head_dim, int physical_pages,
+    int page_size, int max_pages, int num_tasks, int total_partial_slots, pkv_dtype dtype,
+    void* stream) {
+    if (state_out == nullptr)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "state_out must be a CUDA tensor");
+    Common c{q_source, k_pages, v_pages, block_table, B, Hq, Hkv, head_dim,
+             physical_pages, page_size, max_pages, dtype};
+    return workqueue_common(c, seq_lens, work_items, split_offsets, merge_counters, q_indices,
+                            nullptr, nullptr, state_out, workspace, workspace_bytes, q_rows, B,
+                            max_pages * page_size, num_tasks, total_partial_slots,
+                            merge_counters != nullptr, stream);
+}
+
+pkv_status pkv_combine_states(const float* states, int n_parts, const int32_t* out_indices,
+                              void* output, int B, int out_rows, int Hq, int head_dim,
+                              pkv_dtype dtype, void* stream) {
+    if (states == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "states must be a CUDA tensor");
+    if (output == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "output must be a CUDA tensor");
+    if (head_dim != kHeadDim)
+        return fail(PKV_ERR_UNSUPPORTED, "PersistentKV extension currently requires d=128");
+    if (n_parts <= 0) return fail(PKV_ERR_INVALID_ARGUMENT, "n_parts must be positive");
+    if (Hq <= 0 || B < 0 || out_rows <= 0)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "invalid state shape");
+    if (dtype != PKV_DTYPE_F16 && dtype != PKV_DTYPE_BF16)
+        return fail(PKV_ERR_UNSUPPORTED, "output has wrong dtype");
+    if (B == 0) return ok_status();
+    DeviceState* ds = nullptr;
+    pkv_status st = current_device(&ds);
+    if (st != PKV_OK) return st;
+    cudaStream_t stream_h = static_cast<cudaStream_t>(stream);
+    dim3 grid(Hq, B);
+    if (dtype == PKV_DTYPE_F16) {
+        pkv_combine_states_kernel<__half><<<grid, kHeadDim, 0, stream_h>>>(
+            states, n_parts, out_indices, output, B, out_rows, Hq, ds->error_word);
+    } else {
+        pkv_combine_states_kernel<__nv_bfloat16><<<grid, kHeadDim, 0, stream_h>>>(
+            states, n_parts, out_indices, output, B, out_rows, Hq, ds->error_word);
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess)
+        return fail(PKV_ERR_CUDA, "combine launch failed: %s", cudaGetErrorString(e));
+    return ok_status();
+}
+
+pkv_status pkv_device_error(uint32_t* code, int clear) {
+    if (code == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "code must not be null");
+    DeviceState* ds = nullptr;
+    pkv_status st = current_device(&ds);
+    if (st != PKV_OK) return st;
+    unsigned value = 0;
+    cudaError_t e = cudaMemcpy(&value, ds->error_word, sizeof(value), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && clear) e = cudaMemset(ds->error_word, 0, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(PKV_ERR_CUDA, "reading the device error word failed: %s",
+                    cudaGetErrorString(e));
+    }
+    *code = value;
+    return ok_status();
+}
+
+}  // extern "C"

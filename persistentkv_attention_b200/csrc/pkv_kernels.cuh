@@ -1,0 +1,672 @@
+// pkv_kernels.cuh -- paged GQA decode attention for B200 (sm_100a).
+//
+// One kernel covers the reference's decode paths (kernels/persistentkv_attention.cuh
+// persistentkv_decode_kernel, :270-717): rectangular split grids (:292-338), the
+// compact work queue (:300-307), row-local masking by seq_lens (:330-337),
+// q/out row indirection (:308, :633-634), partial-state or final-output writes
+// (:615-646) and the fused last-CTA merge (:648-716).  The two merge kernels
+// restate persistentkv_merge_splits_kernel / _workqueue_kernel (:719-784).
+//
+// Design (B200-first, not a translation):
+//  * warp-specialised CTA: warp 4 is a TMA producer, warps 0-3 are consumers;
+//  * the producer resolves block_table entries 32 boxes at a time and streams
+//    16-token K/V boxes (2 x 64-element SW128 halves each for K and V) with
+//    cp.async.bulk.tensor into an NSLOTS-deep mbarrier ring (8 KB per slot);
+//  * each consumer warp owns whole 16-token stages: S^T = K Q^T with
+//    mma.m16n8k16 (tokens x padded GQA group x head_dim), fp32 online
+//    softmax in the log2 domain, P^T moved into B-fragment layout with
+//    movmatrix, O^T += V^T P^T with ldmatrix.trans fragments;
+//  * per-warp softmax states are combined through shared memory at the end of
+//    each work item, then written as a partial state or as the final output;
+//  * the CTA loops over work items (grid-stride) so one launch can run with a
+//    resident grid; every wait is bounded and every index is checked.
+#pragma once
+
+#include "pkv_device.cuh"
+
+namespace pkv {
+
+struct DecodeParams {
+    const void* q;                 // [q_rows, Hq, 128]
+    void* out;                     // [out_rows, Hq, 128] or null (state mode)
+    float* state_out;              // [B, Hq, 130] combined states, or null
+    const int32_t* block_table;    // [B, max_pages]
+    const int32_t* seq_lens;       // [B] or null (every row has `context`)
+    const int32_t* q_indices;      // [B] or null
+    const int32_t* out_indices;    // [B] or null
+    const int32_t* work_items;     // [T, 5] or null (rectangular grid)
+    const int32_t* split_offsets;  // [B + 1] (work queue)
+    int32_t* merge_counters;       // [B, Hkv] for the fused merge, or null
+    float* part_m;                 // [slots * Hq]
+    float* part_l;                 // [slots * Hq]
+    float* part_acc;               // [slots * Hq * 128]
+    unsigned* error;               // device error word
+    int B, q_rows, out_rows, Hq, Hkv;
+    int num_pages, page_size, max_pages;
+    int context, num_splits, num_items, total_slots;
+    float scale_log2;  // softmax scale * log2(e)
+};
+
+struct MergeParams {
+    const float* part_m;
+    const float* part_l;
+    const float* part_acc;
+    const int32_t* split_offsets;  // [B + 1] or null (rectangular)
+    const int32_t* out_indices;    // [B] or null
+    void* out;
+    float* state_out;
+    unsigned* error;
+    int B, Hq, Hkv, out_rows, num_splits, total_slots;
+};
+
+struct Item {
+    int row, kvh, split;
+    int tok_begin, tok_end;  // token range [tok_begin, tok_end)
+    int slot;                // partial-state slot, -1 if none/invalid
+    int row_splits;          // partial slots of this row
+    int q_row, out_row;      // -1 if invalid
+};
+
+__device__ __forceinline__ int ceil_div_i(int a, int b) { return (a + b - 1) / b; }
+
+// Decodes work item `index` (explicit work-queue entry or rectangular
+// (row, kvh, split) triple) and validates every index it implies.  Invalid
+// items become empty and, when `report` is set, raise a device error bit.
+__device__ __forceinline__ Item load_item(const DecodeParams& p, int index, bool report) {
+    Item it;
+    it.slot = -1;
+    it.row_splits = 1;
+    it.q_row = -1;
+    it.out_row = -1;
+    it.tok_begin = 0;
+    it.tok_end = 0;
+    long long tb, te;
+    if (p.work_items != nullptr) {
+        const int32_t* w = p.work_items + (size_t)index * 5;
+        it.row = __ldg(w + 0);
+        it.kvh = __ldg(w + 1);
+        it.split = __ldg(w + 2);
+        tb = __ldg(w + 3);
+        te = __ldg(w + 4);
+        if (it.row < 0 || it.row >= p.B || it.kvh < 0 || it.kvh >= p.Hkv || it.split < 0 ||
+            tb < 0 || te < tb) {
+            if (report) raise_error(p.error, kErrWorkItem);
+            it.row = 0;
+            it.kvh = 0;
+            it.split = 0;
+            return it;
+        }
+    } else {
+        const int per_row = p.Hkv * p.num_splits;
+        it.row = index / per_row;
+        const int r = index - it.row * per_row;
+        it.kvh = r / p.num_splits;
+        it.split = r - it.kvh * p.num_splits;
+    }
+    int seq = p.seq_lens != nullptr ? __ldg(p.seq_lens + it.row) : p.context;
+    const long long limit = (long long)p.max_pages * p.page_size;
+    if (seq < 0) seq = 0;
+    if ((long long)seq > limit) {
+        if (report) raise_error(p.error, kErrLogicalPage);
+        seq = (int)limit;
+    }
+    if (p.work_items == nullptr) {
+        const long long tiles = (seq + kTileTokens - 1) / kTileTokens;
+        tb = tiles * it.split / p.num_splits;
+        te = tiles * (it.split + 1) / p.num_splits;
+    }
+    long long t_begin = tb * kTileTokens;
+    long long t_end = te * kTileTokens;
+    if (t_end > seq) t_end = seq;
+    if (t_begin > t_end) {
+        // tile range starts past the row's last token (malformed work item)
+        if (report) raise_error(p.error, kErrWorkItem);
+        t_begin = t_end;
+    }
+    it.tok_begin = (int)t_begin;
+    it.tok_end = (int)t_end;
+
+    if (p.work_items != nullptr) {
+        const int s0 = __ldg(p.split_offsets + it.row);
+        const int s1 = __ldg(p.split_offsets + it.row + 1);
+        it.row_splits = s1 - s0;
+        const int slot = s0 + it.split;
+        if (s0 < 0 || s1 > p.total_slots || it.split >= it.row_splits || slot >= s1) {
+            if (report) raise_error(p.error, kErrSlot);
+            it.slot = -1;
+            it.row_splits = 2;  // never the direct-write path for a broken row
+        } else {
+            it.slot = slot;
+        }
+    } else {
+        it.row_splits = p.num_splits;
+        it.slot = it.row * p.num_splits + it.split;
+    }
+    const int qr = p.q_indices != nullptr ? __ldg(p.q_indices + it.row) : it.row;
+    if (qr >= 0 && qr < p.q_rows) {
+        it.q_row = qr;
+    } else if (report) {
+        raise_error(p.error, kErrIndex);
+    }
+    const int orow = p.out_indices != nullptr ? __ldg(p.out_indices + it.row) : it.row;
+    if (orow >= 0 && orow < p.out_rows) {
+        it.out_row = orow;
+    } else if (report && p.out != nullptr) {
+        raise_error(p.error, kErrIndex);
+    }
+    return it;
+}
+
+template <int G>
+struct DecodeSmem {
+    static constexpr int kMergeStride = kHeadDim + 4;  // padded: conflict-free combine
+    static constexpr int kMergeFloats = kConsumerWarps * G * kMergeStride;
+};
+
+template <int G, int NSLOTS>
+constexpr size_t decode_smem_bytes() {
+    return 1024 /* alignment slack */ + (size_t)NSLOTS * kSlotBytes +
+           2 * NSLOTS * sizeof(uint64_t) + 64 +
+           2 * 2 * kConsumerWarps * 8 * sizeof(float) +
+           2 * DecodeSmem<G>::kMergeFloats * sizeof(float);
+}
+
+template <int G, typename T, int BOX_ROWS, int NSLOTS>
+__global__ void __launch_bounds__(kThreads, 2)
+    pkv_decode_kernel(const __grid_constant__ DecodeParams p,
+                      const __grid_constant__ CUtensorMap tmap_k,
+                      const __grid_constant__ CUtensorMap tmap_v) {
+    static_assert(G == 1 || G == 2 || G == 4 || G == 8, "G must be 1, 2, 4 or 8");
+    static_assert(BOX_ROWS == 8 || BOX_ROWS == 16, "box rows must be 8 or 16");
+    constexpr int kBoxesPerStage = kStageTokens / BOX_ROWS;
+    constexpr int kStagesPerBatch = 32 / kBoxesPerStage;
+    constexpr int kBoxBytes = BOX_ROWS * kHalfRowBytes;
+    using Ops = ElemOps<T>;
+
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_u32 = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
+    uint8_t* ring = smem;
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(ring + (size_t)NSLOTS * kSlotBytes);
+    uint64_t* empty_bar = full_bar + NSLOTS;
+    volatile int* s_flags = reinterpret_cast<volatile int*>(empty_bar + NSLOTS);  // [0]=abort [1]=last
+    float* s_mstat = reinterpret_cast<float*>(smem + (size_t)NSLOTS * kSlotBytes +
+                                              2 * NSLOTS * sizeof(uint64_t) + 64);
+    float* s_lstat = s_mstat + 2 * kConsumerWarps * 8;
+    float* s_merge = s_lstat + 2 * kConsumerWarps * 8;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NSLOTS; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        s_flags[0] = 0;
+        s_flags[1] = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ============================ producer warp ============================
+        if (lane == 0) {
+            tma_prefetch_map(&tmap_k);
+            tma_prefetch_map(&tmap_v);
+        }
+        const uint64_t policy = l2_evict_first_policy();
+        uint32_t gstage = 0;
+        bool aborted = false;
+        for (int index = blockIdx.x; index < p.num_items && !aborted; index += gridDim.x) {
+            if (index + (int)gridDim.x >= p.num_items) griddep_launch_dependents();
+            const Item it = load_item(p, index, false);
+            const int n_stages = ceil_div_i(it.tok_end - it.tok_begin, kStageTokens);
+            const int n_boxes = n_stages * kBoxesPerStage;
+            const int32_t* bt_row = p.block_table + (size_t)it.row * p.max_pages;
+            auto fetch_page = [&](int box) -> int {
+                const int tok = it.tok_begin + box * BOX_ROWS;
+                if (box >= n_boxes || tok >= it.tok_end) return -1;
+                return __ldg(bt_row + tok / p.page_size);
+            };
+            int pid_next = fetch_page(lane);
+            for (int base = 0; base < n_boxes && !aborted; base += 32) {
+                const int box = base + lane;
+                const int tok = it.tok_begin + box * BOX_ROWS;
+                const int pid = pid_next;
+                if (base + 32 < n_boxes) pid_next = fetch_page(base + 32 + lane);
+                bool ok = box < n_boxes && tok < it.tok_end;
+                int y = 0;
+                if (ok) {
+                    if (pid < 0 || pid >= p.num_pages) {
+                        ok = false;
+                        raise_error(p.error, kErrPageId);
+                    } else {
+                        y = (pid * p.Hkv + it.kvh) * p.page_size + (tok % p.page_size);
+                    }
+                }
+                const int stages_here = min(kStagesPerBatch, n_stages - base / kBoxesPerStage);
+                for (int st = 0; st < stages_here; ++st) {
+                    const uint32_t slot = gstage % NSLOTS;
+                    if (gstage >= (uint32_t)NSLOTS) {
+                        bool waited = true;
+                        if (lane == 0) {
+                            waited = mbar_wait_bounded(&empty_bar[slot],
+                                                       ((gstage / NSLOTS) - 1u) & 1u, s_flags);
+                        }
+                        waited = __shfl_sync(0xffffffffu, waited, 0) && s_flags[0] == 0;
+                        if (!waited) {
+                            if (lane == 0) {
+                                s_flags[0] = 1;
+                                raise_error(p.error, kErrTimeout);
+                            }
+                            aborted = true;
+                            break;
+                        }
+                    }
+                    const bool mine = ok && (lane / kBoxesPerStage) == st;
+                    const unsigned mask = __ballot_sync(0xffffffffu, mine);
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(&full_bar[slot],
+                                              (uint32_t)__popc(mask) * 4u * kBoxBytes);
+                    }
+                    __syncwarp();
+                    if (mine) {
+                        uint8_t* dst = ring + (size_t)slot * kSlotBytes +
+                                       (lane % kBoxesPerStage) * kBoxBytes;
+                        const int half = kStageTokens * kHalfRowBytes;
+                        tma_load_2d(dst, &tmap_k, 0, y, &full_bar[slot], policy);
+                        tma_load_2d(dst + half, &tmap_k, 64, y, &full_bar[slot], policy);
+                        tma_load_2d(dst + 2 * half, &tmap_v, 0, y, &full_bar[slot], policy);
+                        tma_load_2d(dst + 3 * half, &tmap_v, 64, y, &full_bar[slot], policy);
+                    }
+                    ++gstage;
+                }
+            }
+        }
+        // Drain: the last NSLOTS issued stages may still be landing.
+        if (lane == 0) {
+            const uint32_t first = gstage > (uint32_t)NSLOTS ? gstage - NSLOTS : 0u;
+            for (uint32_t g = first; g < gstage; ++g) {
+                if (!mbar_wait_bounded(&full_bar[g % NSLOTS], (g / NSLOTS) & 1u, nullptr)) {
+                    raise_error(p.error, kErrTimeout);
+                    break;
+                }
+            }
+        }
+        return;
+    }
+
+    // ============================== consumer warps ==============================
+    const int tq = lane >> 2;         // token row of C fragments / GQA head of B fragments
+    const int tc = (lane & 3) * 2;    // column pair of C fragments
+    // ldmatrix row/chunk patterns (see the fragment layouts of mma.m16n8k16)
+    const int k_row = (lane & 7) + ((lane >> 3) & 1) * 8;
+    const int k_chunk_hi = lane >> 4;
+    const int v_row = (lane & 7) + ((lane >> 4) & 1) * 8;
+    const int v_chunk_hi = (lane >> 3) & 1;
+    const uint32_t ring_u32 = smem_u32(ring);
+    uint32_t gbase = 0;
+    int buf = 0;
+    bool aborted = false;
+
+    for (int index = blockIdx.x; index < p.num_items; index += gridDim.x) {
+        if (index + (int)gridDim.x >= p.num_items) griddep_launch_dependents();
+        const Item it = load_item(p, index, threadIdx.x == 0);
+        const int n_stages = ceil_div_i(it.tok_end - it.tok_begin, kStageTokens);
+
+        // Q^T as the B operand: lane holds Q[head tq][16 ks + tc (+8) .. +1].
+        uint32_t qf[8][2];
+        if (tq < G && it.q_row >= 0) {
+            const T* qrow = reinterpret_cast<const T*>(p.q) +
+                            ((size_t)it.q_row * p.Hq + (size_t)it.kvh * G + tq) * kHeadDim;
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+                qf[ks][0] = __ldg(reinterpret_cast<const unsigned int*>(qrow + 16 * ks + tc));
+                qf[ks][1] = __ldg(reinterpret_cast<const unsigned int*>(qrow + 16 * ks + 8 + tc));
+            }
+        } else {
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) qf[ks][0] = qf[ks][1] = 0u;
+        }
+
+        float m_run[2] = {-INFINITY, -INFINITY};
+        float l_run[2] = {0.f, 0.f};
+        float acc[8][4];
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+
+        for (int j = warp; j < n_stages; j += kConsumerWarps) {
+            const uint32_t gs = gbase + (uint32_t)j;
+            const uint32_t slot = gs % NSLOTS;
+            if (!aborted) {
+                bool ok = mbar_wait_bounded(&full_bar[slot], (gs / NSLOTS) & 1u, s_flags);
+                ok = __all_sync(0xffffffffu, ok) && s_flags[0] == 0;
+                if (!ok) {
+                    if (lane == 0) {
+                        s_flags[0] = 1;
+                        raise_error(p.error, kErrTimeout);
+                    }
+                    aborted = true;
+                }
+            }
+            if (aborted) break;
+
+            const int t0 = it.tok_begin + j * kStageTokens;
+            const int valid = min(kStageTokens, it.tok_end - t0);
+            uint8_t* sbase = ring + (size_t)slot * kSlotBytes;
+            const uint32_t sbase_u32 = ring_u32 + slot * kSlotBytes;
+            if (valid < kStageTokens) {
+                // Rows past the row's last token may hold anything (stale
+                // slot contents, unwritten pool memory): zero V there so that
+                // p = 0 never meets a non-finite value in the P.V product.
+                const int chunks = (kStageTokens - valid) * 16;
+                for (int c = lane; c < chunks; c += 32) {
+                    const int row = valid + (c >> 4);
+                    const int hv = (c >> 3) & 1;
+                    const int ch = c & 7;
+                    *reinterpret_cast<uint4*>(sbase + 2 * kStageTokens * kHalfRowBytes +
+                                              hv * kStageTokens * kHalfRowBytes +
+                                              row * kHalfRowBytes + ch * 16) =
+                        make_uint4(0u, 0u, 0u, 0u);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+            }
+
+            // ---- S^T[16 tok x 8 heads] = K[16 x 128] . Q^T
+            float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+                const int chunk = (ks & 3) * 2 + k_chunk_hi;
+                const uint32_t addr = sbase_u32 + (ks >> 2) * (kStageTokens * kHalfRowBytes) +
+                                      k_row * kHalfRowBytes + ((chunk ^ (k_row & 7)) << 4);
+                uint32_t a[4];
+                ldsm_x4(addr, a);
+                Ops::mma(s, a, qf[ks][0], qf[ks][1]);
+            }
+
+            // ---- online softmax (log2 domain), heads tc and tc + 1
+            float sc[4];
+            sc[0] = tq < valid ? s[0] * p.scale_log2 : -INFINITY;
+            sc[1] = tq < valid ? s[1] * p.scale_log2 : -INFINITY;
+            sc[2] = tq + 8 < valid ? s[2] * p.scale_log2 : -INFINITY;
+            sc[3] = tq + 8 < valid ? s[3] * p.scale_log2 : -INFINITY;
+            float corr[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float mx = fmaxf(sc[h], sc[2 + h]);
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                const float m_new = fmaxf(m_run[h], mx);
+                corr[h] = fast_exp2(m_run[h] - m_new);
+                m_run[h] = m_new;
+            }
+            float pr[4];
+            pr[0] = fast_exp2(sc[0] - m_run[0]);
+            pr[1] = fast_exp2(sc[1] - m_run[1]);
+            pr[2] = fast_exp2(sc[2] - m_run[0]);
+            pr[3] = fast_exp2(sc[3] - m_run[1]);
+            l_run[0] = l_run[0] * corr[0] + pr[0] + pr[2];
+            l_run[1] = l_run[1] * corr[1] + pr[1] + pr[3];
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+                acc[mt][0] *= corr[0];
+                acc[mt][1] *= corr[1];
+                acc[mt][2] *= corr[0];
+                acc[mt][3] *= corr[1];
+            }
+            // P^T as the B operand of the P.V product (k = token, n = head).
+            // bf16 keeps only 8 significant bits, so P is carried as hi + lo
+            // bf16 parts (two products) to keep fp16-level accuracy.
+            const uint32_t pb0 = movmatrix_trans(Ops::pack(pr[0], pr[1]));
+            const uint32_t pb1 = movmatrix_trans(Ops::pack(pr[2], pr[3]));
+            uint32_t pl0 = 0u, pl1 = 0u;
+            if constexpr (Ops::kSplitP) {
+                pl0 = movmatrix_trans(Ops::pack_residual(pr[0], pr[1]));
+                pl1 = movmatrix_trans(Ops::pack_residual(pr[2], pr[3]));
+            }
+
+            // ---- O^T[128 d x 8 heads] += V^T[128 x 16] . P^T[16 x 8]
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+                const int chunk = (mt & 3) * 2 + v_chunk_hi;
+                const uint32_t addr = sbase_u32 + 2 * kStageTokens * kHalfRowBytes +
+                                      (mt >> 2) * (kStageTokens * kHalfRowBytes) +
+                                      v_row * kHalfRowBytes + ((chunk ^ (v_row & 7)) << 4);
+                uint32_t a[4];
+                ldsm_x4_trans(addr, a);
+                Ops::mma(acc[mt], a, pb0, pb1);
+                if constexpr (Ops::kSplitP) Ops::mma(acc[mt], a, pl0, pl1);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty_bar[slot]);
+        }
+        gbase += (uint32_t)n_stages;
+
+        // ---- combine the four warps' states of this item
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 4);
+            l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 8);
+            l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 16);
+        }
+        float* mbuf = s_merge + buf * DecodeSmem<G>::kMergeFloats;
+        float* mstat = s_mstat + buf * kConsumerWarps * 8;
+        float* lstat = s_lstat + buf * kConsumerWarps * 8;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const int g = tc + (r & 1);
+                const int d = 16 * mt + tq + 8 * (r >> 1);
+                if (g < G) mbuf[(warp * G + g) * DecodeSmem<G>::kMergeStride + d] = acc[mt][r];
+            }
+        }
+        if (lane < 4) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int g = 2 * lane + h;
+                if (g < G) {
+                    mstat[warp * 8 + g] = m_run[h];
+                    lstat[warp * 8 + g] = l_run[h];
+                }
+            }
+        }
+        consumer_bar_sync();
+
+        const int d = threadIdx.x;  // 0..127
+        const bool rect = p.work_items == nullptr;
+        const bool direct = it.row_splits == 1;
+        float outv[G];
+        float mfin[G];
+        float lfin[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float mx = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) mx = fmaxf(mx, mstat[w * 8 + g]);
+            float lsum = 0.f, osum = 0.f;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) {
+                const float mw = mstat[w * 8 + g];
+                const float wt = mw == -INFINITY ? 0.f : fast_exp2(mw - mx);
+                lsum = fmaf(wt, lstat[w * 8 + g], lsum);
+                osum = fmaf(wt, mbuf[(w * G + g) * DecodeSmem<G>::kMergeStride + d], osum);
+            }
+            outv[g] = osum;
+            lfin[g] = lsum;
+            mfin[g] = mx == -INFINITY ? kNegFltMax : mx * kLn2;
+        }
+
+        if (direct) {
+            if (p.state_out != nullptr) {
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float* st = p.state_out + ((size_t)it.row * p.Hq + it.kvh * G + g) * kStateStride;
+                    st[2 + d] = outv[g];
+                    if (d == 0) {
+                        st[0] = mfin[g];
+                        st[1] = lfin[g];
+                    }
+                }
+            } else if (it.out_row >= 0 && (!rect || it.tok_end > it.tok_begin)) {
+                T* orow = reinterpret_cast<T*>(p.out) +
+                          ((size_t)it.out_row * p.Hq + (size_t)it.kvh * G) * kHeadDim;
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float inv = lfin[g] > 0.f ? 1.f / lfin[g] : 0.f;
+                    orow[g * kHeadDim + d] = Ops::from_float(outv[g] * inv);
+                }
+            }
+        } else if (it.slot >= 0) {
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const size_t si = (size_t)it.slot * p.Hq + (size_t)it.kvh * G + g;
+                p.part_acc[si * kHeadDim + d] = outv[g];
+                if (d == 0) {
+                    p.part_m[si] = mfin[g];
+                    p.part_l[si] = lfin[g];
+                }
+            }
+            if (p.merge_counters != nullptr && !rect) {
+                // fused merge: the last task of this (row, kvh) merges all of
+                // the row's slots (reference cuh:648-716).
+                __threadfence();
+                consumer_bar_sync();
+                if (threadIdx.x == 0) {
+                    int32_t* ctr = p.merge_counters + (size_t)it.row * p.Hkv + it.kvh;
+                    const int old = atomicAdd(ctr, 1);
+                    const int last = old == it.row_splits - 1;
+                    if (last) *ctr = 0;
+                    s_flags[1] = last;
+                }
+                consumer_bar_sync();
+                if (s_flags[1]) {
+                    __threadfence();
+                    const int s0 = it.slot - it.split;
+                    const int s1 = s0 + it.row_splits;
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        const size_t qh = (size_t)it.kvh * G + g;
+                        float mx = kNegFltMax;
+                        for (int s = s0; s < s1; ++s)
+                            mx = fmaxf(mx, __ldcg(p.part_m + (size_t)s * p.Hq + qh));
+                        float lsum = 0.f, osum = 0.f;
+                        for (int s = s0; s < s1; ++s) {
+                            const size_t si = (size_t)s * p.Hq + qh;
+                            const float wt = fast_exp2((__ldcg(p.part_m + si) - mx) * kLog2e);
+                            lsum = fmaf(wt, __ldcg(p.part_l + si), lsum);
+                            osum = fmaf(wt, __ldcg(p.part_acc + si * kHeadDim + d), osum);
+                        }
+                        if (p.state_out != nullptr) {
+                            float* st = p.state_out + ((size_t)it.row * p.Hq + qh) * kStateStride;
+                            st[2 + d] = osum;
+                            if (d == 0) {
+                                st[0] = mx;
+                                st[1] = lsum;
+                            }
+                        } else if (it.out_row >= 0) {
+                            T* o = reinterpret_cast<T*>(p.out) +
+                                   ((size_t)it.out_row * p.Hq + qh) * kHeadDim;
+                            o[d] = Ops::from_float(lsum > 0.f ? osum / lsum : 0.f);
+                        }
+                    }
+                }
+            }
+        }
+        buf ^= 1;
+    }
+}
+
+// Segmented log-sum-exp merge of the partial states of each (row, kvh):
+// reference persistentkv_merge_splits_kernel / _workqueue_kernel
+// (kernels/persistentkv_attention.cuh:719-784).  Rows whose single split was
+// already written by the decode kernel are skipped.  grid = (Hkv, B),
+// block = 128 (one thread per head_dim element).
+template <int G, typename T>
+__global__ void __launch_bounds__(kHeadDim)
+    pkv_merge_kernel(const __grid_constant__ MergeParams p) {
+    griddep_wait();
+    const int kvh = blockIdx.x;
+    const int row = blockIdx.y;
+    const int d = threadIdx.x;
+    int s0, s1;
+    if (p.split_offsets != nullptr) {
+        s0 = __ldg(p.split_offsets + row);
+        s1 = __ldg(p.split_offsets + row + 1);
+    } else {
+        s0 = row * p.num_splits;
+        s1 = s0 + p.num_splits;
+    }
+    if (s1 - s0 == 1) return;  // written directly by the decode kernel
+    if (s0 < 0 || s1 < s0 || s1 > p.total_slots) {
+        if (d == 0 && kvh == 0) raise_error(p.error, kErrSlot);
+        return;
+    }
+    int orow = row;
+    if (p.state_out == nullptr) {
+        orow = p.out_indices != nullptr ? __ldg(p.out_indices + row) : row;
+        if (orow < 0 || orow >= p.out_rows) {
+            if (d == 0 && kvh == 0) raise_error(p.error, kErrIndex);
+            return;
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const size_t qh = (size_t)kvh * G + g;
+        float mx = kNegFltMax;
+        for (int s = s0; s < s1; ++s) mx = fmaxf(mx, __ldg(p.part_m + (size_t)s * p.Hq + qh));
+        float lsum = 0.f, osum = 0.f;
+        for (int s = s0; s < s1; ++s) {
+            const size_t si = (size_t)s * p.Hq + qh;
+            const float wt = fast_exp2((__ldg(p.part_m + si) - mx) * kLog2e);
+            lsum = fmaf(wt, __ldg(p.part_l + si), lsum);
+            osum = fmaf(wt, __ldg(p.part_acc + si * kHeadDim + d), osum);
+        }
+        if (p.state_out != nullptr) {
+            float* st = p.state_out + ((size_t)row * p.Hq + qh) * kStateStride;
+            st[2 + d] = osum;
+            if (d == 0) {
+                st[0] = mx;
+                st[1] = lsum;
+            }
+        } else {
+            T* o = reinterpret_cast<T*>(p.out) + ((size_t)orow * p.Hq + qh) * kHeadDim;
+            o[d] = ElemOps<T>::from_float(lsum > 0.f ? osum / lsum : 0.f);
+        }
+    }
+}
+
+// Merges n_parts blocks of combined states [n_parts][B][Hq][130] into the
+// normalised output.  grid = (Hq, B), block = 128.
+template <typename T>
+__global__ void __launch_bounds__(kHeadDim)
+    pkv_combine_states_kernel(const float* __restrict__ states, int n_parts,
+                              const int32_t* __restrict__ out_indices, void* out, int B,
+                              int out_rows, int Hq, unsigned* error) {
+    const int qh = blockIdx.x;
+    const int row = blockIdx.y;
+    const int d = threadIdx.x;
+    const int orow = out_indices != nullptr ? __ldg(out_indices + row) : row;
+    if (orow < 0 || orow >= out_rows) {
+        if (d == 0) raise_error(error, kErrIndex);
+        return;
+    }
+    const size_t part_stride = (size_t)B * Hq * kStateStride;
+    const float* base = states + ((size_t)row * Hq + qh) * kStateStride;
+    float mx = kNegFltMax;
+    for (int r = 0; r < n_parts; ++r) mx = fmaxf(mx, __ldg(base + r * part_stride));
+    float lsum = 0.f, osum = 0.f;
+    for (int r = 0; r < n_parts; ++r) {
+        const float* st = base + r * part_stride;
+        const float wt = fast_exp2((__ldg(st) - mx) * kLog2e);
+        lsum = fmaf(wt, __ldg(st + 1), lsum);
+        osum = fmaf(wt, __ldg(st + 2 + d), osum);
+    }
+    T* o = reinterpret_cast<T*>(out) + ((size_t)orow * Hq + qh) * kHeadDim;
+    o[d] = ElemOps<T>::from_float(lsum > 0.f ? osum / lsum : 0.f);
+}
+
+}  // namespace pkv

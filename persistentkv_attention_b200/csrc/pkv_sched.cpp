@@ -1,0 +1,321 @@
+// pkv_sched.cpp -- host-side scheduler of the decode engine: split-count
+// router, route cost model and compact work-queue builder (C ABI in
+// include/pkv_b200.h).
+//
+// The reference keeps these in Python inside its serving harness
+// (tests/benchmark_serving_trace.py:328-488 and :655-729).  They are restated
+// here in C++ with the reference's constants as a parameter set, so the same
+// integer decisions are reproduced exactly, and extended with a policy that
+// balances tasks over the 148 SMs of a B200.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <numeric>
+#include <set>
+#include <vector>
+
+#include "../../include/pkv_b200.h"
+
+namespace {
+
+inline int round_up4(int v) { return ((v + 3) / 4) * 4; }
+inline int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
+inline int tiles_of(int length) { return (length + PKV_TILE_TOKENS - 1) / PKV_TILE_TOKENS; }
+
+double useful_kv_mb(const pkv_router_params* p, const int32_t* lengths, int n) {
+    // reference useful_kv_mb_for_state (benchmark_serving_trace.py:511-513)
+    long long tokens = 0;
+    for (int i = 0; i < n; ++i) tokens += lengths[i];
+    const double bytes = (double)tokens * p->hkv * p->head_dim * 2.0 * p->elem_bytes;
+    return bytes / (1024.0 * 1024.0);
+}
+
+int balanced_quota(const pkv_router_params* p, const int32_t* seq_lens, int B) {
+    // Smallest tile quota q such that sum_r ceil(tiles_r / q) tasks per KV
+    // head fit in the resident CTA slots (times tasks_per_cta).
+    long long total = 0;
+    for (int r = 0; r < B; ++r) total += tiles_of(std::max(0, (int)seq_lens[r]));
+    const int kvh = std::max(1, p->hkv);
+    const long long slots = (long long)std::max(1, p->sm_count) * std::max(1, p->ctas_per_sm) *
+                            std::max(1, p->tasks_per_cta);
+    const int target = (int)std::max(1ll, slots / kvh);
+    int q = std::max(std::max(1, p->min_tiles_per_task), ceil_div(std::max(1ll, total), target));
+    while (true) {
+        long long tasks = 0;
+        for (int r = 0; r < B; ++r) {
+            const int t = tiles_of(std::max(0, (int)seq_lens[r]));
+            tasks += std::max(1, ceil_div(t, q));
+        }
+        if (tasks <= target || q >= (1 << 24)) break;
+        ++q;
+    }
+    return q;
+}
+
+}  // namespace
+
+extern "C" {
+
+void pkv_router_params_reference(pkv_router_params* p) {
+    std::memset(p, 0, sizeof(*p));
+    p->hq = 32;                 // HQ   benchmark_serving_trace.py:33
+    p->hkv = 8;                 // HKV  :34
+    p->head_dim = 128;          // DIM  :35
+    p->elem_bytes = 2;
+    p->sm_count = 28;           // SM_COUNT :39
+    p->read_gbps = 302.0;       // ROOFLINE_READ_GBPS :40
+    p->launch_us = 8.0;         // LAUNCH_OVERHEAD_US :41
+    p->min_ctas_per_sm = 4.0;   // MIN_CTAS_PER_SM :42
+    p->supported_g = 4;         // SUPPORTED_PERSISTENTKV_GQA :43
+    p->min_split_len = 16384;   // :457
+    p->ctas_per_sm = 2;
+    p->tasks_per_cta = 1;
+    p->max_splits = 48;
+    p->min_tiles_per_task = 1;
+}
+
+void pkv_router_params_b200(pkv_router_params* p) {
+    std::memset(p, 0, sizeof(*p));
+    p->hq = 32;
+    p->hkv = 8;
+    p->head_dim = 128;
+    p->elem_bytes = 2;
+    p->sm_count = 148;          // B200: 2 dies x 74 SMs
+    p->read_gbps = 6556.5;      // measured STREAM-style copy on this pool's B200s
+    p->launch_us = 2.5;         // graph-replayed launch + PDL-overlapped merge
+    p->min_ctas_per_sm = 2.0;   // 2 resident 160-thread decode CTAs per SM
+    p->supported_g = 0;         // every G in {1,2,4,8} runs the split routes
+    p->min_split_len = 0;
+    p->ctas_per_sm = 2;
+    p->tasks_per_cta = 1;
+    p->max_splits = 256;
+    p->min_tiles_per_task = 2;
+}
+
+int pkv_choose_workqueue_row_splits(const pkv_router_params* p, int length, int active_count,
+                                    int requested_splits, int auto_splits) {
+    // reference choose_workqueue_row_splits (benchmark_serving_trace.py:370-393)
+    if (!auto_splits) return requested_splits;
+    const int tiles = std::max(1, tiles_of(length));
+    const int occupancy_floor = round_up4(ceil_div(256, (long long)p->hkv * std::max(1, active_count)));
+    const int length_target = round_up4(ceil_div(tiles, 64));
+    int splits = std::max(occupancy_floor, length_target);
+    if (active_count >= 8) {
+        splits = std::min(splits, 24);
+    } else if (active_count >= 4) {
+        splits = std::min(splits, 32);
+    } else if (active_count == 2) {
+        splits = std::min(splits, 40);
+    } else {
+        splits = std::min(splits, 48);
+    }
+    return std::max(4, std::min(std::min(splits, 48), tiles));
+}
+
+int pkv_choose_splits(const pkv_router_params* p, const int32_t* lengths, int n,
+                      int requested_splits, int auto_splits, int single_bucket) {
+    // reference choose_splits (benchmark_serving_trace.py:328-367)
+    if (!auto_splits) return requested_splits;
+    if (n <= 0) return requested_splits;
+    const int batch = n;
+    int t_max = 0, t_min = 1 << 30;
+    for (int i = 0; i < n; ++i) {
+        const int t = tiles_of(lengths[i]);
+        t_max = std::max(t_max, t);
+        t_min = std::min(t_min, t);
+    }
+    if (single_bucket) {
+        if (batch >= 8) return std::max(4, std::min(40, t_min));
+        if (batch == 4) return std::max(4, std::min(16, t_min));
+        if (batch == 2) return std::max(4, std::min(24, t_min));
+        if (t_max >= 1024) return std::max(4, std::min(36, t_min));
+        return std::max(4, std::min(24, t_min));
+    }
+    if (batch >= 8) return std::max(4, std::min(24, t_min));
+    if (batch == 4) return std::max(4, std::min(28, t_min));
+    if (batch == 2 && t_max >= 1024) return std::max(4, std::min(32, t_min));
+    const int occupancy = ceil_div(320, (long long)p->hkv * batch);
+    const int length_based = ceil_div(t_max, 32);
+    int splits = round_up4(std::max(occupancy, length_based));
+    if (t_max <= 384) splits = std::min(splits, 24);
+    if (batch >= 8) splits = std::min(splits, 40);
+    if (batch <= 2 && t_max >= 1024) splits = std::max(splits, 32);
+    return std::max(4, std::min(std::min(splits, 48), t_min));
+}
+
+int pkv_model_bucket_splits(const pkv_router_params* p, const int32_t* lengths, int n) {
+    // reference model_bucket_splits (benchmark_serving_trace.py:396-402)
+    int t_max = 0, t_min = 1 << 30;
+    for (int i = 0; i < n; ++i) {
+        const int t = tiles_of(lengths[i]);
+        t_max = std::max(t_max, t);
+        t_min = std::min(t_min, t);
+    }
+    if (n <= 0) t_min = 0;
+    const int occupancy = ceil_div(256, (long long)p->hkv * std::max(1, n));
+    const int length_based = ceil_div(t_max, 96);
+    return std::max(4, std::min(std::min(round_up4(std::max(occupancy, length_based)), 48), t_min));
+}
+
+int pkv_model_workqueue_splits(const pkv_router_params* p, const int32_t* lengths, int n) {
+    // reference model_workqueue_splits (benchmark_serving_trace.py:405-415)
+    int best = 0;
+    for (int i = 0; i < n; ++i)
+        best = std::max(best, pkv_choose_workqueue_row_splits(p, lengths[i], n, 1, 1));
+    return best;
+}
+
+double pkv_estimate_route_ms(const pkv_router_params* p, const int32_t* lengths, int n,
+                             pkv_route route, int splits) {
+    // reference estimate_route_ms (benchmark_serving_trace.py:418-442)
+    const double kv_ms = useful_kv_mb(p, lengths, n) / p->read_gbps;
+    const int active = n;
+    std::set<int> uniq(lengths, lengths + n);
+    const int unique_lengths = (int)uniq.size();
+    double ctas_per_sm, merge_mb;
+    int launch_count;
+    const double state_mb =
+        (double)active * p->hq * splits * (2 + p->head_dim) * 4 / (1024.0 * 1024.0);
+    switch (route) {
+        case PKV_ROUTE_SINGLE_PASS:
+            ctas_per_sm = (double)active * p->hkv / p->sm_count;
+            launch_count = 1;
+            merge_mb = 0.0;
+            break;
+        case PKV_ROUTE_BUCKET:
+            ctas_per_sm = (double)active * p->hkv * splits / p->sm_count;
+            launch_count = 2 * unique_lengths;
+            merge_mb = state_mb;
+            break;
+        case PKV_ROUTE_WORKQUEUE:
+        default:
+            ctas_per_sm = (double)active * p->hkv * splits / p->sm_count;
+            launch_count = 2;
+            merge_mb = state_mb;
+            break;
+    }
+    const double occupancy_penalty =
+        std::max(1.0, p->min_ctas_per_sm / std::max(ctas_per_sm, 1e-6));
+    const double launch_ms = launch_count * p->launch_us / 1000.0;
+    const double merge_ms = merge_mb / p->read_gbps;
+    return kv_ms * occupancy_penalty + merge_ms + launch_ms;
+}
+
+pkv_route pkv_choose_route(const pkv_router_params* p, const int32_t* lengths, int n,
+                           int* splits_out, double* est_ms_out) {
+    // reference choose_adaptive_route_cost_model (benchmark_serving_trace.py:445-488);
+    // its "flashinfer" route is the single-pass route here.
+    pkv_route best = PKV_ROUTE_SINGLE_PASS;
+    int best_splits = 1;
+    double best_ms = pkv_estimate_route_ms(p, lengths, n, PKV_ROUTE_SINGLE_PASS, 1);
+    const int gqa = p->hkv > 0 ? p->hq / p->hkv : 0;
+    int max_len = 0;
+    for (int i = 0; i < n; ++i) max_len = std::max(max_len, (int)lengths[i]);
+    const bool gated = (p->supported_g != 0 && gqa != p->supported_g) || max_len < p->min_split_len;
+    if (!gated) {
+        if (n <= 1) {
+            const int s = pkv_model_bucket_splits(p, lengths, n);
+            const double ms = pkv_estimate_route_ms(p, lengths, n, PKV_ROUTE_BUCKET, s);
+            if (ms < best_ms) {
+                best = PKV_ROUTE_BUCKET;
+                best_splits = s;
+                best_ms = ms;
+            }
+        }
+        if (n >= 8) {
+            const int s = pkv_model_workqueue_splits(p, lengths, n);
+            const double ms = pkv_estimate_route_ms(p, lengths, n, PKV_ROUTE_WORKQUEUE, s);
+            if (ms < best_ms) {
+                best = PKV_ROUTE_WORKQUEUE;
+                best_splits = s;
+                best_ms = ms;
+            }
+        }
+    }
+    if (splits_out) *splits_out = best_splits;
+    if (est_ms_out) *est_ms_out = best_ms;
+    return best;
+}
+
+pkv_status pkv_build_workqueue(const pkv_router_params* p, const int32_t* seq_lens, int B,
+                               int active_count, pkv_split_policy policy, int requested_splits,
+                               int32_t* work_items, int max_items, int32_t* split_offsets,
+                               int* num_items_out, int* total_slots_out) {
+    if (p == nullptr || seq_lens == nullptr || split_offsets == nullptr || B < 0 ||
+        num_items_out == nullptr || total_slots_out == nullptr || p->hkv <= 0) {
+        return PKV_ERR_INVALID_ARGUMENT;
+    }
+    if (policy == PKV_SPLITS_FIXED && requested_splits <= 0) return PKV_ERR_INVALID_ARGUMENT;
+    const int hkv = p->hkv;
+    int quota = 0;
+    if (policy == PKV_SPLITS_BALANCED) quota = balanced_quota(p, seq_lens, B);
+
+    // pass 1: splits per row
+    std::vector<int> splits(B);
+    long long items = 0;
+    split_offsets[0] = 0;
+    for (int r = 0; r < B; ++r) {
+        const int len = std::max(0, (int)seq_lens[r]);
+        const int tiles = tiles_of(len);
+        int s;
+        if (tiles == 0) {
+            s = 1;  // one empty split: the row's output becomes zeros
+        } else {
+            switch (policy) {
+                case PKV_SPLITS_REFERENCE:
+                    s = pkv_choose_workqueue_row_splits(p, len, active_count, requested_splits,
+                                                        requested_splits <= 0);
+                    break;
+                case PKV_SPLITS_FIXED:
+                    s = requested_splits;
+                    break;
+                case PKV_SPLITS_BALANCED:
+                default:
+                    s = ceil_div(tiles, quota);
+                    if (p->max_splits > 0) s = std::min(s, p->max_splits);
+                    break;
+            }
+            s = std::max(1, std::min(s, tiles));  // never an empty (unwritten) slot
+        }
+        splits[r] = s;
+        split_offsets[r + 1] = split_offsets[r] + s;
+        items += (long long)s * hkv;
+    }
+    *total_slots_out = split_offsets[B];
+    *num_items_out = (int)items;
+    if (work_items == nullptr || items > max_items) return PKV_ERR_CAPACITY;
+
+    // pass 2: items {row, kvh, split, tile_begin, tile_end}; reference order
+    // (row, split, kvh) for the reference and fixed policies, largest task
+    // first for the balanced policy (blocks are dispatched in index order).
+    struct Task {
+        int row, kvh, split, tb, te;
+    };
+    std::vector<Task> tasks;
+    tasks.reserve((size_t)items);
+    for (int r = 0; r < B; ++r) {
+        const int tiles = tiles_of(std::max(0, (int)seq_lens[r]));
+        const int s = splits[r];
+        for (int k = 0; k < s; ++k) {
+            const int tb = (int)((long long)tiles * k / s);
+            const int te = (int)((long long)tiles * (k + 1) / s);
+            for (int h = 0; h < hkv; ++h) tasks.push_back({r, h, k, tb, te});
+        }
+    }
+    if (policy == PKV_SPLITS_BALANCED) {
+        std::stable_sort(tasks.begin(), tasks.end(), [](const Task& a, const Task& b) {
+            return (a.te - a.tb) > (b.te - b.tb);
+        });
+    }
+    for (size_t i = 0; i < tasks.size(); ++i) {
+        int32_t* w = work_items + 5 * i;
+        w[0] = tasks[i].row;
+        w[1] = tasks[i].kvh;
+        w[2] = tasks[i].split;
+        w[3] = tasks[i].tb;
+        w[4] = tasks[i].te;
+    }
+    return PKV_OK;
+}
+
+}  // extern "C"

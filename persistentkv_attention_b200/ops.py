@@ -1,0 +1,300 @@
+"""PyTorch-facing operator surface of the B200 decode engine.
+
+The four functions below keep the names, argument order, argument meaning and
+error behaviour (``RuntimeError`` with the same messages) of the reference's
+extension module, ``tests/persistentkv_torch_extension.cu:319-336``, so the
+reference's serving harness can load this module in place of its own:
+
+    paged_attention(q, k_pages, v_pages, block_table, output, workspace,
+                    context, page_size, num_splits)
+    paged_attention_masked(q, k_pages, v_pages, block_table, seq_lens, output,
+                           workspace, bucket_context, page_size, num_splits)
+    paged_attention_indexed(q_source, k_pages, v_pages, block_table, seq_lens,
+                            q_indices, out_indices, output, workspace,
+                            bucket_context, page_size, num_splits)
+    paged_attention_workqueue(q_source, k_pages, v_pages, block_table, seq_lens,
+                              work_items, split_offsets, merge_counters,
+                              q_indices, out_indices, output, workspace,
+                              bucket_context, page_size, total_partial_slots,
+                              fused_merge)
+
+Each call only validates tensors and forwards raw pointers to the C ABI of
+``libpkv_b200.so`` on the current CUDA stream; PyTorch supplies device memory
+and streams, never the computation.  Beyond the reference, q/K/V/output may be
+bfloat16 (all of them), and two calls serve sequence sharding across GPUs
+(``paged_attention_workqueue_state`` and ``combine_states``).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _native
+
+HEAD_DIM = 128
+STATE_STRIDE = HEAD_DIM + 2
+
+_DTYPES = {torch.float16: _native.PKV_DTYPE_F16, torch.bfloat16: _native.PKV_DTYPE_BF16}
+
+
+def _check_tensor(tensor: torch.Tensor, name: str, dtype, dims: int) -> None:
+    # reference check_tensor (tests/persistentkv_torch_extension.cu:9-19)
+    if not tensor.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+    if (tensor.dtype not in dtype) if isinstance(dtype, tuple) else tensor.dtype != dtype:
+        raise RuntimeError(f"{name} has wrong dtype")
+    if tensor.dim() != dims:
+        raise RuntimeError(f"{name} has wrong rank")
+    if not tensor.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+def _check_supported_gqa(hq: int, hkv: int) -> None:
+    # reference check_supported_gqa (tests/persistentkv_torch_extension.cu:21-31)
+    if hkv <= 0:
+        raise RuntimeError("Hkv must be positive")
+    if hq % hkv != 0:
+        raise RuntimeError("Hq must be divisible by Hkv")
+    g = hq // hkv
+    if g not in (1, 2, 4, 8):
+        raise RuntimeError(
+            f"PersistentKV supports G=Hq/Hkv in {{1,2,4,8}}; got G={g} from Hq={hq} Hkv={hkv}"
+        )
+
+
+def _check_kv(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tensor, page_size: int):
+    dt = q.dtype
+    _check_tensor(k_pages, "k_pages", dt, 4)
+    _check_tensor(v_pages, "v_pages", dt, 4)
+    d = q.size(2)
+    hkv = k_pages.size(1)
+    physical_pages = k_pages.size(0)
+    if d != HEAD_DIM:
+        raise RuntimeError("PersistentKV extension currently requires d=128")
+    if not (v_pages.size(0) == physical_pages and v_pages.size(1) == hkv
+            and v_pages.size(2) == page_size and v_pages.size(3) == d):
+        raise RuntimeError("v_pages shape mismatch")
+    if not (k_pages.size(2) == page_size and k_pages.size(3) == d):
+        raise RuntimeError("k_pages shape mismatch")
+    return hkv, physical_pages
+
+
+def _workspace(workspace: torch.Tensor):
+    if not workspace.is_cuda:
+        raise RuntimeError("workspace must be a CUDA tensor")
+    if not workspace.is_contiguous():
+        raise RuntimeError("workspace must be contiguous")
+    if workspace.numel() == 0:
+        return None, 0
+    return workspace.data_ptr(), workspace.numel() * workspace.element_size()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _positive(value: int, name: str) -> None:
+    if value <= 0:
+        raise RuntimeError(f"{name} must be positive")
+
+
+def paged_attention(q, k_pages, v_pages, block_table, output, workspace, context: int,
+                    page_size: int, num_splits: int) -> None:
+    """Reference ``persistentkv_paged_attention`` (extension :35-93)."""
+    _check_tensor(q, "q", tuple(_DTYPES), 3)
+    hkv, physical_pages = _check_kv(q, k_pages, v_pages, page_size)
+    _check_tensor(block_table, "block_table", torch.int32, 2)
+    _check_tensor(output, "output", q.dtype, 3)
+    ws_ptr, ws_bytes = _workspace(workspace)
+    b, hq, d = q.shape
+    if not (output.size(0) == b and output.size(1) == hq and output.size(2) == d):
+        raise RuntimeError("output shape must match q")
+    if block_table.size(0) != b:
+        raise RuntimeError("block_table batch mismatch")
+    _check_supported_gqa(hq, hkv)
+    _positive(context, "context")
+    _positive(page_size, "page_size")
+    _positive(num_splits, "num_splits")
+    lib = _native.load()
+    _native.check(lib.pkv_paged_attention(
+        q.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), block_table.data_ptr(),
+        output.data_ptr(), ws_ptr, ws_bytes, b, hq, hkv, d, physical_pages, page_size,
+        block_table.size(1), int(context), int(num_splits), _DTYPES[q.dtype], _stream()))
+
+
+def paged_attention_masked(q, k_pages, v_pages, block_table, seq_lens, output, workspace,
+                           bucket_context: int, page_size: int, num_splits: int) -> None:
+    """Reference ``persistentkv_paged_attention_masked`` (extension :95-157)."""
+    _check_tensor(q, "q", tuple(_DTYPES), 3)
+    hkv, physical_pages = _check_kv(q, k_pages, v_pages, page_size)
+    _check_tensor(block_table, "block_table", torch.int32, 2)
+    _check_tensor(seq_lens, "seq_lens", torch.int32, 1)
+    _check_tensor(output, "output", q.dtype, 3)
+    ws_ptr, ws_bytes = _workspace(workspace)
+    b, hq, d = q.shape
+    if not (output.size(0) == b and output.size(1) == hq and output.size(2) == d):
+        raise RuntimeError("output shape must match q")
+    if seq_lens.size(0) != b:
+        raise RuntimeError("seq_lens batch mismatch")
+    if block_table.size(0) != b:
+        raise RuntimeError("block_table batch mismatch")
+    _check_supported_gqa(hq, hkv)
+    _positive(bucket_context, "bucket_context")
+    _positive(page_size, "page_size")
+    _positive(num_splits, "num_splits")
+    lib = _native.load()
+    _native.check(lib.pkv_paged_attention_masked(
+        q.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), block_table.data_ptr(),
+        seq_lens.data_ptr(), output.data_ptr(), ws_ptr, ws_bytes, b, hq, hkv, d,
+        physical_pages, page_size, block_table.size(1), int(bucket_context), int(num_splits),
+        _DTYPES[q.dtype], _stream()))
+
+
+def paged_attention_indexed(q_source, k_pages, v_pages, block_table, seq_lens, q_indices,
+                            out_indices, output, workspace, bucket_context: int,
+                            page_size: int, num_splits: int) -> None:
+    """Reference ``persistentkv_paged_attention_indexed`` (extension :159-228)."""
+    _check_tensor(q_source, "q_source", tuple(_DTYPES), 3)
+    hkv, physical_pages = _check_kv(q_source, k_pages, v_pages, page_size)
+    _check_tensor(block_table, "block_table", torch.int32, 2)
+    _check_tensor(seq_lens, "seq_lens", torch.int32, 1)
+    _check_tensor(q_indices, "q_indices", torch.int32, 1)
+    _check_tensor(out_indices, "out_indices", torch.int32, 1)
+    _check_tensor(output, "output", q_source.dtype, 3)
+    ws_ptr, ws_bytes = _workspace(workspace)
+    b = block_table.size(0)
+    hq, d = q_source.size(1), q_source.size(2)
+    if not (output.size(1) == hq and output.size(2) == d):
+        raise RuntimeError("output shape must match q head dimensions")
+    if seq_lens.size(0) != b:
+        raise RuntimeError("seq_lens batch mismatch")
+    if q_indices.size(0) != b:
+        raise RuntimeError("q_indices batch mismatch")
+    if out_indices.size(0) != b:
+        raise RuntimeError("out_indices batch mismatch")
+    _check_supported_gqa(hq, hkv)
+    _positive(bucket_context, "bucket_context")
+    _positive(page_size, "page_size")
+    _positive(num_splits, "num_splits")
+    lib = _native.load()
+    _native.check(lib.pkv_paged_attention_indexed(
+        q_source.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), block_table.data_ptr(),
+        seq_lens.data_ptr(), q_indices.data_ptr(), out_indices.data_ptr(), output.data_ptr(),
+        ws_ptr, ws_bytes, b, q_source.size(0), output.size(0), hq, hkv, d, physical_pages,
+        page_size, block_table.size(1), int(bucket_context), int(num_splits),
+        _DTYPES[q_source.dtype], _stream()))
+
+
+def _check_workqueue(q_source, k_pages, v_pages, block_table, seq_lens, work_items,
+                     split_offsets, merge_counters, q_indices, page_size):
+    _check_tensor(q_source, "q_source", tuple(_DTYPES), 3)
+    hkv, physical_pages = _check_kv(q_source, k_pages, v_pages, page_size)
+    _check_tensor(block_table, "block_table", torch.int32, 2)
+    _check_tensor(seq_lens, "seq_lens", torch.int32, 1)
+    _check_tensor(work_items, "work_items", torch.int32, 2)
+    _check_tensor(split_offsets, "split_offsets", torch.int32, 1)
+    _check_tensor(merge_counters, "merge_counters", torch.int32, 2)
+    _check_tensor(q_indices, "q_indices", torch.int32, 1)
+    b = block_table.size(0)
+    if work_items.size(1) != 5:
+        raise RuntimeError("work_items must have shape [T, 5]")
+    if split_offsets.size(0) != b + 1:
+        raise RuntimeError("split_offsets batch mismatch")
+    if not (merge_counters.size(0) == b and merge_counters.size(1) == hkv):
+        raise RuntimeError("merge_counters shape mismatch")
+    if seq_lens.size(0) != b:
+        raise RuntimeError("seq_lens batch mismatch")
+    if q_indices.size(0) != b:
+        raise RuntimeError("q_indices batch mismatch")
+    return hkv, physical_pages, b
+
+
+def paged_attention_workqueue(q_source, k_pages, v_pages, block_table, seq_lens, work_items,
+                              split_offsets, merge_counters, q_indices, out_indices, output,
+                              workspace, bucket_context: int, page_size: int,
+                              total_partial_slots: int, fused_merge: bool) -> None:
+    """Reference ``persistentkv_paged_attention_workqueue`` (extension :230-317)."""
+    hkv, physical_pages, b = _check_workqueue(q_source, k_pages, v_pages, block_table, seq_lens,
+                                              work_items, split_offsets, merge_counters,
+                                              q_indices, page_size)
+    _check_tensor(out_indices, "out_indices", torch.int32, 1)
+    _check_tensor(output, "output", q_source.dtype, 3)
+    ws_ptr, ws_bytes = _workspace(workspace)
+    hq, d = q_source.size(1), q_source.size(2)
+    if not (output.size(1) == hq and output.size(2) == d):
+        raise RuntimeError("output shape must match q head dimensions")
+    if out_indices.size(0) != b:
+        raise RuntimeError("out_indices batch mismatch")
+    _check_supported_gqa(hq, hkv)
+    _positive(bucket_context, "bucket_context")
+    _positive(page_size, "page_size")
+    if work_items.size(0) <= 0:
+        raise RuntimeError("work_items must not be empty")
+    if total_partial_slots <= 0:
+        raise RuntimeError("total_partial_slots must be positive")
+    lib = _native.load()
+    _native.check(lib.pkv_paged_attention_workqueue(
+        q_source.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), block_table.data_ptr(),
+        seq_lens.data_ptr(), work_items.data_ptr(), split_offsets.data_ptr(),
+        merge_counters.data_ptr(), q_indices.data_ptr(), out_indices.data_ptr(),
+        output.data_ptr(), ws_ptr, ws_bytes, b, q_source.size(0), output.size(0), hq, hkv, d,
+        physical_pages, page_size, block_table.size(1), int(bucket_context),
+        work_items.size(0), int(total_partial_slots), 1 if fused_merge else 0,
+        _DTYPES[q_source.dtype], _stream()))
+
+
+def paged_attention_workqueue_state(q_source, k_pages, v_pages, block_table, seq_lens,
+                                    work_items, split_offsets, merge_counters, q_indices,
+                                    state_out, workspace, page_size: int,
+                                    total_partial_slots: int, fused_merge: bool) -> None:
+    """Work-queue decode that writes each row's combined (m, l, acc) state.
+
+    ``state_out`` is float32 ``[B, Hq, 130]``; no counterpart in the reference.
+    """
+    hkv, physical_pages, b = _check_workqueue(q_source, k_pages, v_pages, block_table, seq_lens,
+                                              work_items, split_offsets, merge_counters,
+                                              q_indices, page_size)
+    _check_tensor(state_out, "state_out", torch.float32, 3)
+    hq, d = q_source.size(1), q_source.size(2)
+    if tuple(state_out.shape) != (b, hq, STATE_STRIDE):
+        raise RuntimeError("state_out must have shape [B, Hq, 130]")
+    _check_supported_gqa(hq, hkv)
+    ws_ptr, ws_bytes = _workspace(workspace)
+    lib = _native.load()
+    _native.check(lib.pkv_paged_attention_workqueue_state(
+        q_source.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), block_table.data_ptr(),
+        seq_lens.data_ptr(), work_items.data_ptr(), split_offsets.data_ptr(),
+        merge_counters.data_ptr() if fused_merge else None, q_indices.data_ptr(),
+        state_out.data_ptr(), ws_ptr, ws_bytes, b, q_source.size(0), hq, hkv, d,
+        physical_pages, page_size, block_table.size(1), work_items.size(0),
+        int(total_partial_slots), _DTYPES[q_source.dtype], _stream()))
+
+
+def combine_states(states, output, out_indices=None) -> None:
+    """Merges ``states[n_parts, B, Hq, 130]`` into ``output`` rows (LSE combine)."""
+    _check_tensor(states, "states", torch.float32, 4)
+    _check_tensor(output, "output", tuple(_DTYPES), 3)
+    n_parts, b, hq, width = states.shape
+    if width != STATE_STRIDE:
+        raise RuntimeError("states must have 130 values per head")
+    if output.size(1) != hq or output.size(2) != HEAD_DIM:
+        raise RuntimeError("output shape must match q head dimensions")
+    idx_ptr = None
+    if out_indices is not None:
+        _check_tensor(out_indices, "out_indices", torch.int32, 1)
+        if out_indices.size(0) != b:
+            raise RuntimeError("out_indices batch mismatch")
+        idx_ptr = out_indices.data_ptr()
+    lib = _native.load()
+    _native.check(lib.pkv_combine_states(
+        states.data_ptr(), n_parts, idx_ptr, output.data_ptr(), b, output.size(0), hq,
+        HEAD_DIM, _DTYPES[output.dtype], _stream()))
+
+
+def workspace_bytes(batch: int, hq: int, num_splits: int) -> int:
+    """Reference ``persistentkv_workspace_bytes`` (kernels/persistentkv_attention.cuh:891)."""
+    return int(_native.load().pkv_workspace_bytes(batch, hq, num_splits))
+
+
+def workqueue_workspace_bytes(total_partial_slots: int, hq: int) -> int:
+    return int(_native.load().pkv_workqueue_workspace_bytes(total_partial_slots, hq))

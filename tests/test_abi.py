@@ -1,0 +1,127 @@
+"""The C ABI library: exports and host-side validation (no GPU, no kernel launch)."""
+
+import ctypes
+import re
+
+import pytest
+import torch
+
+from persistentkv_attention_b200 import _native, ops
+from tests.conftest import REPO, gpu_available
+
+HEADER = REPO / "include" / "pkv_b200.h"
+FAKE = 0x10000  # never dereferenced: every call below fails validation first
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(pkv_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared_functions()
+    assert len(names) >= 20
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(names) == set(_native.SIGNATURES)
+
+
+def test_status_strings(lib):
+    assert lib.pkv_status_string(0) == b"PKV_OK"
+    assert lib.pkv_status_string(4) == b"PKV_ERR_WORKSPACE"
+    assert lib.pkv_abi_version() == 1
+
+
+def test_workspace_bytes_formula(lib):
+    # reference persistentkv_workspace_bytes (kernels/persistentkv_attention.cuh:891-898)
+    assert lib.pkv_workspace_bytes(1, 32, 1) == 0
+    assert lib.pkv_workspace_bytes(8, 32, 24) == 8 * 32 * 24 * 130 * 4
+    assert lib.pkv_workqueue_workspace_bytes(100, 32) == 100 * 32 * 130 * 4
+
+
+def call_paged(lib, **kw):
+    args = dict(q=FAKE, k=FAKE, v=FAKE, bt=FAKE, out=FAKE, ws=FAKE, ws_bytes=1 << 30, B=1,
+                Hq=32, Hkv=8, d=128, P=64, page=16, maxp=32, context=512, splits=4,
+                dtype=0, stream=None)
+    args.update(kw)
+    return lib.pkv_paged_attention(*args.values())
+
+
+@pytest.mark.parametrize("kw,status,msg", [
+    (dict(d=64), 2, "requires d=128"),
+    (dict(Hkv=0), 1, "Hkv must be positive"),
+    (dict(Hq=30), 1, "divisible"),
+    (dict(Hq=24), 2, "G=3"),
+    (dict(Hq=128, Hkv=8), 2, "G=16"),
+    (dict(page=12), 2, "multiple of 8"),
+    (dict(page=0), 1, "page_size must be positive"),
+    (dict(context=0), 1, "context must be positive"),
+    (dict(splits=0), 1, "num_splits must be positive"),
+    (dict(splits=17), 1, "exceeds the 16 tiles"),
+    (dict(maxp=31), 1, "block_table has 31 pages"),
+    (dict(ws=None), 4, "Split dispatch requires workspace"),
+    (dict(ws_bytes=100), 4, "workspace holds 100 bytes"),
+    (dict(k=FAKE + 8), 3, "16-byte aligned"),
+    (dict(q=None), 1, "q must be a CUDA tensor"),
+    (dict(dtype=7), 2, "wrong dtype"),
+    (dict(P=1 << 22, Hkv=8, page=128), 2, "2^31 rows"),
+])
+def test_rectangular_validation(lib, kw, status, msg):
+    assert call_paged(lib, **kw) == status
+    assert msg in lib.pkv_last_error_message().decode()
+
+
+def test_workqueue_validation(lib):
+    base = [FAKE] * 12 + [1 << 30] + [1, 1, 1, 32, 8, 128, 64, 16, 32, 512, 10, 40, 0, 0, None]
+    if not gpu_available():  # a valid call would launch on the fake pointers
+        assert lib.pkv_paged_attention_workqueue(*base) == _native.PKV_ERR_NO_DEVICE
+    bad = list(base)
+    bad[23] = 0  # num_tasks
+    assert lib.pkv_paged_attention_workqueue(*bad) == 1
+    assert b"work_items must not be empty" in lib.pkv_last_error_message()
+    bad = list(base)
+    bad[24] = 0  # total_partial_slots
+    assert lib.pkv_paged_attention_workqueue(*bad) == 1
+    bad = list(base)
+    bad[11] = None  # workspace
+    assert lib.pkv_paged_attention_workqueue(*bad) == 4
+    assert b"Workqueue dispatch requires workspace" in lib.pkv_last_error_message()
+    bad = list(base)
+    bad[12] = 10  # workspace bytes
+    assert lib.pkv_paged_attention_workqueue(*bad) == 4
+    bad = list(base)
+    bad[7] = None  # merge_counters with fused merge
+    bad[25] = 1
+    assert lib.pkv_paged_attention_workqueue(*bad) == 1
+
+
+@pytest.mark.skipif(gpu_available(), reason="would launch on fake pointers")
+def test_valid_call_without_gpu_reports_no_device(lib):
+    assert call_paged(lib) == _native.PKV_ERR_NO_DEVICE
+    code = ctypes.c_uint32(0)
+    assert lib.pkv_device_error(ctypes.byref(code), 0) == _native.PKV_ERR_NO_DEVICE
+
+
+def test_torch_mirror_errors_match_reference_messages():
+    q = torch.zeros(1, 32, 128, dtype=torch.float16)
+    k = torch.zeros(4, 8, 16, 128, dtype=torch.float16)
+    bt = torch.zeros(1, 4, dtype=torch.int32)
+    out = torch.zeros_like(q)
+    ws = torch.zeros(0)
+    with pytest.raises(RuntimeError, match="q must be a CUDA tensor"):
+        ops.paged_attention(q, k, k, bt, out, ws, 64, 16, 1)
+    with pytest.raises(RuntimeError, match="q must be a CUDA tensor"):
+        ops.paged_attention_masked(q, k, k, bt, bt[0], out, ws, 64, 16, 1)
+    with pytest.raises(RuntimeError, match="q_source must be a CUDA tensor"):
+        ops.paged_attention_indexed(q, k, k, bt, bt[0], bt[0], bt[0], out, ws, 64, 16, 1)
+    with pytest.raises(RuntimeError, match="q_source must be a CUDA tensor"):
+        ops.paged_attention_workqueue(q, k, k, bt, bt[0], bt, bt[0], bt, bt[0], bt[0], out, ws,
+                                      64, 16, 1, False)
+
+
+def test_no_cpu_fallback_in_product_path():
+    """The engine never imports the oracle."""
+    for path in (REPO / "persistentkv_attention_b200").rglob("*.py"):
+        text = path.read_text()
+        assert "import oracle" not in text and "from oracle" not in text, path

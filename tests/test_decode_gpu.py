@@ -1,0 +1,302 @@
+"""GPU parity of the four operator entry points against the CPU oracle, the
+reference's golden outputs and (when built) the reference's own CUDA path."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import pkv_oracle as po
+from oracle import ref as ref_artefacts
+from persistentkv_attention_b200 import _native, ops
+from persistentkv_attention_b200.scheduler import Router
+from tests.golden.make_golden import smoke_inputs
+from tests.helpers import MAX_ERR, assert_close, make_case
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _clean_error_word():
+    _native.device_error(clear=True)
+    yield
+    torch.cuda.synchronize()
+    code = _native.device_error(clear=True)
+    assert code == 0, _native.describe_device_error(code)
+
+
+def _ws(b, hq, splits):
+    return torch.empty(max(1, ops.workspace_bytes(b, hq, splits) // 4), device="cuda",
+                       dtype=torch.float32) if splits > 1 else torch.empty(0, device="cuda")
+
+
+def test_smoke_kat(smoke_kat):
+    """The reference smoke-test cases (tests/smoke_test.cu:486-493) on the paged
+    path, against the reference's own cpu_gqa_attention outputs."""
+    for i, (case, q, k, v) in enumerate(smoke_inputs()):
+        kind, b, hq, hkv, n, splits, page = case
+        page = page or 16
+        per = (n + page - 1) // page
+        kp = np.zeros((b * per, hkv, page, 128), np.float32)
+        vp = np.zeros_like(kp)
+        table = np.zeros((b, per), np.int32)
+        for bi in range(b):
+            for lp in range(per):
+                phys = bi * per + (per - 1 - lp)   # reversed, smoke_test.cu:239-258
+                table[bi, lp] = phys
+                t0, t1 = lp * page, min(n, (lp + 1) * page)
+                kp[phys, :, : t1 - t0] = k[bi, :, t0:t1]
+                vp[phys, :, : t1 - t0] = v[bi, :, t0:t1]
+        dev = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+        out = torch.zeros(b, hq, 128, device="cuda", dtype=torch.float16)
+        ops.paged_attention(dev(q).half(), dev(kp).half(), dev(vp).half(), dev(table), out,
+                            _ws(b, hq, splits), n, page, splits)
+        torch.cuda.synchronize()
+        assert_close(out, smoke_kat[f"out_{i}"].astype(np.float64), "f16", str(case))
+
+
+EDGE_LENS = [1, 7, 15, 16, 17, 31, 32, 33, 63, 100, 257, 513, 1000]
+
+
+@pytest.mark.parametrize("g", [1, 2, 4, 8])
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("page", [8, 16, 32, 64])
+def test_masked_splits(g, dtype, page):
+    hq = 32 if g > 1 else 8
+    c = make_case(EDGE_LENS, hq=hq, hkv=hq // g, page_size=page, dtype=dtype, seed=g * 7 + page)
+    d = c.cuda()
+    want = c.oracle()
+    bucket = int(c.seq_lens.max())
+    for splits in (1, 3, 8):
+        out = torch.full((len(EDGE_LENS), hq, 128), float("nan"), device="cuda",
+                         dtype=d["q_source"].dtype)
+        ops.paged_attention_masked(d["q_source"], d["k_pages"], d["v_pages"], d["block_table"],
+                                   d["seq_lens"], out, _ws(len(EDGE_LENS), hq, splits), bucket,
+                                   page, splits)
+        torch.cuda.synchronize()
+        assert_close(out, want, dtype, f"splits={splits}")
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_unmasked_context(dtype):
+    c = make_case([700, 700, 700], dtype=dtype, seed=5, extra_pages=3)
+    d = c.cuda()
+    want = c.oracle(seq_lens=False, context=700)
+    for splits in (1, 2, 22):
+        out = torch.empty(3, 32, 128, device="cuda", dtype=d["q_source"].dtype)
+        ops.paged_attention(d["q_source"], d["k_pages"], d["v_pages"], d["block_table"], out,
+                            _ws(3, 32, splits), 700, 16, splits)
+        torch.cuda.synchronize()
+        assert_close(out, want, dtype, f"splits={splits}")
+
+
+def test_indexed_rows():
+    c = make_case([40, 5000, 1, 333, 2048], seed=9, indexed=True)
+    d = c.cuda()
+    want = c.oracle()
+    out = torch.full((c.out_rows, 32, 128), 7.0, device="cuda", dtype=torch.float16)
+    ops.paged_attention_indexed(d["q_source"], d["k_pages"], d["v_pages"], d["block_table"],
+                                d["seq_lens"], d["q_indices"], d["out_indices"], out,
+                                _ws(5, 32, 4), 5000, 16, 4)
+    torch.cuda.synchronize()
+    assert_close(out, want, "f16")
+    untouched = sorted(set(range(c.out_rows)) - set(c.out_indices.tolist()))
+    assert (out[untouched] == 7.0).all()          # rows nobody writes stay as they were
+
+
+def _run_workqueue(c, d, queue, fused, dtype):
+    items = torch.from_numpy(queue.work_items).cuda()
+    offsets = torch.from_numpy(queue.split_offsets).cuda()
+    counters = torch.zeros(len(c.seq_lens), c.hkv, device="cuda", dtype=torch.int32)
+    ws = torch.empty(ops.workqueue_workspace_bytes(queue.total_slots, c.hq) // 4, device="cuda")
+    out = torch.full((c.out_rows, c.hq, 128), float("nan"), device="cuda",
+                     dtype=d["q_source"].dtype)
+    ops.paged_attention_workqueue(d["q_source"], d["k_pages"], d["v_pages"], d["block_table"],
+                                  d["seq_lens"], items, offsets, counters, d["q_indices"],
+                                  d["out_indices"], out, ws, int(c.seq_lens.max()), c.page_size,
+                                  queue.total_slots, fused)
+    torch.cuda.synchronize()
+    assert (counters == 0).all(), "fused merge must leave the counters at zero"
+    return out
+
+
+@pytest.mark.parametrize("policy", ["reference", "balanced"])
+@pytest.mark.parametrize("fused", [False, True])
+@pytest.mark.parametrize("g,dtype", [(4, "f16"), (1, "f16"), (8, "bf16"), (2, "bf16")])
+def test_workqueue(policy, fused, g, dtype):
+    lens = [4096, 517, 1, 0, 12000, 64, 2500, 8191]
+    c = make_case(lens, hq=32, hkv=32 // g, dtype=dtype, seed=3 + g, indexed=True)
+    d = c.cuda()
+    want = c.oracle()
+    router = Router.reference(32, c.hkv) if policy == "reference" else Router.b200(32, c.hkv)
+    queue = router.build_workqueue(c.seq_lens, len(lens), policy)
+    out = _run_workqueue(c, d, queue, fused, dtype)
+    assert_close(out, want, dtype, f"{policy} fused={fused}")
+
+
+def test_state_shards_combine():
+    """Sequence sharding: per-shard (m, l, acc) states merge to the full answer."""
+    lens = [9000, 33, 4000]
+    c = make_case(lens, seed=21)
+    want = c.oracle()
+    d = c.cuda()
+    router = Router.b200(32, 8)
+    states = []
+    cut_pages = [int(np.ceil(n / 16) * 0.4) for n in lens]
+    for shard in range(2):
+        tables, sl = [], []
+        for b, n in enumerate(lens):
+            cut = cut_pages[b]
+            row = c.block_table[b]
+            if shard == 0:
+                tables.append(row[:cut]), sl.append(min(n, cut * 16))
+            else:
+                tables.append(row[cut:]), sl.append(max(0, n - cut * 16))
+        width = max(len(t) for t in tables) or 1
+        bt = np.stack([np.pad(t, (0, width - len(t)), mode="edge") if len(t) else
+                       np.zeros(width, np.int32) for t in tables]).astype(np.int32)
+        queue = router.build_workqueue(sl)
+        st = torch.empty(len(lens), 32, 130, device="cuda")
+        ws = torch.empty(ops.workqueue_workspace_bytes(queue.total_slots, 32) // 4, device="cuda")
+        counters = torch.zeros(len(lens), 8, device="cuda", dtype=torch.int32)
+        ops.paged_attention_workqueue_state(
+            d["q_source"], d["k_pages"], d["v_pages"], torch.from_numpy(bt).cuda(),
+            torch.tensor(sl, dtype=torch.int32, device="cuda"),
+            torch.from_numpy(queue.work_items).cuda(), torch.from_numpy(queue.split_offsets).cuda(),
+            counters, d["q_indices"], st, ws, 16, queue.total_slots, shard == 1)
+        states.append(st)
+    out = torch.empty(len(lens), 32, 128, device="cuda", dtype=torch.float16)
+    ops.combine_states(torch.stack(states), out)
+    torch.cuda.synchronize()
+    assert_close(out, want, "f16")
+
+
+def test_cuda_graph_replay():
+    c = make_case([3000, 800, 5000, 16], seed=31)
+    d = c.cuda()
+    queue = Router.b200(32, 8).build_workqueue(c.seq_lens)
+    items = torch.from_numpy(queue.work_items).cuda()
+    offsets = torch.from_numpy(queue.split_offsets).cuda()
+    counters = torch.zeros(4, 8, device="cuda", dtype=torch.int32)
+    ws = torch.empty(ops.workqueue_workspace_bytes(queue.total_slots, 32) // 4, device="cuda")
+    out = torch.zeros(4, 32, 128, device="cuda", dtype=torch.float16)
+
+    def step():
+        ops.paged_attention_workqueue(d["q_source"], d["k_pages"], d["v_pages"],
+                                      d["block_table"], d["seq_lens"], items, offsets, counters,
+                                      d["q_indices"], d["out_indices"], out, ws, 5000, 16,
+                                      queue.total_slots, True)
+
+    step()
+    torch.cuda.synchronize()
+    first = out.clone()
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            step()
+    out.zero_()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, first)
+    assert_close(out, c.oracle(), "f16")
+
+
+def test_full_size_properties():
+    """A BASELINE-size row (config 4: 32k tokens): equal results for every split
+    plan, exact invariance under relabelling of physical pages, and agreement
+    with the oracle."""
+    n = 32768
+    c = make_case([n], seed=77, holes=0.1)
+    d = c.cuda()
+    results = []
+    for splits in (1, 37, 128):
+        out = torch.empty(1, 32, 128, device="cuda", dtype=torch.float16)
+        ops.paged_attention_masked(d["q_source"], d["k_pages"], d["v_pages"], d["block_table"],
+                                   d["seq_lens"], out, _ws(1, 32, splits), n, 16, splits)
+        results.append(out)
+    torch.cuda.synchronize()
+    for r in results[1:]:
+        assert (r.float() - results[0].float()).abs().max().item() < MAX_ERR
+    # relabel physical pages: same answer, bit for bit
+    perm = torch.randperm(c.k_pages.shape[0], generator=torch.Generator().manual_seed(1))
+    inv = torch.empty_like(perm)
+    inv[perm] = torch.arange(perm.numel())
+    kp2 = d["k_pages"][perm.cuda()].contiguous()
+    vp2 = d["v_pages"][perm.cuda()].contiguous()
+    bt2 = inv.cuda()[d["block_table"].long()].to(torch.int32)
+    out2 = torch.empty(1, 32, 128, device="cuda", dtype=torch.float16)
+    ops.paged_attention_masked(d["q_source"], kp2, vp2, bt2, d["seq_lens"], out2,
+                               _ws(1, 32, 37), n, 16, 37)
+    torch.cuda.synchronize()
+    assert torch.equal(out2, results[1])
+    assert_close(results[1], c.oracle(), "f16")
+
+
+def test_device_errors_are_flagged_not_faults():
+    """Out-of-range page ids / lengths are skipped in-kernel and reported."""
+    c = make_case([300, 200], seed=41)
+    d = c.cuda()
+    bt = d["block_table"].clone()
+    bt[0, 3] = c.k_pages.shape[0] + 5
+    bt[1, 0] = -3
+    out = torch.empty(2, 32, 128, device="cuda", dtype=torch.float16)
+    ops.paged_attention_masked(d["q_source"], d["k_pages"], d["v_pages"], bt, d["seq_lens"], out,
+                               _ws(2, 32, 2), 300, 16, 2)
+    torch.cuda.synchronize()
+    code = _native.device_error(clear=True)
+    assert code & 0x1
+    sl = d["seq_lens"].clone()
+    sl[1] = 10 ** 6
+    ops.paged_attention_masked(d["q_source"], d["k_pages"], d["v_pages"], d["block_table"], sl,
+                               out, _ws(2, 32, 2), 300, 16, 2)
+    torch.cuda.synchronize()
+    assert _native.device_error(clear=True) & 0x2
+
+
+def _ref_ext():
+    ext = ref_artefacts.load_torch_ext()
+    if ext is None:
+        pytest.skip("reference extension not built (oracle/build_ref.py)")
+    return ext
+
+
+def test_reference_cuda_path_rectangular():
+    """Same inputs through the reference's own kernels built for sm_100a."""
+    ext = _ref_ext()
+    c = make_case([4096, 4096], seed=51, indexed=True)
+    d = c.cuda()
+    for splits in (1, 16):
+        ours = torch.zeros(c.out_rows, 32, 128, device="cuda", dtype=torch.float16)
+        theirs = torch.zeros_like(ours)
+        ws = torch.empty(2 * 32 * 16 * 130, device="cuda")
+        ops.paged_attention_indexed(d["q_source"], d["k_pages"], d["v_pages"], d["block_table"],
+                                    d["seq_lens"], d["q_indices"], d["out_indices"], ours, ws,
+                                    4096, 16, splits)
+        ext.paged_attention_indexed(d["q_source"], d["k_pages"], d["v_pages"], d["block_table"],
+                                    d["seq_lens"], d["q_indices"], d["out_indices"], theirs, ws,
+                                    4096, 16, splits)
+        torch.cuda.synchronize()
+        assert (ours.float() - theirs.float()).abs().max().item() < MAX_ERR
+
+
+def test_reference_cuda_path_workqueue():
+    ext = _ref_ext()
+    lens = [7000, 650, 3000, 1500, 20000, 800, 4100, 900]
+    c = make_case(lens, seed=52, indexed=True)
+    d = c.cuda()
+    queue = Router.reference(32, 8).build_workqueue(c.seq_lens, len(lens), "reference")
+    ours = _run_workqueue(c, d, queue, True, "f16")
+    items = torch.from_numpy(queue.work_items).cuda()
+    offsets = torch.from_numpy(queue.split_offsets).cuda()
+    counters = torch.zeros(len(lens), 8, device="cuda", dtype=torch.int32)
+    ws = torch.zeros(queue.total_slots * 32 * 130, device="cuda")
+    theirs = torch.full_like(ours, float("nan"))
+    ext.paged_attention_workqueue(d["q_source"], d["k_pages"], d["v_pages"], d["block_table"],
+                                  d["seq_lens"], items, offsets, counters, d["q_indices"],
+                                  d["out_indices"], theirs, ws, 20000, 16, queue.total_slots,
+                                  False)
+    torch.cuda.synchronize()
+    rows = torch.from_numpy(c.out_indices).long().cuda()
+    assert (ours[rows].float() - theirs[rows].float()).abs().max().item() < MAX_ERR
+    assert_close(theirs, c.oracle(), "f16", "reference kernel vs oracle")

@@ -1,0 +1,153 @@
+"""C++ router / work-queue builder / trace restatement vs the reference (no GPU)."""
+
+import numpy as np
+import pytest
+
+from persistentkv_attention_b200 import trace as tr
+from persistentkv_attention_b200.scheduler import Router
+
+REF_ROUTE = {"flashinfer": "single_pass", "persistentkv_bucket": "bucket",
+             "persistentkv_workqueue": "workqueue"}
+
+
+def router(hkv):
+    return Router.reference(hq=32, hkv=hkv)
+
+
+def test_choose_workqueue_row_splits(scheduler_golden):
+    for hkv, length, active, requested, auto, want in scheduler_golden["row_splits"]:
+        got = router(hkv).choose_workqueue_row_splits(length, active, requested, bool(auto))
+        assert got == want, (hkv, length, active, requested, auto)
+
+
+def test_choose_splits(scheduler_golden):
+    for hkv, lens, requested, auto, single, want in scheduler_golden["choose_splits"]:
+        assert router(hkv).choose_splits(lens, requested, bool(auto), bool(single)) == want
+
+
+def test_model_splits(scheduler_golden):
+    for hkv, lens, want in scheduler_golden["bucket_splits"]:
+        assert router(hkv).model_bucket_splits(lens) == want
+    for hkv, lens, want in scheduler_golden["workqueue_splits"]:
+        assert router(hkv).model_workqueue_splits(lens) == want
+
+
+def test_estimate_route_ms(scheduler_golden):
+    for hkv, lens, route, splits, want in scheduler_golden["route_ms"]:
+        got = router(hkv).estimate_route_ms(lens, REF_ROUTE[route], splits)
+        assert got == pytest.approx(want, rel=1e-12, abs=0)
+
+
+def test_choose_route(scheduler_golden):
+    for hkv, lens, route, splits, ms in scheduler_golden["routes"]:
+        got_route, got_splits, got_ms = router(hkv).choose_route(lens)
+        assert got_route == REF_ROUTE[route]
+        assert got_splits == splits
+        assert got_ms == pytest.approx(ms, rel=1e-12)
+
+
+def _check_queue_invariants(q, lens, hkv):
+    items = q.work_items
+    offs = q.split_offsets
+    assert offs[0] == 0 and q.total_slots == offs[-1]
+    written = set()
+    for b, length in enumerate(lens):
+        tiles = (length + 31) // 32
+        splits = offs[b + 1] - offs[b]
+        assert splits >= 1
+        for h in range(hkv):
+            mine = sorted((int(it[3]), int(it[4]), int(it[2])) for it in items
+                          if it[0] == b and it[1] == h)
+            assert len(mine) == splits
+            covered = 0
+            for tb, te, s in mine:
+                assert tb == covered and (te > tb or tiles == 0)
+                covered = te
+                written.add((offs[b] + s, h))
+            assert covered == tiles
+    # every (slot, kvh) partial state is written exactly once: no unwritten slot
+    assert len(written) == q.total_slots * hkv == len(items)
+
+
+def test_workqueue_matches_reference(scheduler_golden):
+    r = router(8)
+    for case in scheduler_golden["workqueues"]:
+        lens = case["lengths"]
+        q = r.build_workqueue(lens, case["active"], "reference",
+                              requested_splits=0 if case["auto"] else case["requested"])
+        # the reference may give a row more splits than tiles (unwritten slots);
+        # this builder clamps to the row's tile count and is otherwise identical
+        ref_splits = np.diff(case["split_offsets"])
+        tiles = [(x + 31) // 32 for x in lens]
+        clamped = np.minimum(ref_splits, np.maximum(tiles, 1))
+        assert np.array_equal(np.diff(q.split_offsets), clamped)
+        if np.array_equal(clamped, ref_splits):
+            assert q.work_items.tolist() == case["items"]
+            assert q.total_slots == case["total_slots"]
+        _check_queue_invariants(q, lens, 8)
+
+
+@pytest.mark.parametrize("policy", ["reference", "balanced", "fixed"])
+def test_workqueue_invariants(policy):
+    rng = np.random.default_rng(11)
+    for trial in range(40):
+        hkv = int(rng.choice([1, 4, 8, 32]))
+        lens = rng.integers(0, 40000, size=int(rng.integers(1, 12))).tolist()
+        if trial % 5 == 0:
+            lens[0] = 0
+        r = Router.b200(hq=32, hkv=hkv) if policy == "balanced" else Router.reference(32, hkv)
+        q = r.build_workqueue(lens, len(lens), policy, requested_splits=20)
+        _check_queue_invariants(q, lens, hkv)
+
+
+def test_balanced_fills_sms_evenly():
+    r = Router.b200(hq=32, hkv=8)
+    for lens in ([4096], [30000], [8000, 600, 5000, 7000, 512, 3000, 8192, 1000],
+                 [700] * 6 + [30000, 20000]):
+        q = r.build_workqueue(lens)
+        slots = r.params.sm_count * r.params.ctas_per_sm * r.params.tasks_per_cta
+        assert q.num_items <= slots
+        sizes = q.work_items[:, 4] - q.work_items[:, 3]
+        assert sizes.max() <= np.ceil(sum((x + 31) // 32 for x in lens) * 8 / (slots // 8 * 8)) * 2
+        assert np.all(np.diff(sizes) <= 0)            # largest task first
+
+
+def test_traces_match_reference(traces_golden):
+    for case in traces_golden:
+        lengths = tr.make_lengths(case["trace"], case["requests"], case["seed"])
+        assert [list(x) for x in lengths] == case["lengths"]
+        reqs, physical = tr.build_requests(case["trace"], case["requests"], case["max_active"],
+                                           case["seed"], case["hole"])
+        assert physical == case["physical_pages"]
+        assert [list(r.physical_pages[:5]) for r in reqs] == case["pages_head"]
+        assert [len(r.physical_pages) for r in reqs] == case["pages_len"]
+        assert [r.arrival for r in reqs] == case["arrivals"]
+        steps = tr.build_steps(reqs, case["max_active"])
+        assert len(steps) == case["n_steps"]
+        assert [[s.step, list(s.active_ids), list(s.lengths)] for s in steps[::7]] == case["steps"]
+
+
+@pytest.mark.parametrize("trace", tr.ENGINE_TRACES)
+def test_engine_traces(trace):
+    if trace == "long_b1":
+        reqs, _ = tr.build_requests(trace, 16, 1, 20260622, 0.0)
+        steps = tr.build_steps(reqs, 1)
+        assert len(steps) == 16 * 64
+        assert all(len(s.active_ids) == 1 for s in steps)
+        assert all(24576 <= s.lengths[0] <= 32768 + 64 for s in steps)
+        return
+    active = 64 if trace == "zipf_b64" else 8
+    n = 128 if trace == "zipf_b64" else 24
+    reqs, physical = tr.build_requests(trace, n, active, 20260622, 0.1 if active == 64 else 0.0)
+    steps = tr.build_steps(reqs, active)[:48]
+    assert len(steps) == 48
+    lens = np.concatenate([s.lengths for s in steps])
+    if trace == "uniform_8k":
+        assert lens.min() >= 512 and lens.max() <= 8192 + 96
+    if trace == "bimodal_32k":
+        assert ((lens <= 2048 + 64) | (lens >= 16384)).all()
+    if trace == "zipf_b64":
+        assert lens.min() >= 256 and lens.max() <= 32768 + 96
+        assert all(len(s.active_ids) == 64 for s in steps)
+    used = sorted(p for r in reqs for p in r.physical_pages)
+    assert len(used) == len(set(used)) and max(used) < physical
