@@ -1,0 +1,430 @@
+#!/usr/bin/env python3
+"""Decode-step benchmark of the B200 paged decode-attention engine.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
+                    [--impl engine|reference]
+
+A step is one continuous-batching decode step of a seeded synthetic trace
+(default: BASELINE config 2, B8 uniform [512, 8192] tokens, Hq 32 / Hkv 8,
+head_dim 128, page 16, fp16).  With N GPUs every rank decodes its own
+independent batch (batch partitioning, weak scaling); the job throughput is
+the tokens of all ranks over the slowest rank's device time.
+
+Reported (one JSON line on rank 0):
+  value       tokens/s with all inputs resident in HBM, per-step CUDA-event
+              intervals around graph-replayed decode steps, L2 flushed
+              (256 MiB write) before every step outside the intervals;
+  e2e         tokens/s through the public operator API from pinned host
+              buffers: host work-queue build, H2D of q rows + metadata,
+              decode, D2H of the output, per step;
+  roofline    algorithmic K/V bytes per step / step interval vs the measured
+              HBM copy bandwidth;
+  cpu_baseline the reference's own fp32 CPU decode (cpu_gqa_attention built
+              from its sources) on the host cores, bounded sample.
+
+``--impl reference`` times that reference CPU implementation alone on the
+same workload (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+from persistentkv_attention_b200 import trace as tr  # noqa: E402
+
+WORKLOADS = {
+    "uniform_8k": dict(trace="uniform_8k", requests=24, max_active=8, hole=0.0, hkv=8,
+                       desc="config 2: B8 uniform context [512, 8192], 24 requests, 8 active"),
+    "bimodal_32k": dict(trace="bimodal_32k", requests=24, max_active=8, hole=0.0, hkv=8,
+                        desc="config 3: B8 bimodal 75% [512, 2048] / 25% [16384, 32768]"),
+    "long_b1": dict(trace="long_b1", requests=16, max_active=1, hole=0.0, hkv=8,
+                    desc="config 4: B1 long context [24576, 32768], 16 sequential requests"),
+    "zipf_b64": dict(trace="zipf_b64", requests=128, max_active=64, hole=0.1, hkv=8,
+                     desc="config 5: B64 Zipf(1.1) context [256, 32768], 10% holes"),
+}
+HQ = 32
+PAGE = 16
+D = 128
+SEED = 20260622
+FLUSH_BYTES = 256 << 20
+
+
+def measured_peak_gbs() -> tuple[float, str]:
+    path = REPO / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.proc = None
+        self.device = device
+
+    def __enter__(self):
+        try:
+            props = torch.cuda.get_device_properties(self.device)
+            try:
+                sel = (f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:"
+                       f"{props.pci_device_id:02X}.0")
+            except AttributeError:
+                visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+                sel = visible.split(",")[self.device] if visible else str(self.device)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", sel, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        rows = []
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                rows.append((float(parts[0]), float(parts[1]), parts[3:]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for _, _, p in rows for n, v in zip(names, p[1:]) if v == "Active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows),
+                "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ workload
+def build_workload(name: str, rank: int, steps_needed: int):
+    w = WORKLOADS[name]
+    reqs, physical = tr.build_requests(w["trace"], w["requests"], w["max_active"], SEED + rank,
+                                       w["hole"], 0, PAGE)
+    steps = tr.build_steps(reqs, w["max_active"])
+    steps = steps[: max(1, min(len(steps), max(steps_needed, 48)))]
+    return w, reqs, physical, steps
+
+
+def kv_bytes(state, hkv: int, elem: int = 2) -> int:
+    return int(sum(state.lengths)) * hkv * D * 2 * elem
+
+
+# ------------------------------------------------------------------ CPU reference
+def cpu_reference_steps(reqs, steps, k_host, v_host, q_host, budget_s: float, hkv: int):
+    """Reference cpu_gqa_attention (oracle/_ref) over trace steps, rows in parallel.
+
+    Returns (tokens/s, steps run, threads, kind, seconds)."""
+    from oracle import ref as ref_artefacts
+
+    threads = len(os.sched_getaffinity(0))
+    by_id = {r.request_id: r for r in reqs}
+    use_ref = ref_artefacts.ref_cpu_available()
+    if not use_ref:
+        from oracle import build_oracle
+
+    g = HQ // hkv
+
+    def row_job(args):
+        # one (row, KV head) group: the reference oracle with Hq = G, Hkv = 1
+        rid, n, h = args
+        pages = np.asarray(by_id[rid].physical_pages[: (n + PAGE - 1) // PAGE], dtype=np.int64)
+        k = np.ascontiguousarray(k_host[pages, h].reshape(-1, D)[:n], dtype=np.float32)
+        v = np.ascontiguousarray(v_host[pages, h].reshape(-1, D)[:n], dtype=np.float32)
+        q = q_host[rid, h * g:(h + 1) * g][None].astype(np.float32)
+        return ref_artefacts.cpu_gqa_attention(q, k[None, None], v[None, None])
+
+    tokens = 0
+    done = 0
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(threads) as pool:
+        for state in steps:
+            if use_ref:
+                list(pool.map(row_job, [(r, n, h) for r, n in zip(state.active_ids, state.lengths)
+                                        for h in range(hkv)]))
+            else:
+                rows = [list(by_id[r].physical_pages) for r in state.active_ids]
+                width = max(len(r) for r in rows)
+                bt = np.array([r + [r[-1]] * (width - len(r)) for r in rows], np.int32)
+                build_oracle.port_decode(q_host.astype(np.float16), k_host.astype(np.float16),
+                                         v_host.astype(np.float16), bt, np.array(state.lengths),
+                                         q_indices=np.array(state.active_ids),
+                                         threads=threads)
+            tokens += len(state.active_ids)
+            done += 1
+            if time.perf_counter() - t0 > budget_s:
+                break
+    secs = time.perf_counter() - t0
+    return tokens / secs, done, threads, "reference" if use_ref else "port", secs
+
+
+def run_reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    w, reqs, physical, steps = build_workload(args.workload, 0, args.steps + args.warmup)
+    hkv = w["hkv"]
+    gen = torch.Generator().manual_seed(SEED + 7)
+    k_host = torch.randn(physical, hkv, PAGE, D, generator=gen).half().float().numpy()
+    v_host = torch.randn(physical, hkv, PAGE, D, generator=gen).half().float().numpy()
+    q_host = torch.randn(w["requests"], HQ, D, generator=gen).half().float().numpy()
+    warm = steps[: args.warmup]
+    cpu_reference_steps(reqs, warm, k_host, v_host, q_host, 1e9, hkv)
+    timed = [steps[(args.warmup + i) % len(steps)] for i in range(args.steps)]
+    per_step = max(0.5, 120.0 / max(1, args.steps))
+    value, done, threads, kind, secs = cpu_reference_steps(reqs, timed, k_host, v_host, q_host,
+                                                           per_step * args.steps, hkv)
+    line = {
+        "impl": "reference", "metric": "decode-step tokens/s", "value": value,
+        "unit": "tokens/s", "n_gpus": args.gpus, "steps": done, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * secs / max(1, done), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fp16-quantised inputs)",
+        "data": "synthetic", "config": {"workload": f"{args.workload}: {w['desc']}",
+                                        "hq": HQ, "hkv": hkv, "head_dim": D, "page_size": PAGE},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
+                         "sample": f"{done} decode steps of the trace, (row, KV head) groups "
+                                    f"in parallel"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ engine arm
+def run_engine_arm(args) -> None:
+    from persistentkv_attention_b200 import _native
+    from persistentkv_attention_b200.serving import DecodeEngine
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    w, reqs, physical, steps = build_workload(args.workload, rank, args.steps + args.warmup)
+    hkv = w["hkv"]
+    gen = torch.Generator(device=dev).manual_seed(SEED + 7 + rank)
+    k_pages = torch.randn(physical, hkv, PAGE, D, generator=gen, device=dev).half()
+    v_pages = torch.randn(physical, hkv, PAGE, D, generator=gen, device=dev).half()
+    q_pool = torch.randn(w["requests"], HQ, D, generator=gen, device=dev).half()
+    engine = DecodeEngine(k_pages, v_pages, HQ, fused=not args.no_fused)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(dev)
+
+    # device-resident plans + one CUDA graph per distinct step
+    plans, graphs, outs = [], [], []
+    n_distinct = min(len(steps), args.steps + args.warmup)
+    for state in steps[:n_distinct]:
+        p = engine.upload(engine.plan_from_trace(reqs, state))
+        plans.append(p)
+    for p in plans:
+        o = torch.empty(p.batch, HQ, D, dtype=torch.float16, device=dev)
+        outs.append(o)
+        graphs.append(engine.capture(p, q_pool, o, stream))
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    sched = [i % n_distinct for i in range(args.warmup + args.steps)]
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    with torch.cuda.stream(stream):
+        for j in sched[: args.warmup]:
+            flush.fill_(1)
+            graphs[j].replay()
+    barrier()
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            torch.cuda._sleep(2_000_000)          # lets the host queue run ahead
+            for i, j in enumerate(sched[args.warmup:]):
+                flush.fill_(i & 0xFF)
+                ev[i][0].record(stream)
+                graphs[j].replay()
+                ev[i][1].record(stream)
+        barrier()
+    times_ms = [a.elapsed_time(b) for a, b in ev]
+    tokens = sum(plans[j].batch for j in sched[args.warmup:])
+    bytes_alg = sum(kv_bytes(steps[j], hkv) for j in sched[args.warmup:])
+    total_ms = sum(times_ms)
+    launches = args.steps * (1 if not args.no_fused else 2)
+    code = _native.device_error(clear=True)
+    if code:
+        raise RuntimeError(f"device error: {_native.describe_device_error(code)}")
+    # correctness gate on one step (reference: one mid-trace check, :1082-1088)
+    check_step = len(plans) // 2
+    graphs[check_step].replay()
+    torch.cuda.synchronize()
+    from oracle import pkv_oracle as po  # checker only
+
+    st = steps[check_step]
+    row = 0
+    rid = st.active_ids[row]
+    k_row = k_pages[torch.tensor(reqs[rid].physical_pages[: (st.lengths[row] + PAGE - 1) // PAGE],
+                                 device=dev)]
+    v_row = v_pages[torch.tensor(reqs[rid].physical_pages[: (st.lengths[row] + PAGE - 1) // PAGE],
+                                 device=dev)]
+    kk = k_row.permute(1, 0, 2, 3).reshape(hkv, -1, D)[:, : st.lengths[row]].double().cpu().numpy()
+    vv = v_row.permute(1, 0, 2, 3).reshape(hkv, -1, D)[:, : st.lengths[row]].double().cpu().numpy()
+    want = po.attend_row(q_pool[rid].double().cpu().numpy(), kk, vv)
+    max_err = float(np.abs(outs[check_step][row].double().cpu().numpy() - want).max())
+    if max_err >= 2e-3:
+        raise SystemExit(f"correctness gate failed: max abs error {max_err:.3e}")
+
+    # ---- end to end through the public API from pinned host buffers
+    q_host = q_pool.cpu().pin_memory()
+    out_host = torch.empty(max(p.batch for p in plans), HQ, D, dtype=torch.float16).pin_memory()
+    scratch: dict = {}
+    bi = bo = 0
+    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+    host_rows = []
+    for state in steps[:n_distinct]:
+        plan = engine.plan_from_trace(reqs, state)
+        v = plan.views(plan.buf)
+        host_rows.append((list(state.lengths), v["block_table"].numpy().copy(),
+                          torch.stack([q_host[r] for r in state.active_ids]).pin_memory()))
+    with torch.cuda.stream(stream):
+        for j in sched[: args.warmup]:
+            lens, rows, qh = host_rows[j]
+            engine.step_host(lens, rows, qh, out_host, scratch)
+            stream.synchronize()
+        barrier()
+        for i, j in enumerate(sched[args.warmup:]):
+            lens, rows, qh = host_rows[j]
+            flush.fill_(i & 0xFF)
+            stream.synchronize()
+            e2e_ev[i][0].record(stream)
+            h, d = engine.step_host(lens, rows, qh, out_host, scratch)
+            e2e_ev[i][1].record(stream)
+            stream.synchronize()
+            bi += h
+            bo += d
+        barrier()
+    e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev)
+
+    # ---- aggregate over ranks (max time, summed tokens)
+    stats = torch.tensor([total_ms, e2e_ms, float(tokens), float(bytes_alg)], dtype=torch.float64,
+                         device=dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        mx = stats.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = stats.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        total_ms, e2e_ms = float(mx[0]), float(mx[1])
+        tokens, bytes_alg = float(sm[2]), float(sm[3])
+    if rank != 0:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+
+    peak, peak_kind = measured_peak_gbs()
+    value = tokens / (total_ms / 1000.0)
+    per_step_bytes = bytes_alg / args.steps / world
+    achieved = per_step_bytes / (total_ms / args.steps / 1000.0) / 1e9
+    traffic = None
+    tpath = REPO / "profiles" / f"traffic_{args.workload}.json"
+    if tpath.exists():
+        traffic = json.loads(tpath.read_text()).get("dram_bytes_per_launch")
+    line = {
+        "metric": "decode-step tokens/s", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded trace, K/V/q ~ N(0,1))",
+        "config": {
+            "workload": f"{args.workload}: {w['desc']}", "hq": HQ, "hkv": hkv, "head_dim": D,
+            "page_size": PAGE, "active_per_gpu": w["max_active"],
+            "parallelism": f"batch-partitioned x{world} (independent batch per GPU)",
+            "l2": "flushed (256 MiB write) before every step, outside the timed intervals",
+            "merge": "fused last-task merge" if not args.no_fused else "PDL merge kernel",
+            "split_policy": "balanced (C++ builder)",
+        },
+        "hbm_gbs": achieved, "hbm_frac_of_8tbs": achieved / 8000.0,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                     "kernel": "pkv_decode_kernel (fused merge), 1 launch per step"},
+        "e2e": {"value": tokens / (e2e_ms / 1000.0), "unit": "tokens/s",
+                "h2d_bytes_per_step": bi // args.steps, "d2h_bytes_per_step": bo // args.steps},
+        "gpu_launches": launches,
+        "correctness_max_abs_err": max_err,
+    }
+    c = clocks.summary()
+    line["clocks"] = c
+    if world == 1 and not args.no_cpu_baseline:
+        k_host = k_pages.float().cpu().numpy()
+        v_host = v_pages.float().cpu().numpy()
+        qn = q_pool.float().cpu().numpy()
+        val, done, threads, kind, secs = cpu_reference_steps(reqs, steps[: args.steps], k_host,
+                                                             v_host, qn, 15.0, hkv)
+        line["cpu_baseline"] = {"value": val, "unit": "tokens/s", "cores": threads, "kind": kind,
+                                "sample": f"first {done} decode steps of the trace "
+                                          f"({secs:.1f} s), (row, KV head) groups in parallel"}
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=48)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="uniform_8k")
+    ap.add_argument("--impl", choices=["engine", "reference"], default="engine")
+    ap.add_argument("--no-fused", action="store_true", help="separate PDL merge kernel")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_engine_arm(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -20,9 +20,13 @@
  *   split_offsets  [B + 1] int32              partial slots of row b are
  *                                              split_offsets[b] + split
  *   merge_counters [B, Hkv] int32             zero on entry, zero on return
- *   workspace      fp32 partial states: m[slots*Hq] | l[slots*Hq] |
- *                  acc[slots*Hq*128]   (slots = B*num_splits, or
- *                  total_partial_slots on the work-queue route)
+ *   workspace      16-byte aligned fp32 scratch for slots*Hq partial states
+ *                  of 130 floats (slots = B*num_splits, or
+ *                  total_partial_slots on the work-queue route); its
+ *                  layout is internal to the library
+ *
+ * A work-queue entry {-1, -1, *, *, *} is a no-op (padding emitted by the
+ * balanced builder policy between resident CTA slots).
  */
 #ifndef PKV_B200_H
 #define PKV_B200_H

@@ -22,8 +22,11 @@ __device__ unsigned int g_pkv_error_word = 0u;
 
 namespace {
 
-constexpr int kSlots = 8;        // ring depth (8 KB per slot)
-constexpr int kCtasPerSm = 2;    // resident decode CTAs per SM
+#ifndef PKV_RING_SLOTS
+#define PKV_RING_SLOTS 8
+#endif
+constexpr int kSlots = PKV_RING_SLOTS;          // ring depth (8 KB per slot)
+constexpr int kCtasPerSm = PKV_MIN_CTAS_PER_SM;  // resident decode CTAs per SM
 constexpr int kMaxDevices = 64;
 
 thread_local char t_last_error[512] = "";
@@ -338,11 +341,13 @@ void fill_common(LaunchSpec& ls, const Common& c) {
     ls.merge = false;
 }
 
+// Workspace layout (internal): acc[slots*Hq*128] | m[slots*Hq] | l[slots*Hq],
+// acc first so its rows stay 16-byte aligned for vector loads.
 void partition_workspace(DecodeParams& dp, void* ws, long long slots) {
     float* base = static_cast<float*>(ws);
-    dp.part_m = base;
-    dp.part_l = base + slots * dp.Hq;
-    dp.part_acc = base + 2 * slots * dp.Hq;
+    dp.part_acc = base;
+    dp.part_m = base + slots * dp.Hq * kHeadDim;
+    dp.part_l = dp.part_m + slots * dp.Hq;
 }
 
 // Shared body of the three rectangular entry points.
@@ -375,8 +380,8 @@ pkv_status rectangular(const Common& c, const int32_t* seq_lens, const int32_t* 
             return fail(PKV_ERR_WORKSPACE, "workspace holds %zu bytes but %zu are needed",
                         workspace_bytes, need);
         }
-        if (reinterpret_cast<uintptr_t>(workspace) & 3u)
-            return fail(PKV_ERR_MISALIGNED, "workspace must be 4-byte aligned");
+        if (reinterpret_cast<uintptr_t>(workspace) & 15u)
+            return fail(PKV_ERR_MISALIGNED, "workspace must be 16-byte aligned");
     }
     if (q_rows <= 0 || out_rows <= 0) {
         if (c.B == 0) return ok_status();
@@ -435,8 +440,8 @@ pkv_status workqueue_common(const Common& c, const int32_t* seq_lens, const int3
         return fail(PKV_ERR_WORKSPACE, "workspace holds %zu bytes but %zu are needed",
                     workspace_bytes, need);
     }
-    if (reinterpret_cast<uintptr_t>(workspace) & 3u)
-        return fail(PKV_ERR_MISALIGNED, "workspace must be 4-byte aligned");
+    if (reinterpret_cast<uintptr_t>(workspace) & 15u)
+        return fail(PKV_ERR_MISALIGNED, "workspace must be 16-byte aligned");
     if (q_rows <= 0) return fail(PKV_ERR_INVALID_ARGUMENT, "q_source must have at least one row");
     if (state_out == nullptr && out_rows <= 0)
         return fail(PKV_ERR_INVALID_ARGUMENT, "output must have at least one row");

@@ -14,7 +14,13 @@ namespace pkv {
 constexpr int kHeadDim = 128;        // reference: kernels/persistentkv_attention.cuh:26
 constexpr int kTileTokens = 32;      // work-item tile unit, reference cuh:28
 constexpr int kStageTokens = 16;     // tokens staged per ring slot
-constexpr int kConsumerWarps = 4;    // math warps per CTA
+#ifndef PKV_CONSUMER_WARPS
+#define PKV_CONSUMER_WARPS 4
+#endif
+#ifndef PKV_MIN_CTAS_PER_SM
+#define PKV_MIN_CTAS_PER_SM 2
+#endif
+constexpr int kConsumerWarps = PKV_CONSUMER_WARPS;  // math warps per CTA
 constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
 constexpr int kStateStride = kHeadDim + 2;  // {m, l, acc[128]} per state row
 constexpr int kRowBytes = kHeadDim * 2;     // one token of one KV head

@@ -65,6 +65,7 @@ struct Item {
     int slot;                // partial-state slot, -1 if none/invalid
     int row_splits;          // partial slots of this row
     int q_row, out_row;      // -1 if invalid
+    bool noop;               // padding entry {-1, -1, ...}: no work, no output
 };
 
 __device__ __forceinline__ int ceil_div_i(int a, int b) { return (a + b - 1) / b; }
@@ -80,6 +81,7 @@ __device__ __forceinline__ Item load_item(const DecodeParams& p, int index, bool
     it.out_row = -1;
     it.tok_begin = 0;
     it.tok_end = 0;
+    it.noop = false;
     long long tb, te;
     if (p.work_items != nullptr) {
         const int32_t* w = p.work_items + (size_t)index * 5;
@@ -88,6 +90,13 @@ __device__ __forceinline__ Item load_item(const DecodeParams& p, int index, bool
         it.split = __ldg(w + 2);
         tb = __ldg(w + 3);
         te = __ldg(w + 4);
+        if (it.row == -1 && it.kvh == -1) {  // builder padding between resident slots
+            it.noop = true;
+            it.row = 0;
+            it.kvh = 0;
+            it.split = 0;
+            return it;
+        }
         if (it.row < 0 || it.row >= p.B || it.kvh < 0 || it.kvh >= p.Hkv || it.split < 0 ||
             tb < 0 || te < tb) {
             if (report) raise_error(p.error, kErrWorkItem);
@@ -157,6 +166,127 @@ __device__ __forceinline__ Item load_item(const DecodeParams& p, int index, bool
     return it;
 }
 
+// ------------------------------------------------------------------ merge
+// Segmented log-sum-exp merge of the partial states in slots [s0, s0 + n) for
+// the G query heads qh0 .. qh0+G-1 of one row (reference cuh:719-784 and the
+// fused merge :660-708).  Run by NW warps; memory-level parallel: m / l are
+// reduced across all threads, weights are staged in shared memory per chunk
+// of 64 slots, and acc rows are read as float4 by NW slot groups.
+constexpr int kMergeChunk = 64;
+
+template <int NW>
+__host__ __device__ constexpr int merge_scratch_floats() {
+    return kMergeChunk * 8 + 2 * NW * 8;
+}
+
+struct MergeSmem {
+    float* w;     // [kMergeChunk][8] weights of the current chunk
+    float* stat;  // [2][NW][8] per-warp max / l partials
+    float* red;   // [NW][G][128] acc partials (16-byte aligned)
+};
+
+template <bool kNamedBarrier>
+__device__ __forceinline__ void sync_merge() {
+    if constexpr (kNamedBarrier) {
+        consumer_bar_sync();
+    } else {
+        __syncthreads();
+    }
+}
+
+template <int G, typename T, int NW, bool kNamedBarrier>
+__device__ __forceinline__ void merge_slots(const float* __restrict__ pm,
+                                            const float* __restrict__ pl,
+                                            const float* __restrict__ pa, int s0, int n, int Hq,
+                                            int qh0, const MergeSmem& sm, T* out,
+                                            float* state) {
+    constexpr int NT = NW * 32;
+    const int t = threadIdx.x % NT;
+    const int warp = t >> 5;
+    const int lane = t & 31;
+    constexpr int kSlotsPerPass = NT / G;
+    const int g = t % G;  // fixed: the strides below are multiples of G
+    float mx = kNegFltMax;
+    for (int s = t / G; s < n; s += kSlotsPerPass)
+        mx = fmaxf(mx, __ldcg(pm + (size_t)(s0 + s) * Hq + qh0 + g));
+#pragma unroll
+    for (int off = 16; off >= G; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane < G) sm.stat[warp * 8 + lane] = mx;
+    sync_merge<kNamedBarrier>();
+    float m_all[G];
+#pragma unroll
+    for (int gg = 0; gg < G; ++gg) {
+        float v = sm.stat[gg];
+#pragma unroll
+        for (int w = 1; w < NW; ++w) v = fmaxf(v, sm.stat[w * 8 + gg]);
+        m_all[gg] = v;
+    }
+    float m_mine = m_all[0];
+#pragma unroll
+    for (int gg = 1; gg < G; ++gg) m_mine = gg == g ? m_all[gg] : m_mine;
+    float ls = 0.f;
+    for (int s = t / G; s < n; s += kSlotsPerPass) {
+        const size_t i = (size_t)(s0 + s) * Hq + qh0 + g;
+        ls = fmaf(fast_exp2((__ldcg(pm + i) - m_mine) * kLog2e), __ldcg(pl + i), ls);
+    }
+#pragma unroll
+    for (int off = 16; off >= G; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+    if (lane < G) sm.stat[NW * 8 + warp * 8 + lane] = ls;
+
+    float4 acc[G];
+#pragma unroll
+    for (int gg = 0; gg < G; ++gg) acc[gg] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c0 = 0; c0 < n; c0 += kMergeChunk) {
+        const int cn = min(kMergeChunk, n - c0);
+        for (int i = t; i < cn * G; i += NT) {
+            const int s = i / G;  // i % G == g
+            sm.w[s * 8 + g] = fast_exp2(
+                (__ldcg(pm + (size_t)(s0 + c0 + s) * Hq + qh0 + g) - m_mine) * kLog2e);
+        }
+        sync_merge<kNamedBarrier>();
+#pragma unroll 4
+        for (int s = warp; s < cn; s += NW) {
+            const float* row = pa + ((size_t)(s0 + c0 + s) * Hq + qh0) * kHeadDim + 4 * lane;
+#pragma unroll
+            for (int gg = 0; gg < G; ++gg) {
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(row + gg * kHeadDim));
+                const float w = sm.w[s * 8 + gg];
+                acc[gg].x = fmaf(w, v.x, acc[gg].x);
+                acc[gg].y = fmaf(w, v.y, acc[gg].y);
+                acc[gg].z = fmaf(w, v.z, acc[gg].z);
+                acc[gg].w = fmaf(w, v.w, acc[gg].w);
+            }
+        }
+        sync_merge<kNamedBarrier>();
+    }
+#pragma unroll
+    for (int gg = 0; gg < G; ++gg)
+        *reinterpret_cast<float4*>(sm.red + (warp * G + gg) * kHeadDim + 4 * lane) = acc[gg];
+    sync_merge<kNamedBarrier>();
+    for (int idx = t; idx < G * kHeadDim; idx += NT) {
+        const int gg = idx / kHeadDim;
+        const int d = idx % kHeadDim;
+        float l_all = 0.f, o = 0.f;
+#pragma unroll
+        for (int j = 0; j < NW; ++j) {
+            l_all += sm.stat[NW * 8 + j * 8 + gg];
+            o += sm.red[(j * G + gg) * kHeadDim + d];
+        }
+        if (state != nullptr) {
+            state[gg * kStateStride + 2 + d] = o;
+            if (d == 0) {
+                float mv = sm.stat[gg];
+#pragma unroll
+                for (int w = 1; w < NW; ++w) mv = fmaxf(mv, sm.stat[w * 8 + gg]);
+                state[gg * kStateStride] = mv;
+                state[gg * kStateStride + 1] = l_all;
+            }
+        } else if (out != nullptr) {
+            out[gg * kHeadDim + d] = ElemOps<T>::from_float(l_all > 0.f ? o / l_all : 0.f);
+        }
+    }
+}
+
 template <int G>
 struct DecodeSmem {
     static constexpr int kMergeStride = kHeadDim + 4;  // padded: conflict-free combine
@@ -168,11 +298,12 @@ constexpr size_t decode_smem_bytes() {
     return 1024 /* alignment slack */ + (size_t)NSLOTS * kSlotBytes +
            2 * NSLOTS * sizeof(uint64_t) + 64 +
            2 * 2 * kConsumerWarps * 8 * sizeof(float) +
-           2 * DecodeSmem<G>::kMergeFloats * sizeof(float);
+           2 * DecodeSmem<G>::kMergeFloats * sizeof(float) +
+           merge_scratch_floats<kConsumerWarps>() * sizeof(float);
 }
 
 template <int G, typename T, int BOX_ROWS, int NSLOTS>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     pkv_decode_kernel(const __grid_constant__ DecodeParams p,
                       const __grid_constant__ CUtensorMap tmap_k,
                       const __grid_constant__ CUtensorMap tmap_v) {
@@ -194,6 +325,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                                               2 * NSLOTS * sizeof(uint64_t) + 64);
     float* s_lstat = s_mstat + 2 * kConsumerWarps * 8;
     float* s_merge = s_lstat + 2 * kConsumerWarps * 8;
+    float* s_mw = s_merge + 2 * DecodeSmem<G>::kMergeFloats;  // merge weights + stats
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -313,6 +445,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int index = blockIdx.x; index < p.num_items; index += gridDim.x) {
         if (index + (int)gridDim.x >= p.num_items) griddep_launch_dependents();
         const Item it = load_item(p, index, threadIdx.x == 0);
+        if (it.noop) continue;
         const int n_stages = ceil_div_i(it.tok_end - it.tok_begin, kStageTokens);
 
         // Q^T as the B operand: lane holds Q[head tq][16 ks + tc (+8) .. +1].
@@ -476,14 +609,13 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         consumer_bar_sync();
 
-        const int d = threadIdx.x;  // 0..127
         const bool rect = p.work_items == nullptr;
         const bool direct = it.row_splits == 1;
-        float outv[G];
-        float mfin[G];
-        float lfin[G];
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
+        const bool write_direct_out = direct && p.state_out == nullptr && it.out_row >= 0 &&
+                                      (!rect || it.tok_end > it.tok_begin);
+        for (int idx = threadIdx.x; idx < G * kHeadDim; idx += kConsumerWarps * 32) {
+            const int g = idx / kHeadDim;
+            const int d = idx % kHeadDim;
             float mx = -INFINITY;
 #pragma unroll
             for (int w = 0; w < kConsumerWarps; ++w) mx = fmaxf(mx, mstat[w * 8 + g]);
@@ -495,41 +627,31 @@ __global__ void __launch_bounds__(kThreads, 2)
                 lsum = fmaf(wt, lstat[w * 8 + g], lsum);
                 osum = fmaf(wt, mbuf[(w * G + g) * DecodeSmem<G>::kMergeStride + d], osum);
             }
-            outv[g] = osum;
-            lfin[g] = lsum;
-            mfin[g] = mx == -INFINITY ? kNegFltMax : mx * kLn2;
-        }
-
-        if (direct) {
-            if (p.state_out != nullptr) {
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    float* st = p.state_out + ((size_t)it.row * p.Hq + it.kvh * G + g) * kStateStride;
-                    st[2 + d] = outv[g];
+            const float mnat = mx == -INFINITY ? kNegFltMax : mx * kLn2;
+            if (direct) {
+                if (p.state_out != nullptr) {
+                    float* st =
+                        p.state_out + ((size_t)it.row * p.Hq + it.kvh * G + g) * kStateStride;
+                    st[2 + d] = osum;
                     if (d == 0) {
-                        st[0] = mfin[g];
-                        st[1] = lfin[g];
+                        st[0] = mnat;
+                        st[1] = lsum;
                     }
+                } else if (write_direct_out) {
+                    T* orow = reinterpret_cast<T*>(p.out) +
+                              ((size_t)it.out_row * p.Hq + (size_t)it.kvh * G + g) * kHeadDim;
+                    orow[d] = Ops::from_float(osum * (lsum > 0.f ? 1.f / lsum : 0.f));
                 }
-            } else if (it.out_row >= 0 && (!rect || it.tok_end > it.tok_begin)) {
-                T* orow = reinterpret_cast<T*>(p.out) +
-                          ((size_t)it.out_row * p.Hq + (size_t)it.kvh * G) * kHeadDim;
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    const float inv = lfin[g] > 0.f ? 1.f / lfin[g] : 0.f;
-                    orow[g * kHeadDim + d] = Ops::from_float(outv[g] * inv);
-                }
-            }
-        } else if (it.slot >= 0) {
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
+            } else if (it.slot >= 0) {
                 const size_t si = (size_t)it.slot * p.Hq + (size_t)it.kvh * G + g;
-                p.part_acc[si * kHeadDim + d] = outv[g];
+                p.part_acc[si * kHeadDim + d] = osum;
                 if (d == 0) {
-                    p.part_m[si] = mfin[g];
-                    p.part_l[si] = lfin[g];
+                    p.part_m[si] = mnat;
+                    p.part_l[si] = lsum;
                 }
             }
+        }
+        if (!direct && it.slot >= 0) {
             if (p.merge_counters != nullptr && !rect) {
                 // fused merge: the last task of this (row, kvh) merges all of
                 // the row's slots (reference cuh:648-716).
@@ -545,34 +667,18 @@ __global__ void __launch_bounds__(kThreads, 2)
                 consumer_bar_sync();
                 if (s_flags[1]) {
                     __threadfence();
-                    const int s0 = it.slot - it.split;
-                    const int s1 = s0 + it.row_splits;
-#pragma unroll
-                    for (int g = 0; g < G; ++g) {
-                        const size_t qh = (size_t)it.kvh * G + g;
-                        float mx = kNegFltMax;
-                        for (int s = s0; s < s1; ++s)
-                            mx = fmaxf(mx, __ldcg(p.part_m + (size_t)s * p.Hq + qh));
-                        float lsum = 0.f, osum = 0.f;
-                        for (int s = s0; s < s1; ++s) {
-                            const size_t si = (size_t)s * p.Hq + qh;
-                            const float wt = fast_exp2((__ldcg(p.part_m + si) - mx) * kLog2e);
-                            lsum = fmaf(wt, __ldcg(p.part_l + si), lsum);
-                            osum = fmaf(wt, __ldcg(p.part_acc + si * kHeadDim + d), osum);
-                        }
-                        if (p.state_out != nullptr) {
-                            float* st = p.state_out + ((size_t)it.row * p.Hq + qh) * kStateStride;
-                            st[2 + d] = osum;
-                            if (d == 0) {
-                                st[0] = mx;
-                                st[1] = lsum;
-                            }
-                        } else if (it.out_row >= 0) {
-                            T* o = reinterpret_cast<T*>(p.out) +
-                                   ((size_t)it.out_row * p.Hq + qh) * kHeadDim;
-                            o[d] = Ops::from_float(lsum > 0.f ? osum / lsum : 0.f);
-                        }
+                    MergeSmem ms{s_mw, s_mw + kMergeChunk * 8, s_merge};
+                    const int qh0 = it.kvh * G;
+                    T* o = nullptr;
+                    float* st = nullptr;
+                    if (p.state_out != nullptr) {
+                        st = p.state_out + ((size_t)it.row * p.Hq + qh0) * kStateStride;
+                    } else if (it.out_row >= 0) {
+                        o = reinterpret_cast<T*>(p.out) + ((size_t)it.out_row * p.Hq + qh0) * kHeadDim;
                     }
+                    merge_slots<G, T, kConsumerWarps, true>(p.part_m, p.part_l, p.part_acc, it.slot - it.split,
+                                            it.row_splits, p.Hq, qh0, ms, o, st);
+                    consumer_bar_sync();  // merge scratch aliases the combine buffers
                 }
             }
         }
@@ -588,10 +694,11 @@ __global__ void __launch_bounds__(kThreads, 2)
 template <int G, typename T>
 __global__ void __launch_bounds__(kHeadDim)
     pkv_merge_kernel(const __grid_constant__ MergeParams p) {
+    __shared__ __align__(16) float s_w[merge_scratch_floats<4>()];
+    __shared__ __align__(16) float s_red[4 * G * kHeadDim];
     griddep_wait();
     const int kvh = blockIdx.x;
     const int row = blockIdx.y;
-    const int d = threadIdx.x;
     int s0, s1;
     if (p.split_offsets != nullptr) {
         s0 = __ldg(p.split_offsets + row);
@@ -602,41 +709,24 @@ __global__ void __launch_bounds__(kHeadDim)
     }
     if (s1 - s0 == 1) return;  // written directly by the decode kernel
     if (s0 < 0 || s1 < s0 || s1 > p.total_slots) {
-        if (d == 0 && kvh == 0) raise_error(p.error, kErrSlot);
+        if (threadIdx.x == 0 && kvh == 0) raise_error(p.error, kErrSlot);
         return;
     }
-    int orow = row;
-    if (p.state_out == nullptr) {
-        orow = p.out_indices != nullptr ? __ldg(p.out_indices + row) : row;
+    const int qh0 = kvh * G;
+    T* o = nullptr;
+    float* st = nullptr;
+    if (p.state_out != nullptr) {
+        st = p.state_out + ((size_t)row * p.Hq + qh0) * kStateStride;
+    } else {
+        const int orow = p.out_indices != nullptr ? __ldg(p.out_indices + row) : row;
         if (orow < 0 || orow >= p.out_rows) {
-            if (d == 0 && kvh == 0) raise_error(p.error, kErrIndex);
+            if (threadIdx.x == 0 && kvh == 0) raise_error(p.error, kErrIndex);
             return;
         }
+        o = reinterpret_cast<T*>(p.out) + ((size_t)orow * p.Hq + qh0) * kHeadDim;
     }
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-        const size_t qh = (size_t)kvh * G + g;
-        float mx = kNegFltMax;
-        for (int s = s0; s < s1; ++s) mx = fmaxf(mx, __ldg(p.part_m + (size_t)s * p.Hq + qh));
-        float lsum = 0.f, osum = 0.f;
-        for (int s = s0; s < s1; ++s) {
-            const size_t si = (size_t)s * p.Hq + qh;
-            const float wt = fast_exp2((__ldg(p.part_m + si) - mx) * kLog2e);
-            lsum = fmaf(wt, __ldg(p.part_l + si), lsum);
-            osum = fmaf(wt, __ldg(p.part_acc + si * kHeadDim + d), osum);
-        }
-        if (p.state_out != nullptr) {
-            float* st = p.state_out + ((size_t)row * p.Hq + qh) * kStateStride;
-            st[2 + d] = osum;
-            if (d == 0) {
-                st[0] = mx;
-                st[1] = lsum;
-            }
-        } else {
-            T* o = reinterpret_cast<T*>(p.out) + ((size_t)orow * p.Hq + qh) * kHeadDim;
-            o[d] = ElemOps<T>::from_float(lsum > 0.f ? osum / lsum : 0.f);
-        }
-    }
+    MergeSmem ms{s_w, s_w + kMergeChunk * 8, s_red};
+    merge_slots<G, T, 4, false>(p.part_m, p.part_l, p.part_acc, s0, s1 - s0, p.Hq, qh0, ms, o, st);
 }
 
 // Merges n_parts blocks of combined states [n_parts][B][Hq][130] into the

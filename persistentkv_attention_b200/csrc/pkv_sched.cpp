@@ -30,26 +30,34 @@ double useful_kv_mb(const pkv_router_params* p, const int32_t* lengths, int n) {
     return bytes / (1024.0 * 1024.0);
 }
 
+long long tasks_for_quota(const int32_t* seq_lens, int B, int q) {
+    long long tasks = 0;
+    for (int r = 0; r < B; ++r) tasks += std::max(1, ceil_div(tiles_of(std::max(0, (int)seq_lens[r])), q));
+    return tasks;
+}
+
 int balanced_quota(const pkv_router_params* p, const int32_t* seq_lens, int B) {
-    // Smallest tile quota q such that sum_r ceil(tiles_r / q) tasks per KV
-    // head fit in the resident CTA slots (times tasks_per_cta).
-    long long total = 0;
-    for (int r = 0; r < B; ++r) total += tiles_of(std::max(0, (int)seq_lens[r]));
+    // Smallest tile quota q (>= min_tiles_per_task) whose tasks per KV head,
+    // sum_r ceil(tiles_r / q), fit in the resident CTA slots times
+    // tasks_per_cta; every row needs at least one task, so the target never
+    // drops below B.  tasks(q) is non-increasing in q: binary search.
+    int max_tiles = 1;
+    for (int r = 0; r < B; ++r) max_tiles = std::max(max_tiles, tiles_of(std::max(0, (int)seq_lens[r])));
     const int kvh = std::max(1, p->hkv);
     const long long slots = (long long)std::max(1, p->sm_count) * std::max(1, p->ctas_per_sm) *
                             std::max(1, p->tasks_per_cta);
-    const int target = (int)std::max(1ll, slots / kvh);
-    int q = std::max(std::max(1, p->min_tiles_per_task), ceil_div(std::max(1ll, total), target));
-    while (true) {
-        long long tasks = 0;
-        for (int r = 0; r < B; ++r) {
-            const int t = tiles_of(std::max(0, (int)seq_lens[r]));
-            tasks += std::max(1, ceil_div(t, q));
+    const long long target = std::max<long long>(B, std::max(1ll, slots / kvh));
+    int lo = std::max(1, p->min_tiles_per_task), hi = std::max(lo, max_tiles);
+    if (tasks_for_quota(seq_lens, B, lo) <= target) return lo;
+    while (lo < hi) {
+        const int mid = lo + (hi - lo) / 2;
+        if (tasks_for_quota(seq_lens, B, mid) <= target) {
+            hi = mid;
+        } else {
+            lo = mid + 1;
         }
-        if (tasks <= target || q >= (1 << 24)) break;
-        ++q;
     }
-    return q;
+    return lo;
 }
 
 }  // namespace
@@ -87,9 +95,9 @@ void pkv_router_params_b200(pkv_router_params* p) {
     p->supported_g = 0;         // every G in {1,2,4,8} runs the split routes
     p->min_split_len = 0;
     p->ctas_per_sm = 2;
-    p->tasks_per_cta = 1;
+    p->tasks_per_cta = 2;       // LPT-packed: about two tasks per resident CTA
     p->max_splits = 256;
-    p->min_tiles_per_task = 2;
+    p->min_tiles_per_task = 4;   // 128 tokens: 8 ring stages, two per consumer warp
 }
 
 int pkv_choose_workqueue_row_splits(const pkv_router_params* p, int length, int active_count,
@@ -282,12 +290,9 @@ pkv_status pkv_build_workqueue(const pkv_router_params* p, const int32_t* seq_le
         items += (long long)s * hkv;
     }
     *total_slots_out = split_offsets[B];
-    *num_items_out = (int)items;
-    if (work_items == nullptr || items > max_items) return PKV_ERR_CAPACITY;
 
-    // pass 2: items {row, kvh, split, tile_begin, tile_end}; reference order
-    // (row, split, kvh) for the reference and fixed policies, largest task
-    // first for the balanced policy (blocks are dispatched in index order).
+    // pass 2: items {row, kvh, split, tile_begin, tile_end} in the reference
+    // order (row, split, kvh).
     struct Task {
         int row, kvh, split, tb, te;
     };
@@ -302,18 +307,61 @@ pkv_status pkv_build_workqueue(const pkv_router_params* p, const int32_t* seq_le
             for (int h = 0; h < hkv; ++h) tasks.push_back({r, h, k, tb, te});
         }
     }
+    std::vector<Task> order;
     if (policy == PKV_SPLITS_BALANCED) {
+        // Longest-processing-time packing of the tasks onto the resident CTA
+        // slots, emitted in the kernel's grid-stride order (slot c runs items
+        // c, c + R, c + 2R, ...); short slots are padded with no-op items.
+        const int R = std::max(1, p->sm_count) * std::max(1, p->ctas_per_sm);
         std::stable_sort(tasks.begin(), tasks.end(), [](const Task& a, const Task& b) {
             return (a.te - a.tb) > (b.te - b.tb);
         });
+        if ((long long)tasks.size() <= R) {
+            order = tasks;
+        } else {
+            const long long kItemCost = 2;  // per-item overhead in tiles
+            std::vector<std::vector<int>> bins(R);
+            std::vector<long long> load(R, 0);
+            // min-heap on (load, slot)
+            std::vector<std::pair<long long, int>> heap;
+            heap.reserve(R);
+            for (int c = 0; c < R; ++c) heap.push_back({0, c});
+            auto cmp = [](const std::pair<long long, int>& a, const std::pair<long long, int>& b) {
+                return a > b;
+            };
+            std::make_heap(heap.begin(), heap.end(), cmp);
+            for (size_t i = 0; i < tasks.size(); ++i) {
+                std::pop_heap(heap.begin(), heap.end(), cmp);
+                auto& top = heap.back();
+                bins[top.second].push_back((int)i);
+                top.first += (tasks[i].te - tasks[i].tb) + kItemCost;
+                std::push_heap(heap.begin(), heap.end(), cmp);
+            }
+            size_t depth = 0;
+            for (const auto& b : bins) depth = std::max(depth, b.size());
+            order.reserve(depth * R);
+            for (size_t k = 0; k < depth; ++k) {
+                for (int c = 0; c < R; ++c) {
+                    if (k < bins[c].size()) {
+                        order.push_back(tasks[bins[c][k]]);
+                    } else {
+                        order.push_back({-1, -1, 0, 0, 0});  // no-op padding
+                    }
+                }
+            }
+        }
+    } else {
+        order = tasks;
     }
-    for (size_t i = 0; i < tasks.size(); ++i) {
+    *num_items_out = (int)order.size();
+    if (work_items == nullptr || (long long)order.size() > max_items) return PKV_ERR_CAPACITY;
+    for (size_t i = 0; i < order.size(); ++i) {
         int32_t* w = work_items + 5 * i;
-        w[0] = tasks[i].row;
-        w[1] = tasks[i].kvh;
-        w[2] = tasks[i].split;
-        w[3] = tasks[i].tb;
-        w[4] = tasks[i].te;
+        w[0] = order[i].row;
+        w[1] = order[i].kvh;
+        w[2] = order[i].split;
+        w[3] = order[i].tb;
+        w[4] = order[i].te;
     }
     return PKV_OK;
 }

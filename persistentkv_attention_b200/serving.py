@@ -1,0 +1,198 @@
+"""Decode-step runtime around the kernels: step plans, CUDA graphs, host I/O.
+
+The reference's serving harness compiles per-step metadata in Python
+(``compile_persistentkv_metadata``, tests/benchmark_serving_trace.py:655-729),
+copies it to the GPU with ``torch.tensor(..., device="cuda")`` and optionally
+captures each step in a CUDA graph (:1439-1452).  ``DecodeEngine`` does the
+same jobs for this engine:
+
+* ``plan_step``  -- host metadata of one step (block table padded like the
+  reference, seq_lens, request-id q indices, dense out indices, and the
+  C++-built work queue) in one pinned int32 staging buffer;
+* ``upload``     -- one host-to-device copy of that buffer into a
+  device-resident ``StepPlan``;
+* ``run``        -- one work-queue decode call (fused merge by default);
+* ``capture``    -- a CUDA graph of ``run`` for replay;
+* ``step_host``  -- the end-to-end call a server makes: plan on the host,
+  copy q rows and metadata from pinned host memory, decode, copy the output
+  back to pinned host memory.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import ops
+from .scheduler import Router
+
+HEAD_DIM = 128
+
+
+@dataclass
+class HostPlan:
+    buf: torch.Tensor          # pinned int32 staging buffer
+    batch: int
+    max_pages: int
+    num_items: int
+    total_slots: int
+    bucket: int
+    tokens: int                # sum of seq_lens
+
+    def views(self, t: torch.Tensor):
+        """Splits a (host or device) copy of the buffer into its fields."""
+        b, mp, n = self.batch, self.max_pages, self.num_items
+        o = 0
+        out = {}
+        for name, size in (("block_table", b * mp), ("seq_lens", b), ("q_indices", b),
+                           ("out_indices", b), ("split_offsets", b + 1), ("work_items", 5 * n)):
+            out[name] = t[o:o + size]
+            o += size
+        out["block_table"] = out["block_table"].view(b, mp)
+        out["work_items"] = out["work_items"].view(n, 5)
+        return out
+
+    @property
+    def nbytes(self) -> int:
+        return int(self.buf.numel() * 4)
+
+
+@dataclass
+class StepPlan:
+    """Device-resident metadata of one decode step."""
+
+    host: HostPlan
+    dev: torch.Tensor
+    fields: dict
+
+    @property
+    def batch(self) -> int:
+        return self.host.batch
+
+
+def _staging_size(batch: int, max_pages: int, items: int) -> int:
+    return batch * max_pages + 4 * batch + 1 + 5 * items
+
+
+class DecodeEngine:
+    """Work-queue decode over one paged K/V pool on the current device."""
+
+    def __init__(self, k_pages: torch.Tensor, v_pages: torch.Tensor, hq: int,
+                 router: Router | None = None, policy: str = "balanced", fused: bool = True,
+                 requested_splits: int = 0):
+        self.k_pages = k_pages
+        self.v_pages = v_pages
+        self.hq = hq
+        self.hkv = k_pages.shape[1]
+        self.page_size = k_pages.shape[2]
+        self.dtype = k_pages.dtype
+        self.device = k_pages.device
+        if router is None:
+            sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+            router = Router.b200(hq=hq, hkv=self.hkv, sm_count=sms)
+        self.router = router
+        self.policy = policy
+        self.fused = fused
+        self.requested_splits = requested_splits
+        self._workspace = torch.empty(0, device=self.device, dtype=torch.float32)
+        self._counters = torch.zeros(0, device=self.device, dtype=torch.int32)
+
+    # ---------------------------------------------------------------- planning
+    def plan_step(self, seq_lens, block_rows: np.ndarray, q_indices=None,
+                  out: torch.Tensor | None = None) -> HostPlan:
+        """Host metadata of one step into a pinned buffer (``out`` reuses one)."""
+        seq = np.asarray(seq_lens, dtype=np.int32)
+        b = seq.size
+        queue = self.router.build_workqueue(seq, b, self.policy, self.requested_splits)
+        mp = block_rows.shape[1]
+        size = _staging_size(b, mp, queue.num_items)
+        if out is None or out.numel() < size:
+            out = torch.empty(size, dtype=torch.int32, pin_memory=True)
+        buf = out[:size]
+        plan = HostPlan(buf, b, mp, queue.num_items, queue.total_slots, int(seq.max(initial=1)),
+                        int(seq.sum()))
+        v = plan.views(buf)
+        v["block_table"].numpy()[:] = block_rows
+        v["seq_lens"].numpy()[:] = seq
+        v["q_indices"].numpy()[:] = np.arange(b) if q_indices is None else q_indices
+        v["out_indices"].numpy()[:] = np.arange(b)
+        v["split_offsets"].numpy()[:] = queue.split_offsets
+        v["work_items"].numpy()[:] = queue.work_items
+        return plan
+
+    def plan_from_trace(self, requests, state) -> HostPlan:
+        """Plan of one reference-style trace step (q rows indexed by request id)."""
+        by_id = {r.request_id: r for r in requests}
+        page_count = math.ceil(max(state.lengths) / self.page_size)
+        rows = np.empty((len(state.active_ids), page_count), dtype=np.int32)
+        for i, rid in enumerate(state.active_ids):
+            pages = by_id[rid].physical_pages[:page_count]
+            if len(pages) < page_count:
+                pages = pages + (by_id[rid].physical_pages[-1],) * (page_count - len(pages))
+            rows[i] = pages
+        return self.plan_step(state.lengths, rows, q_indices=np.asarray(state.active_ids))
+
+    def upload(self, plan: HostPlan, dev_buf: torch.Tensor | None = None,
+               non_blocking: bool = False) -> StepPlan:
+        if dev_buf is None or dev_buf.numel() < plan.buf.numel():
+            dev_buf = torch.empty(plan.buf.numel(), dtype=torch.int32, device=self.device)
+        dev = dev_buf[: plan.buf.numel()]
+        dev.copy_(plan.buf, non_blocking=non_blocking)
+        self.reserve(plan.batch, plan.total_slots)
+        return StepPlan(plan, dev, plan.views(dev))
+
+    def reserve(self, batch: int, total_slots: int) -> None:
+        """Grows the shared workspace / merge counters (never inside a capture)."""
+        need = ops.workqueue_workspace_bytes(total_slots, self.hq) // 4
+        if self._workspace.numel() < need:
+            self._workspace = torch.empty(need, device=self.device, dtype=torch.float32)
+        if self._counters.numel() < batch * self.hkv:
+            self._counters = torch.zeros(batch * self.hkv, device=self.device, dtype=torch.int32)
+
+    # ---------------------------------------------------------------- execution
+    def run(self, plan: StepPlan, q_source: torch.Tensor, out: torch.Tensor) -> None:
+        f = plan.fields
+        counters = self._counters[: plan.batch * self.hkv].view(plan.batch, self.hkv)
+        ops.paged_attention_workqueue(
+            q_source, self.k_pages, self.v_pages, f["block_table"], f["seq_lens"],
+            f["work_items"], f["split_offsets"], counters, f["q_indices"], f["out_indices"], out,
+            self._workspace, plan.host.bucket, self.page_size, plan.host.total_slots, self.fused)
+
+    def capture(self, plan: StepPlan, q_source: torch.Tensor, out: torch.Tensor,
+                stream: torch.cuda.Stream | None = None) -> torch.cuda.CUDAGraph:
+        self.run(plan, q_source, out)          # first call outside capture (attributes, maps)
+        graph = torch.cuda.CUDAGraph()
+        stream = stream or torch.cuda.Stream(self.device)
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(graph, stream=stream):
+                self.run(plan, q_source, out)
+        return graph
+
+    def step_host(self, seq_lens, block_rows: np.ndarray, q_host: torch.Tensor,
+                  out_host: torch.Tensor, scratch: dict) -> tuple[int, int]:
+        """End-to-end step from pinned host buffers; returns (h2d_bytes, d2h_bytes).
+
+        ``q_host`` [B, Hq, 128] and ``out_host`` are pinned host tensors;
+        ``scratch`` keeps the pinned staging and device buffers between calls.
+        """
+        plan = self.plan_step(seq_lens, block_rows, out=scratch.get("stage"))
+        scratch["stage"] = plan.buf if scratch.get("stage") is None or \
+            scratch["stage"].numel() < plan.buf.numel() else scratch["stage"]
+        step = self.upload(plan, scratch.get("meta"), non_blocking=True)
+        scratch["meta"] = step.dev if scratch.get("meta") is None or \
+            scratch["meta"].numel() < step.dev.numel() else scratch["meta"]
+        b = plan.batch
+        q_dev = scratch.get("q")
+        if q_dev is None or q_dev.shape[0] < b:
+            q_dev = scratch["q"] = torch.empty(max(b, q_host.shape[0]), self.hq, HEAD_DIM,
+                                               dtype=self.dtype, device=self.device)
+            scratch["o"] = torch.empty_like(q_dev)
+        q_dev[:b].copy_(q_host[:b], non_blocking=True)
+        self.run(step, q_dev[:b], scratch["o"][:b])
+        out_host[:b].copy_(scratch["o"][:b], non_blocking=True)
+        h2d = plan.nbytes + b * self.hq * HEAD_DIM * q_host.element_size()
+        d2h = b * self.hq * HEAD_DIM * out_host.element_size()
+        return h2d, d2h
