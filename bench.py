@@ -12,8 +12,9 @@ the tokens of all ranks over the slowest rank's device time.
 
 Reported (one JSON line on rank 0):
   value       tokens/s with all inputs resident in HBM, per-step CUDA-event
-              intervals around graph-replayed decode steps, L2 flushed
-              (256 MiB write) before every step outside the intervals;
+              intervals around graph-replayed decode steps; before every step,
+              outside the intervals, L2 is flushed by a 256 MiB write and a
+              256 MiB read (so no dirty lines are left for the timed step);
   e2e         tokens/s through the public operator API from pinned host
               buffers: host work-queue build, H2D of q rows + metadata,
               decode, D2H of the output, per step;
@@ -73,59 +74,92 @@ def measured_peak_gbs() -> tuple[float, str]:
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons sampled during the timed region.
+
+    Polls NVML from a background thread (the timed region lasts milliseconds,
+    far shorter than nvidia-smi's sampling period); only samples taken
+    between ``__enter__`` and ``__exit__`` count."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
     def __init__(self, device: int):
-        self.proc = None
         self.device = device
+        self.samples: list[tuple[float, int]] = []
+        self.error = None
+        self.handle = None
+        self.max_mhz = None
+        try:
+            import pynvml
+
+            self.nvml = pynvml
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(device)
+            bus = (f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:"
+                   f"{props.pci_device_id:02X}.0")
+            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # no NVML: the line reports why
+            self.error = f"{type(exc).__name__}: {exc}"
+
+    def _poll(self):
+        nv = self.nvml
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                try:
+                    reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                except AttributeError:
+                    reasons = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.handle)
+                self.samples.append((float(mhz), int(reasons)))
+            except Exception as exc:
+                self.error = f"{type(exc).__name__}: {exc}"
+                return
+            self._stop.wait(0.0005)
 
     def __enter__(self):
-        try:
-            props = torch.cuda.get_device_properties(self.device)
-            try:
-                sel = (f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:"
-                       f"{props.pci_device_id:02X}.0")
-            except AttributeError:
-                visible = os.environ.get("CUDA_VISIBLE_DEVICES")
-                sel = visible.split(",")[self.device] if visible else str(self.device)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", sel, f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except Exception:
-            self.proc = None
+        import threading
+
+        self._stop = threading.Event()
+        self._thread = None
+        if self.handle is not None:
+            self._thread = threading.Thread(target=self._poll, daemon=True)
+            self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except Exception:
-                self.proc.kill()
-                out = ""
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
 
     def summary(self):
-        rows = []
-        for ln in getattr(self, "lines", []):
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 8:
-                continue
-            try:
-                rows.append((float(parts[0]), float(parts[1]), parts[3:]))
-            except ValueError:
-                continue
-        if not rows:
-            return None
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({n for _, _, p in rows for n, v in zip(names, p[1:]) if v == "Active"})
-        return {"sm_mhz": statistics.median(r[0] for r in rows),
-                "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
-                "samples": len(rows)}
+        if not self.samples:
+            return {"error": self.error or "no samples"}
+        mask = 0
+        for _, r in self.samples:
+            mask |= r
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "samples": len(self.samples),
+                "reasons": [name for bit, name in self.REASONS.items() if mask & bit],
+                "source": "NVML, polled during the timed region"}
+
+
+class L2Flush:
+    """Evicts L2 between timed steps without leaving dirty lines behind.
+
+    Writing a buffer larger than L2 evicts everything but leaves up to a full
+    L2 of dirty lines, whose write-back would then be charged to the next
+    timed kernel; reading a second buffer larger than L2 afterwards forces
+    those write-backs here and leaves L2 holding clean, unrelated lines."""
+
+    def __init__(self, dev):
+        self.wbuf = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        self.rbuf = torch.ones(FLUSH_BYTES // 8, dtype=torch.int64, device=dev)
+        self.acc = torch.empty((), dtype=torch.int64, device=dev)
+
+    def __call__(self, i: int) -> None:
+        self.wbuf.fill_(i & 0xFF)
+        torch.sum(self.rbuf, dim=0, out=self.acc)
 
 
 # ------------------------------------------------------------------ workload
@@ -247,7 +281,7 @@ def run_engine_arm(args) -> None:
     v_pages = torch.randn(physical, hkv, PAGE, D, generator=gen, device=dev).half()
     q_pool = torch.randn(w["requests"], HQ, D, generator=gen, device=dev).half()
     engine = DecodeEngine(k_pages, v_pages, HQ, fused=not args.no_fused)
-    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
     stream = torch.cuda.Stream(dev)
 
     # device-resident plans + one CUDA graph per distinct step
@@ -272,14 +306,14 @@ def run_engine_arm(args) -> None:
           for _ in range(args.steps)]
     with torch.cuda.stream(stream):
         for j in sched[: args.warmup]:
-            flush.fill_(1)
+            flush(j)
             graphs[j].replay()
     barrier()
     with ClockSampler(local) as clocks:
         with torch.cuda.stream(stream):
             torch.cuda._sleep(2_000_000)          # lets the host queue run ahead
             for i, j in enumerate(sched[args.warmup:]):
-                flush.fill_(i & 0xFF)
+                flush(i)
                 ev[i][0].record(stream)
                 graphs[j].replay()
                 ev[i][1].record(stream)
@@ -333,7 +367,7 @@ def run_engine_arm(args) -> None:
         barrier()
         for i, j in enumerate(sched[args.warmup:]):
             lens, rows, qh = host_rows[j]
-            flush.fill_(i & 0xFF)
+            flush(i)
             stream.synchronize()
             e2e_ev[i][0].record(stream)
             h, d = engine.step_host(lens, rows, qh, out_host, scratch)
@@ -378,7 +412,8 @@ def run_engine_arm(args) -> None:
             "workload": f"{args.workload}: {w['desc']}", "hq": HQ, "hkv": hkv, "head_dim": D,
             "page_size": PAGE, "active_per_gpu": w["max_active"],
             "parallelism": f"batch-partitioned x{world} (independent batch per GPU)",
-            "l2": "flushed (256 MiB write) before every step, outside the timed intervals",
+            "l2": "flushed before every step outside the timed intervals: 256 MiB write, "
+                  "then 256 MiB read (no dirty lines left for the timed step)",
             "merge": "fused last-task merge" if not args.no_fused else "PDL merge kernel",
             "split_policy": "balanced (C++ builder)",
         },

@@ -25,7 +25,11 @@ namespace {
 #ifndef PKV_RING_SLOTS
 #define PKV_RING_SLOTS 8
 #endif
+#ifndef PKV_LOAD_MODE
+#define PKV_LOAD_MODE 1
+#endif
 constexpr int kSlots = PKV_RING_SLOTS;          // ring depth (8 KB per slot)
+constexpr int kLoadMode = PKV_LOAD_MODE;        // kLoadCpAsync or kLoadTma
 constexpr int kCtasPerSm = PKV_MIN_CTAS_PER_SM;  // resident decode CTAs per SM
 constexpr int kMaxDevices = 64;
 
@@ -211,8 +215,8 @@ pkv_status check_common(const Common& c) {
     }
     if ((reinterpret_cast<uintptr_t>(c.k) & 15u) || (reinterpret_cast<uintptr_t>(c.v) & 15u))
         return fail(PKV_ERR_MISALIGNED, "k_pages and v_pages must be 16-byte aligned");
-    if (reinterpret_cast<uintptr_t>(c.q) & 3u)
-        return fail(PKV_ERR_MISALIGNED, "q must be 4-byte aligned");
+    if (reinterpret_cast<uintptr_t>(c.q) & 15u)
+        return fail(PKV_ERR_MISALIGNED, "q must be 16-byte aligned");
     return PKV_OK;
 }
 
@@ -233,7 +237,7 @@ struct LaunchSpec {
 template <int G, typename T, int BR>
 pkv_status launch_typed(const LaunchSpec& ls, const CUtensorMap& tk, const CUtensorMap& tv,
                         cudaStream_t stream, DeviceState* ds) {
-    auto kern = pkv_decode_kernel<G, T, BR, kSlots>;
+    auto kern = pkv_decode_kernel<G, T, BR, kSlots, kLoadMode>;
     const size_t smem = decode_smem_bytes<G, kSlots>();
     static std::atomic<unsigned long long> attr_done{0ull};
     int dev = 0;
@@ -332,6 +336,8 @@ void fill_common(LaunchSpec& ls, const Common& c) {
     ls.dp.page_size = c.page_size;
     ls.dp.max_pages = c.max_pages;
     ls.dp.scale_log2 = (1.0f / sqrtf((float)kHeadDim)) * kLog2e;
+    ls.dp.k_pages = static_cast<const uint8_t*>(c.k);
+    ls.dp.v_pages = static_cast<const uint8_t*>(c.v);
     ls.G = c.Hq / c.Hkv;
     ls.box_rows = box_rows_for(c.page_size);
     ls.dtype = c.dtype;

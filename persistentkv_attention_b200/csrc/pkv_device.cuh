@@ -141,6 +141,27 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
         : "memory");
 }
 
+// 16-byte cp.async global -> shared (L2 only); bytes beyond src_bytes (0 or
+// 16) are zero-filled, so a masked chunk reads nothing.
+__device__ __forceinline__ void cp_async_16(uint32_t smem_dst, const void* src, uint32_t src_bytes,
+                                            uint64_t policy) {
+    asm volatile(
+        "cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;" ::"r"(smem_dst),
+        "l"(src), "r"(src_bytes), "l"(policy)
+        : "memory");
+}
+
+// Arrives on `bar` once all prior cp.async of this thread have completed
+// (the barrier's expected count includes this arrival).
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- PDL
 __device__ __forceinline__ void griddep_wait() {
     asm volatile("griddepcontrol.wait;" ::: "memory");

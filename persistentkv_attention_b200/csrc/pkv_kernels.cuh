@@ -40,6 +40,8 @@ struct DecodeParams {
     float* part_m;                 // [slots * Hq]
     float* part_l;                 // [slots * Hq]
     float* part_acc;               // [slots * Hq * 128]
+    const uint8_t* k_pages;        // pool bases (cp.async load path)
+    const uint8_t* v_pages;
     unsigned* error;               // device error word
     int B, q_rows, out_rows, Hq, Hkv;
     int num_pages, page_size, max_pages;
@@ -293,16 +295,62 @@ struct DecodeSmem {
     static constexpr int kMergeFloats = kConsumerWarps * G * kMergeStride;
 };
 
+// Work-item descriptors travel from the producer to the consumers through a
+// small shared-memory ring, together with the item's G query rows, so the
+// consumer warps never touch global memory for metadata.
+constexpr int kDescSlots = 4;
+constexpr int kQSlotBytes = 8 * kHeadDim * 2;  // up to 8 query heads of 128 x 16-bit
+
+struct ItemDesc {
+    int row, kvh, split, tok_begin, tok_end, slot, row_splits, q_row, out_row, noop;
+    int pad[6];
+};
+
 template <int G, int NSLOTS>
 constexpr size_t decode_smem_bytes() {
     return 1024 /* alignment slack */ + (size_t)NSLOTS * kSlotBytes +
-           2 * NSLOTS * sizeof(uint64_t) + 64 +
+           (size_t)kDescSlots * kQSlotBytes + kDescSlots * sizeof(ItemDesc) +
+           (2 * NSLOTS + 2 * kDescSlots) * sizeof(uint64_t) + 64 +
            2 * 2 * kConsumerWarps * 8 * sizeof(float) +
            2 * DecodeSmem<G>::kMergeFloats * sizeof(float) +
            merge_scratch_floats<kConsumerWarps>() * sizeof(float);
 }
 
-template <int G, typename T, int BOX_ROWS, int NSLOTS>
+// How the producer warp moves K/V pages into the ring.
+constexpr int kLoadTma = 0;      // cp.async.bulk.tensor boxes, one issuing lane
+constexpr int kLoadCpAsync = 1;  // 16-byte cp.async from all 32 lanes, zero-filled tails
+
+// Producer view of an item: the descriptor plus this lane's page id for box
+// `lane` of the item's first batch of 32 boxes.  On the work-queue route the
+// block-table read is issued from the work item alone, in parallel with the
+// seq_lens / split_offsets / index reads.
+template <int BOX_ROWS>
+__device__ __forceinline__ Item producer_item(const DecodeParams& p, int index, int lane,
+                                              int& pid0) {
+    pid0 = -1;
+    int spec = -1;
+    if (p.work_items != nullptr) {
+        const int32_t* w = p.work_items + (size_t)index * 5;
+        const int row = __ldg(w + 0);
+        const int tb = __ldg(w + 3);
+        const int te = __ldg(w + 4);
+        const long long tok = (long long)tb * kTileTokens + (long long)lane * BOX_ROWS;
+        if (row >= 0 && row < p.B && tb >= 0 && tok < (long long)te * kTileTokens &&
+            tok < (long long)p.max_pages * p.page_size) {
+            spec = __ldg(p.block_table + (size_t)row * p.max_pages + (int)(tok / p.page_size));
+        }
+    }
+    const Item it = load_item(p, index, lane == 0);  // the producer reports bad items
+    const int tok = it.tok_begin + lane * BOX_ROWS;
+    if (!it.noop && tok < it.tok_end) {
+        pid0 = p.work_items != nullptr
+                   ? spec
+                   : __ldg(p.block_table + (size_t)it.row * p.max_pages + tok / p.page_size);
+    }
+    return it;
+}
+
+template <int G, typename T, int BOX_ROWS, int NSLOTS, int LOAD>
 __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     pkv_decode_kernel(const __grid_constant__ DecodeParams p,
                       const __grid_constant__ CUtensorMap tmap_k,
@@ -318,22 +366,33 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     const uint32_t raw_u32 = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
     uint8_t* ring = smem;
-    uint64_t* full_bar = reinterpret_cast<uint64_t*>(ring + (size_t)NSLOTS * kSlotBytes);
+    uint8_t* s_q = ring + (size_t)NSLOTS * kSlotBytes;                    // [kDescSlots][8][128]
+    ItemDesc* s_desc = reinterpret_cast<ItemDesc*>(s_q + kDescSlots * kQSlotBytes);
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(s_desc + kDescSlots);
     uint64_t* empty_bar = full_bar + NSLOTS;
-    volatile int* s_flags = reinterpret_cast<volatile int*>(empty_bar + NSLOTS);  // [0]=abort [1]=last
-    float* s_mstat = reinterpret_cast<float*>(smem + (size_t)NSLOTS * kSlotBytes +
-                                              2 * NSLOTS * sizeof(uint64_t) + 64);
+    uint64_t* desc_full = empty_bar + NSLOTS;
+    uint64_t* desc_empty = desc_full + kDescSlots;
+    uint8_t* s_flag_bytes = reinterpret_cast<uint8_t*>(desc_empty + kDescSlots);
+    volatile int* s_flags = reinterpret_cast<volatile int*>(s_flag_bytes);  // [0] abort, [1] last
+    float* s_mstat = reinterpret_cast<float*>(s_flag_bytes + 64);
     float* s_lstat = s_mstat + 2 * kConsumerWarps * 8;
     float* s_merge = s_lstat + 2 * kConsumerWarps * 8;
     float* s_mw = s_merge + 2 * DecodeSmem<G>::kMergeFloats;  // merge weights + stats
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const int my_items = (int)blockIdx.x < p.num_items
+                             ? (p.num_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
+                             : 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NSLOTS; ++s) {
-            mbar_init(&full_bar[s], 1);
+            mbar_init(&full_bar[s], LOAD == kLoadTma ? 1 : 32);
             mbar_init(&empty_bar[s], 1);
+        }
+        for (int s = 0; s < kDescSlots; ++s) {
+            mbar_init(&desc_full[s], 33);  // 32 lanes' Q copies + the descriptor store
+            mbar_init(&desc_empty[s], kConsumerWarps);
         }
         s_flags[0] = 0;
         s_flags[1] = 0;
@@ -343,17 +402,72 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
 
     if (warp == kConsumerWarps) {
         // ============================ producer warp ============================
-        if (lane == 0) {
+        if (LOAD == kLoadTma && lane == 0) {
             tma_prefetch_map(&tmap_k);
             tma_prefetch_map(&tmap_v);
         }
         const uint64_t policy = l2_evict_first_policy();
+        // cp.async path: lane copies 16-byte chunk pc of half ph of tokens
+        // pt0, pt0 + 2, ..., pt0 + 14 of every stage, for K and for V
+        const int ph = (lane >> 3) & 1;
+        const int pc = lane & 7;
+        const int pt0 = lane >> 4;
+        const uint32_t ring_base = smem_u32(ring);
+        const uint32_t q_base = smem_u32(s_q);
         uint32_t gstage = 0;
         bool aborted = false;
-        for (int index = blockIdx.x; index < p.num_items && !aborted; index += gridDim.x) {
-            if (index + (int)gridDim.x >= p.num_items) griddep_launch_dependents();
-            const Item it = load_item(p, index, false);
-            const int n_stages = ceil_div_i(it.tok_end - it.tok_begin, kStageTokens);
+        int pid0 = -1;
+        Item cur;
+        if (my_items > 0) cur = producer_item<BOX_ROWS>(p, blockIdx.x, lane, pid0);
+        for (int s = 0; s < my_items && !aborted; ++s) {
+            const int index = (int)blockIdx.x + s * (int)gridDim.x;
+            if (s == my_items - 1) griddep_launch_dependents();
+
+            // ---- publish the descriptor and the G query rows of this item
+            const int e = s % kDescSlots;
+            if (s >= kDescSlots) {
+                bool waited = true;
+                if (lane == 0)
+                    waited = mbar_wait_bounded(&desc_empty[e], ((s / kDescSlots) - 1) & 1, s_flags);
+                waited = __shfl_sync(0xffffffffu, waited, 0) && s_flags[0] == 0;
+                if (!waited) {
+                    if (lane == 0) {
+                        s_flags[0] = 1;
+                        raise_error(p.error, kErrTimeout);
+                    }
+                    aborted = true;
+                    break;
+                }
+            }
+            {
+                const bool qok = !cur.noop && cur.q_row >= 0;
+                const uint8_t* qsrc = reinterpret_cast<const uint8_t*>(p.q) +
+                                      ((size_t)(qok ? cur.q_row : 0) * p.Hq + (size_t)cur.kvh * G) *
+                                          kRowBytes;
+#pragma unroll
+                for (int c = lane; c < G * 16; c += 32) {
+                    cp_async_16(q_base + e * kQSlotBytes + c * 16, qsrc + c * 16, qok ? 16u : 0u,
+                                policy);
+                }
+                cp_async_mbar_arrive_noinc(&desc_full[e]);
+                if (lane == 0) {
+                    ItemDesc& d = s_desc[e];
+                    d.row = cur.row;
+                    d.kvh = cur.kvh;
+                    d.split = cur.split;
+                    d.tok_begin = cur.tok_begin;
+                    d.tok_end = cur.tok_end;
+                    d.slot = cur.slot;
+                    d.row_splits = cur.row_splits;
+                    d.q_row = cur.q_row;
+                    d.out_row = cur.out_row;
+                    d.noop = cur.noop ? 1 : 0;
+                    mbar_arrive(&desc_full[e]);
+                }
+            }
+
+            const Item it = cur;
+            const int n_stages = it.noop ? 0 : ceil_div_i(it.tok_end - it.tok_begin, kStageTokens);
             const int n_boxes = n_stages * kBoxesPerStage;
             const int32_t* bt_row = p.block_table + (size_t)it.row * p.max_pages;
             auto fetch_page = [&](int box) -> int {
@@ -361,7 +475,12 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                 if (box >= n_boxes || tok >= it.tok_end) return -1;
                 return __ldg(bt_row + tok / p.page_size);
             };
-            int pid_next = fetch_page(lane);
+            // next item: metadata + first page ids, fetched while this one streams
+            const bool has_next = s + 1 < my_items;
+            bool fetched = !has_next;
+            Item nxt = it;
+            int nxt_pid0 = -1;
+            int pid_next = pid0;
             for (int base = 0; base < n_boxes && !aborted; base += 32) {
                 const int box = base + lane;
                 const int tok = it.tok_begin + box * BOX_ROWS;
@@ -396,28 +515,59 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                             break;
                         }
                     }
-                    const bool mine = ok && (lane / kBoxesPerStage) == st;
-                    const unsigned mask = __ballot_sync(0xffffffffu, mine);
-                    if (lane == 0) {
-                        mbar_arrive_expect_tx(&full_bar[slot],
-                                              (uint32_t)__popc(mask) * 4u * kBoxBytes);
-                    }
-                    __syncwarp();
-                    if (mine) {
-                        uint8_t* dst = ring + (size_t)slot * kSlotBytes +
-                                       (lane % kBoxesPerStage) * kBoxBytes;
-                        const int half = kStageTokens * kHalfRowBytes;
-                        tma_load_2d(dst, &tmap_k, 0, y, &full_bar[slot], policy);
-                        tma_load_2d(dst + half, &tmap_k, 64, y, &full_bar[slot], policy);
-                        tma_load_2d(dst + 2 * half, &tmap_v, 0, y, &full_bar[slot], policy);
-                        tma_load_2d(dst + 3 * half, &tmap_v, 64, y, &full_bar[slot], policy);
+                    if constexpr (LOAD == kLoadTma) {
+                        const bool mine = ok && (lane / kBoxesPerStage) == st;
+                        const unsigned mask = __ballot_sync(0xffffffffu, mine);
+                        if (lane == 0) {
+                            mbar_arrive_expect_tx(&full_bar[slot],
+                                                  (uint32_t)__popc(mask) * 4u * kBoxBytes);
+                        }
+                        __syncwarp();
+                        if (mine) {
+                            uint8_t* dst = ring + (size_t)slot * kSlotBytes +
+                                           (lane % kBoxesPerStage) * kBoxBytes;
+                            const int half = kStageTokens * kHalfRowBytes;
+                            tma_load_2d(dst, &tmap_k, 0, y, &full_bar[slot], policy);
+                            tma_load_2d(dst + half, &tmap_k, 64, y, &full_bar[slot], policy);
+                            tma_load_2d(dst + 2 * half, &tmap_v, 0, y, &full_bar[slot], policy);
+                            tma_load_2d(dst + 3 * half, &tmap_v, 64, y, &full_bar[slot], policy);
+                        }
+                    } else {
+                        // page rows of the stage's boxes, from the lanes that resolved them
+                        const int ya = __shfl_sync(0xffffffffu, y, st * kBoxesPerStage);
+                        const bool oka = __shfl_sync(0xffffffffu, ok, st * kBoxesPerStage);
+                        const int yb = __shfl_sync(0xffffffffu, y, st * kBoxesPerStage + kBoxesPerStage - 1);
+                        const bool okb = __shfl_sync(0xffffffffu, ok, st * kBoxesPerStage + kBoxesPerStage - 1);
+                        const int t0 = it.tok_begin + (base / kBoxesPerStage + st) * kStageTokens;
+                        const uint32_t sdst = ring_base + slot * kSlotBytes + ph * (kStageTokens * kHalfRowBytes);
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            const int t = pt0 + 2 * k;
+                            const bool second = BOX_ROWS == 8 && t >= 8;
+                            const bool valid = (second ? okb : oka) && t0 + t < it.tok_end;
+                            const size_t row = valid ? (size_t)((second ? yb : ya) + (t & (BOX_ROWS - 1))) : 0;
+                            const size_t off = row * kRowBytes + ph * kHalfRowBytes + pc * 16;
+                            const uint32_t dst = sdst + t * kHalfRowBytes + ((pc ^ (t & 7)) << 4);
+                            const uint32_t nbytes = valid ? 16u : 0u;
+                            cp_async_16(dst, p.k_pages + off, nbytes, policy);
+                            cp_async_16(dst + 2 * kStageTokens * kHalfRowBytes, p.v_pages + off, nbytes, policy);
+                        }
+                        cp_async_mbar_arrive_noinc(&full_bar[slot]);
                     }
                     ++gstage;
                 }
+                if (!fetched) {
+                    fetched = true;
+                    nxt = producer_item<BOX_ROWS>(p, index + (int)gridDim.x, lane, nxt_pid0);
+                }
             }
+            if (!fetched) nxt = producer_item<BOX_ROWS>(p, index + (int)gridDim.x, lane, nxt_pid0);
+            cur = nxt;
+            pid0 = nxt_pid0;
         }
-        // Drain: the last NSLOTS issued stages may still be landing.
-        if (lane == 0) {
+        // Drain: every copy this warp issued must land before the CTA exits.
+        if constexpr (LOAD == kLoadCpAsync) cp_async_wait_all();
+        if (LOAD == kLoadTma && lane == 0) {
             const uint32_t first = gstage > (uint32_t)NSLOTS ? gstage - NSLOTS : 0u;
             for (uint32_t g = first; g < gstage; ++g) {
                 if (!mbar_wait_bounded(&full_bar[g % NSLOTS], (g / NSLOTS) & 1u, nullptr)) {
@@ -442,26 +592,57 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     int buf = 0;
     bool aborted = false;
 
-    for (int index = blockIdx.x; index < p.num_items; index += gridDim.x) {
-        if (index + (int)gridDim.x >= p.num_items) griddep_launch_dependents();
-        const Item it = load_item(p, index, threadIdx.x == 0);
-        if (it.noop) continue;
-        const int n_stages = ceil_div_i(it.tok_end - it.tok_begin, kStageTokens);
-
-        // Q^T as the B operand: lane holds Q[head tq][16 ks + tc (+8) .. +1].
+    for (int s = 0; s < my_items; ++s) {
+        if (s == my_items - 1) griddep_launch_dependents();
+        const int e = s % kDescSlots;
+        Item it;
+        it.noop = true;
+        it.tok_begin = it.tok_end = 0;
+        it.row = it.kvh = it.split = 0;
+        it.slot = -1;
+        it.row_splits = 2;
+        it.q_row = it.out_row = -1;
         uint32_t qf[8][2];
-        if (tq < G && it.q_row >= 0) {
-            const T* qrow = reinterpret_cast<const T*>(p.q) +
-                            ((size_t)it.q_row * p.Hq + (size_t)it.kvh * G + tq) * kHeadDim;
+        if (!aborted) {
+            bool ok = mbar_wait_bounded(&desc_full[e], (s / kDescSlots) & 1, s_flags);
+            ok = __all_sync(0xffffffffu, ok) && s_flags[0] == 0;
+            if (!ok) {
+                if (lane == 0) {
+                    s_flags[0] = 1;
+                    raise_error(p.error, kErrTimeout);
+                }
+                aborted = true;
+            }
+        }
+        if (!aborted) {
+            const ItemDesc& d = s_desc[e];
+            it.row = d.row;
+            it.kvh = d.kvh;
+            it.split = d.split;
+            it.tok_begin = d.tok_begin;
+            it.tok_end = d.tok_end;
+            it.slot = d.slot;
+            it.row_splits = d.row_splits;
+            it.q_row = d.q_row;
+            it.out_row = d.out_row;
+            it.noop = d.noop != 0;
+            // Q^T as the B operand: lane holds Q[head tq][16 ks + tc (+8) .. +1]
+            // (zeros beyond the G heads and for an invalid q row)
+            const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+                s_q + e * kQSlotBytes + (tq < G ? tq : 0) * kRowBytes);
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
-                qf[ks][0] = __ldg(reinterpret_cast<const unsigned int*>(qrow + 16 * ks + tc));
-                qf[ks][1] = __ldg(reinterpret_cast<const unsigned int*>(qrow + 16 * ks + 8 + tc));
+                qf[ks][0] = tq < G ? qrow[(16 * ks + tc) / 2] : 0u;
+                qf[ks][1] = tq < G ? qrow[(16 * ks + 8 + tc) / 2] : 0u;
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&desc_empty[e]);
         } else {
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) qf[ks][0] = qf[ks][1] = 0u;
         }
+        if (it.noop && !aborted) continue;
+        const int n_stages = aborted ? 0 : ceil_div_i(it.tok_end - it.tok_begin, kStageTokens);
 
         float m_run[2] = {-INFINITY, -INFINITY};
         float l_run[2] = {0.f, 0.f};
@@ -489,7 +670,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
             const int valid = min(kStageTokens, it.tok_end - t0);
             uint8_t* sbase = ring + (size_t)slot * kSlotBytes;
             const uint32_t sbase_u32 = ring_u32 + slot * kSlotBytes;
-            if (valid < kStageTokens) {
+            if (LOAD == kLoadTma && valid < kStageTokens) {
                 // Rows past the row's last token may hold anything (stale
                 // slot contents, unwritten pool memory): zero V there so that
                 // p = 0 never meets a non-finite value in the P.V product.

@@ -95,7 +95,7 @@ void pkv_router_params_b200(pkv_router_params* p) {
     p->supported_g = 0;         // every G in {1,2,4,8} runs the split routes
     p->min_split_len = 0;
     p->ctas_per_sm = 2;
-    p->tasks_per_cta = 2;       // LPT-packed: about two tasks per resident CTA
+    p->tasks_per_cta = 1;       // one task per resident CTA slot measured fastest
     p->max_splits = 256;
     p->min_tiles_per_task = 4;   // 128 tokens: 8 ring stages, two per consumer warp
 }

@@ -99,6 +99,9 @@ class DecodeEngine:
         self.requested_splits = requested_splits
         self._workspace = torch.empty(0, device=self.device, dtype=torch.float32)
         self._counters = torch.zeros(0, device=self.device, dtype=torch.int32)
+        # buffers replaced by a larger one stay alive: captured graphs may
+        # still reference them
+        self._retired: list[torch.Tensor] = []
 
     # ---------------------------------------------------------------- planning
     def plan_step(self, seq_lens, block_rows: np.ndarray, q_indices=None,
@@ -148,8 +151,10 @@ class DecodeEngine:
         """Grows the shared workspace / merge counters (never inside a capture)."""
         need = ops.workqueue_workspace_bytes(total_slots, self.hq) // 4
         if self._workspace.numel() < need:
+            self._retired.append(self._workspace)
             self._workspace = torch.empty(need, device=self.device, dtype=torch.float32)
         if self._counters.numel() < batch * self.hkv:
+            self._retired.append(self._counters)
             self._counters = torch.zeros(batch * self.hkv, device=self.device, dtype=torch.int32)
 
     # ---------------------------------------------------------------- execution
