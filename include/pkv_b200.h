@@ -126,6 +126,38 @@ pkv_status pkv_paged_attention_workqueue(
     int bucket_context, int num_tasks, int total_partial_slots,
     int fused_merge, pkv_dtype dtype, void* stream);
 
+/* Capacity of the scratch array used by
+ * pkv_paged_attention_workqueue_noalloc (bytes of fp32 partial states). */
+#define PKV_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/* pkv_paged_attention_workqueue for callers that cannot allocate device
+ * memory -- an FFI host (Go, Java, C) handed device pointers by an inference
+ * server that owns every allocation through its own pool, or code that must
+ * not call cudaMalloc on the decode path.  It takes the same inputs and
+ * output but no workspace and no merge counters: the split partial states go
+ * to a static device array inside this library, PKV_NOALLOC_SCRATCH_BYTES
+ * (8 MiB) per GPU that loads the library, held until the process exits, and
+ * the splits are merged by the separate merge kernel.  It allocates nothing.
+ * Limits and rules:
+ *  - total_partial_slots * Hq * 130 * 4 bytes must fit in the array, else it
+ *    returns PKV_ERR_CAPACITY without launching anything;
+ *  - the first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture;
+ *  - all calls on a device share the array: calls that overlap on the GPU
+ *    (other streams, other threads) race on it and must be serialised.
+ * Has no counterpart in the reference, whose entry points always take a
+ * caller-allocated workspace. */
+pkv_status pkv_paged_attention_workqueue_noalloc(
+    const void* q_source, const void* k_pages, const void* v_pages,
+    const int32_t* block_table, const int32_t* seq_lens,
+    const int32_t* work_items, const int32_t* split_offsets,
+    const int32_t* q_indices, const int32_t* out_indices, void* output,
+    int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim,
+    int physical_pages, int page_size, int max_pages,
+    int bucket_context, int num_tasks, int total_partial_slots,
+    pkv_dtype dtype, void* stream);
+
 /* Same as pkv_paged_attention_workqueue, but instead of the normalised
  * output it writes, per row b and query head h, the combined log-sum-exp
  * state of all of the row's splits to

@@ -20,6 +20,14 @@ using namespace pkv;
 // Device-side error word (one per device that loads the library).
 __device__ unsigned int g_pkv_error_word = 0u;
 
+// Scratch for pkv_paged_attention_workqueue_noalloc: the split partial
+// states live in this file-scope device array instead of a caller-provided
+// workspace, for callers that cannot allocate device memory.  Every GPU that
+// loads the library holds it until exit; every call on a device shares it
+// (calls that overlap on the GPU race on it).  In host code the name is only
+// a stand-in: kernels get its device address from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_pkv_noalloc_scratch[PKV_NOALLOC_SCRATCH_BYTES];
+
 namespace {
 
 #ifndef PKV_RING_SLOTS
@@ -473,6 +481,37 @@ pkv_status workqueue_common(const Common& c, const int32_t* seq_lens, const int3
     return launch(ls, stream);
 }
 
+// ---------------------------------------------------------------- no-alloc
+std::atomic<void*> g_noalloc_scratch_ptr[kMaxDevices];
+std::mutex g_noalloc_mutex;
+
+// Once per device, with that device current: the device address of the
+// scratch array.
+pkv_status noalloc_scratch(void** out) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        cudaGetLastError();
+        return fail(PKV_ERR_NO_DEVICE, "no CUDA device is available (%s)", cudaGetErrorString(e));
+    }
+    void* ptr = g_noalloc_scratch_ptr[dev].load(std::memory_order_acquire);
+    if (ptr == nullptr) {
+        std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+        ptr = g_noalloc_scratch_ptr[dev].load(std::memory_order_relaxed);
+        if (ptr == nullptr) {
+            e = cudaGetSymbolAddress(&ptr, g_pkv_noalloc_scratch);
+            if (e != cudaSuccess || ptr == nullptr) {
+                cudaGetLastError();
+                return fail(PKV_ERR_CUDA, "cudaGetSymbolAddress(no-alloc scratch) failed: %s",
+                            cudaGetErrorString(e));
+            }
+            g_noalloc_scratch_ptr[dev].store(ptr, std::memory_order_release);
+        }
+    }
+    *out = ptr;
+    return PKV_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -561,6 +600,37 @@ pkv_status pkv_paged_attention_workqueue(
                             out_indices, output, nullptr, workspace, workspace_bytes, q_rows,
                             out_rows, bucket_context, num_tasks, total_partial_slots, fused_merge,
                             stream);
+}
+
+pkv_status pkv_paged_attention_workqueue_noalloc(
+    const void* q_source, const void* k_pages, const void* v_pages, const int32_t* block_table,
+    const int32_t* seq_lens, const int32_t* work_items, const int32_t* split_offsets,
+    const int32_t* q_indices, const int32_t* out_indices, void* output, int B, int q_rows,
+    int out_rows, int Hq, int Hkv, int head_dim, int physical_pages, int page_size, int max_pages,
+    int bucket_context, int num_tasks, int total_partial_slots, pkv_dtype dtype, void* stream) {
+    // Same checks and kernels as pkv_paged_attention_workqueue with the
+    // separate merge kernel; only the workspace is the library's own array.
+    if (total_partial_slots > 0 && Hq > 0) {
+        const size_t need = pkv_workqueue_workspace_bytes(total_partial_slots, Hq);
+        if (need > (size_t)PKV_NOALLOC_SCRATCH_BYTES) {
+            return fail(PKV_ERR_CAPACITY,
+                        "total_partial_slots=%d with Hq=%d needs %zu bytes of partial-state "
+                        "scratch; the no-alloc entry point holds at most %zu bytes "
+                        "(PKV_NOALLOC_SCRATCH_BYTES)",
+                        total_partial_slots, Hq, need, (size_t)PKV_NOALLOC_SCRATCH_BYTES);
+        }
+    }
+    Common c{q_source, k_pages, v_pages, block_table, B, Hq, Hkv, head_dim,
+             physical_pages, page_size, max_pages, dtype};
+    pkv_status st = check_common(c);
+    if (st != PKV_OK) return st;
+    void* scratch = nullptr;
+    st = noalloc_scratch(&scratch);
+    if (st != PKV_OK) return st;
+    return workqueue_common(c, seq_lens, work_items, split_offsets, nullptr, q_indices,
+                            out_indices, output, nullptr, scratch,
+                            (size_t)PKV_NOALLOC_SCRATCH_BYTES, q_rows, out_rows, bucket_context,
+                            num_tasks, total_partial_slots, 0, stream);
 }
 
 pkv_status pkv_paged_attention_workqueue_state(
