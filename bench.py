@@ -415,7 +415,7 @@ def run_engine_arm(args) -> None:
             "l2": "flushed before every step outside the timed intervals: 256 MiB write, "
                   "then 256 MiB read (no dirty lines left for the timed step)",
             "merge": "fused last-task merge" if not args.no_fused else "PDL merge kernel",
-            "split_policy": "balanced (C++ builder)",
+            "schedule": "device-side equal-token groups (no host work queue)",
         },
         "hbm_gbs": achieved, "hbm_frac_of_8tbs": achieved / 8000.0,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

@@ -126,6 +126,31 @@ pkv_status pkv_paged_attention_workqueue(
     int bucket_context, int num_tasks, int total_partial_slots,
     int fused_merge, pkv_dtype dtype, void* stream);
 
+/* Decode with a device-side schedule: no work queue and no host-side
+ * builder.  The 32-token tiles of all rows, concatenated in row order, are
+ * cut into NG equal ranges (NG = 2 * SMs / Hkv groups of Hkv CTAs); each CTA
+ * decodes the row pieces of its range for one KV head, so every CTA streams
+ * the same number of tokens whatever the mix of lengths.  Row b attends to
+ * seq_lens[b] tokens, reads q_source[q_indices[b]] and writes
+ * output[out_indices[b]] (either index array may be NULL = identity).
+ * merge_counters [B, Hkv] zeroed int32 selects the fused last-task merge
+ * (zero again on return); NULL runs the separate merge kernel.  workspace
+ * needs pkv_auto_workspace_bytes(B, Hq, Hkv, 0) bytes.  The reference has no
+ * counterpart: it always needs a host-built work queue or a fixed split
+ * count (tests/benchmark_serving_trace.py:655-729). */
+pkv_status pkv_paged_attention_auto(
+    const void* q_source, const void* k_pages, const void* v_pages,
+    const int32_t* block_table, const int32_t* seq_lens,
+    const int32_t* q_indices, const int32_t* out_indices, void* output,
+    void* workspace, size_t workspace_bytes, int32_t* merge_counters,
+    int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim,
+    int physical_pages, int page_size, int max_pages,
+    pkv_dtype dtype, void* stream);
+
+/* Workspace bytes of pkv_paged_attention_auto: (B + NG) * Hq * 130 * 4 with
+ * NG = 2 * sm_count / Hkv; sm_count <= 0 queries the current device. */
+size_t pkv_auto_workspace_bytes(int B, int Hq, int Hkv, int sm_count);
+
 /* Capacity of the scratch array used by
  * pkv_paged_attention_workqueue_noalloc (bytes of fp32 partial states). */
 #define PKV_NOALLOC_SCRATCH_BYTES (8u << 20)

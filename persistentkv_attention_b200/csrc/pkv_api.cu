@@ -261,7 +261,9 @@ pkv_status launch_typed(const LaunchSpec& ls, const CUtensorMap& tk, const CUten
         attr_done.fetch_or(bit, std::memory_order_acq_rel);
     }
     const int resident = kCtasPerSm * ds->sm_count;
-    const int grid = ls.dp.num_items < resident ? ls.dp.num_items : resident;
+    const int grid = ls.dp.auto_groups > 0
+                         ? ls.dp.auto_groups * ls.dp.Hkv
+                         : (ls.dp.num_items < resident ? ls.dp.num_items : resident);
     kern<<<grid, kThreads, smem, stream>>>(ls.dp, tk, tv);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess)
@@ -272,6 +274,10 @@ pkv_status launch_typed(const LaunchSpec& ls, const CUtensorMap& tk, const CUten
         mp.part_l = ls.dp.part_l;
         mp.part_acc = ls.dp.part_acc;
         mp.split_offsets = ls.dp.work_items != nullptr ? ls.dp.split_offsets : nullptr;
+        mp.seq_lens = ls.dp.seq_lens;
+        mp.auto_groups = ls.dp.auto_groups;
+        mp.max_pages = ls.dp.max_pages;
+        mp.page_size = ls.dp.page_size;
         mp.out_indices = ls.dp.out_indices;
         mp.out = ls.dp.out;
         mp.state_out = ls.dp.state_out;
@@ -512,6 +518,11 @@ pkv_status noalloc_scratch(void** out) {
     return PKV_OK;
 }
 
+int auto_groups_for(int sm_count, int Hkv) {
+    const int g = (kCtasPerSm * sm_count) / (Hkv > 0 ? Hkv : 1);
+    return g > 0 ? g : 1;
+}
+
 }  // namespace
 
 extern "C" {
@@ -600,6 +611,67 @@ pkv_status pkv_paged_attention_workqueue(
                             out_indices, output, nullptr, workspace, workspace_bytes, q_rows,
                             out_rows, bucket_context, num_tasks, total_partial_slots, fused_merge,
                             stream);
+}
+
+size_t pkv_auto_workspace_bytes(int B, int Hq, int Hkv, int sm_count) {
+    if (B <= 0 || Hq <= 0 || Hkv <= 0) return 0;
+    if (sm_count <= 0) {
+        DeviceState* ds = nullptr;
+        if (current_device(&ds) != PKV_OK) return 0;
+        sm_count = ds->sm_count;
+    }
+    const long long slots = (long long)B + auto_groups_for(sm_count, Hkv);
+    return (size_t)slots * Hq * (kHeadDim + 2) * sizeof(float);
+}
+
+pkv_status pkv_paged_attention_auto(const void* q_source, const void* k_pages, const void* v_pages,
+                                    const int32_t* block_table, const int32_t* seq_lens,
+                                    const int32_t* q_indices, const int32_t* out_indices,
+                                    void* output, void* workspace, size_t workspace_bytes,
+                                    int32_t* merge_counters, int B, int q_rows, int out_rows,
+                                    int Hq, int Hkv, int head_dim, int physical_pages,
+                                    int page_size, int max_pages, pkv_dtype dtype, void* stream) {
+    Common c{q_source, k_pages, v_pages, block_table, B, Hq, Hkv, head_dim,
+             physical_pages, page_size, max_pages, dtype};
+    pkv_status st = check_common(c);
+    if (st != PKV_OK) return st;
+    if (seq_lens == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "seq_lens must be a CUDA tensor");
+    if (output == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "output must be a CUDA tensor");
+    if (q_rows <= 0 || out_rows <= 0)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "q and output must have at least one row");
+    if (B == 0) return ok_status();
+    DeviceState* ds = nullptr;
+    st = current_device(&ds);
+    if (st != PKV_OK) return st;
+    const int NG = auto_groups_for(ds->sm_count, Hkv);
+    const long long slots = (long long)B + NG;
+    const size_t need = (size_t)slots * Hq * (kHeadDim + 2) * sizeof(float);
+    if (workspace == nullptr) return fail(PKV_ERR_WORKSPACE, "auto route requires workspace");
+    if (workspace_bytes < need) {
+        return fail(PKV_ERR_WORKSPACE, "workspace holds %zu bytes but %zu are needed",
+                    workspace_bytes, need);
+    }
+    if (reinterpret_cast<uintptr_t>(workspace) & 15u)
+        return fail(PKV_ERR_MISALIGNED, "workspace must be 16-byte aligned");
+    LaunchSpec ls;
+    fill_common(ls, c);
+    ls.dp.out = output;
+    ls.dp.seq_lens = seq_lens;
+    ls.dp.q_indices = q_indices;
+    ls.dp.out_indices = out_indices;
+    ls.dp.merge_counters = merge_counters;
+    ls.dp.q_rows = q_rows;
+    ls.dp.out_rows = out_rows;
+    ls.dp.context = max_pages * page_size;
+    ls.dp.num_splits = 1;
+    ls.dp.auto_groups = NG;
+    ls.dp.num_items = NG * Hkv;
+    ls.dp.total_slots = (int)slots;
+    // the work-queue form of the fused merge (per-row slot ranges) applies
+    ls.dp.work_items = nullptr;
+    partition_workspace(ls.dp, workspace, slots);
+    ls.merge = merge_counters == nullptr;
+    return launch(ls, stream);
 }
 
 pkv_status pkv_paged_attention_workqueue_noalloc(

@@ -46,6 +46,7 @@ struct DecodeParams {
     int B, q_rows, out_rows, Hq, Hkv;
     int num_pages, page_size, max_pages;
     int context, num_splits, num_items, total_slots;
+    int auto_groups;   // > 0: device-side schedule over auto_groups x Hkv CTAs
     float scale_log2;  // softmax scale * log2(e)
 };
 
@@ -53,7 +54,9 @@ struct MergeParams {
     const float* part_m;
     const float* part_l;
     const float* part_acc;
-    const int32_t* split_offsets;  // [B + 1] or null (rectangular)
+    const int32_t* split_offsets;  // [B + 1] or null (rectangular / auto)
+    const int32_t* seq_lens;       // auto route: slot ranges follow from seq_lens
+    int auto_groups, max_pages, page_size;
     const int32_t* out_indices;    // [B] or null
     void* out;
     float* state_out;
@@ -289,6 +292,154 @@ __device__ __forceinline__ void merge_slots(const float* __restrict__ pm,
     }
 }
 
+// ------------------------------------------------------------ device schedule
+// The "auto" route needs no work queue: the tiles of all rows, concatenated
+// in row order, are cut into NG equal ranges (groups), and CTA
+// c = g * Hkv + kvh decodes, for KV head kvh, every row piece that falls in
+// group g.  Each row's pieces are its split-K partial slots; row b's slots
+// start at O_b = sum over earlier rows of their piece counts.  Everything
+// follows in closed form from seq_lens, so every CTA (and the merge kernel)
+// derives the same schedule without a host-built queue.
+__device__ __forceinline__ int auto_row_tiles(const DecodeParams& p, int b) {
+    int seq = __ldg(p.seq_lens + b);
+    const long long limit = (long long)p.max_pages * p.page_size;
+    if (seq < 0) seq = 0;
+    if ((long long)seq > limit) seq = (int)limit;
+    return (seq + kTileTokens - 1) / kTileTokens;
+}
+
+__device__ __forceinline__ long long auto_group_start(int g, long long T, int NG) {
+    return (long long)g * T / NG;
+}
+
+// Groups holding the first and last tile of a row (tile prefix P, n tiles);
+// an empty row is placed in the group of its position in the stream.
+__device__ __forceinline__ void auto_row_groups(long long P, int n, long long T, int NG, int& gf,
+                                                int& gl) {
+    if (T == 0) {
+        gf = gl = 0;
+        return;
+    }
+    const long long first = n > 0 ? P : (P < T ? P : T - 1);
+    const long long last = n > 0 ? P + n - 1 : first;
+    gf = (int)(((first + 1) * NG - 1) / T);
+    gl = (int)(((last + 1) * NG - 1) / T);
+}
+
+__device__ __forceinline__ int warp_exclusive_scan(int v, int lane) {
+    int x = v;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += y;
+    }
+    return x - v;
+}
+
+__device__ __forceinline__ int warp_sum_int(int v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+
+struct AutoCursor {
+    int g, kvh, NG;
+    long long T;
+    int b, b_end;      // next row to emit, one past the last row of the group
+    long long P;       // tile prefix of row b
+    int O;             // slot prefix of row b
+};
+
+// Whole-warp: the rows of this CTA's group and the prefixes of the first one.
+__device__ __forceinline__ AutoCursor auto_init(const DecodeParams& p, int lane) {
+    AutoCursor c;
+    c.NG = p.auto_groups;
+    c.g = (int)blockIdx.x / p.Hkv;
+    c.kvh = (int)blockIdx.x % p.Hkv;
+    long long T = 0;
+    for (int base = 0; base < p.B; base += 32) {
+        const int b = base + lane;
+        T += warp_sum_int(b < p.B ? auto_row_tiles(p, b) : 0);
+    }
+    c.T = T;
+    int b_lo = -1, b_hi = -1;
+    long long P_lo = 0, P = 0;
+    int O_lo = 0, O = 0;
+    for (int base = 0; base < p.B; base += 32) {
+        const int b = base + lane;
+        const bool valid = b < p.B;
+        const int n = valid ? auto_row_tiles(p, b) : 0;
+        const long long pfx = P + warp_exclusive_scan(n, lane);
+        int gf = 0, gl = -1;
+        if (valid) auto_row_groups(pfx, n, T, c.NG, gf, gl);
+        const int pieces = valid ? gl - gf + 1 : 0;
+        const int ofx = O + warp_exclusive_scan(pieces, lane);
+        const unsigned lo = __ballot_sync(0xffffffffu, valid && gl >= c.g);
+        if (b_lo < 0 && lo != 0u) {
+            const int src = __ffs(lo) - 1;
+            b_lo = base + src;
+            P_lo = __shfl_sync(0xffffffffu, pfx, src);
+            O_lo = __shfl_sync(0xffffffffu, ofx, src);
+        }
+        const unsigned hi = __ballot_sync(0xffffffffu, valid && gf <= c.g);
+        if (hi != 0u) b_hi = base + 31 - __clz(hi);
+        P += warp_sum_int(n);
+        O += warp_sum_int(pieces);
+    }
+    c.b = b_lo;
+    c.b_end = (b_lo >= 0 && b_hi >= b_lo) ? b_hi + 1 : b_lo;
+    c.P = P_lo;
+    c.O = O_lo;
+    return c;
+}
+
+// The next row piece of the cursor as a work item (lane-uniform).
+__device__ __forceinline__ Item auto_item(const DecodeParams& p, AutoCursor& c, bool report) {
+    Item it;
+    it.noop = false;
+    it.row = c.b;
+    it.kvh = c.kvh;
+    const int n = auto_row_tiles(p, c.b);
+    int gf, gl;
+    auto_row_groups(c.P, n, c.T, c.NG, gf, gl);
+    it.split = c.g - gf;
+    it.row_splits = gl - gf + 1;
+    it.slot = c.O + it.split;
+    if (it.slot >= p.total_slots) {  // the workspace bound B + NG never binds
+        if (report) raise_error(p.error, kErrSlot);
+        it.slot = -1;
+        it.row_splits = 2;
+    }
+    long long tb = 0, te = 0;
+    if (n > 0) {
+        const long long s0 = auto_group_start(c.g, c.T, c.NG);
+        const long long s1 = auto_group_start(c.g + 1, c.T, c.NG);
+        tb = (s0 > c.P ? s0 : c.P) - c.P;
+        te = ((c.P + n) < s1 ? (c.P + n) : s1) - c.P;
+    }
+    int seq = __ldg(p.seq_lens + c.b);
+    const long long limit = (long long)p.max_pages * p.page_size;
+    if (seq < 0) seq = 0;
+    if ((long long)seq > limit) {
+        if (report) raise_error(p.error, kErrLogicalPage);
+        seq = (int)limit;
+    }
+    long long t_end = te * kTileTokens;
+    if (t_end > seq) t_end = seq;
+    it.tok_begin = (int)(tb * kTileTokens);
+    it.tok_end = (int)(t_end > it.tok_begin ? t_end : it.tok_begin);
+    const int qr = p.q_indices != nullptr ? __ldg(p.q_indices + c.b) : c.b;
+    it.q_row = (qr >= 0 && qr < p.q_rows) ? qr : -1;
+    if (it.q_row < 0 && report) raise_error(p.error, kErrIndex);
+    const int orow = p.out_indices != nullptr ? __ldg(p.out_indices + c.b) : c.b;
+    it.out_row = (orow >= 0 && orow < p.out_rows) ? orow : -1;
+    if (it.out_row < 0 && report && p.out != nullptr) raise_error(p.error, kErrIndex);
+    c.P += n;
+    c.O += it.row_splits;
+    c.b += 1;
+    return it;
+}
+
 template <int G>
 struct DecodeSmem {
     static constexpr int kMergeStride = kHeadDim + 4;  // padded: conflict-free combine
@@ -350,6 +501,21 @@ __device__ __forceinline__ Item producer_item(const DecodeParams& p, int index, 
     return it;
 }
 
+// Next item of this CTA for the producer, with the first-batch page id.
+template <int BOX_ROWS>
+__device__ __forceinline__ Item producer_next(const DecodeParams& p, int s, int lane, int& pid0,
+                                              AutoCursor& cur) {
+    if (p.auto_groups > 0) {
+        const Item it = auto_item(p, cur, lane == 0);
+        const int tok = it.tok_begin + lane * BOX_ROWS;
+        pid0 = tok < it.tok_end
+                   ? __ldg(p.block_table + (size_t)it.row * p.max_pages + tok / p.page_size)
+                   : -1;
+        return it;
+    }
+    return producer_item<BOX_ROWS>(p, (int)blockIdx.x + s * (int)gridDim.x, lane, pid0);
+}
+
 template <int G, typename T, int BOX_ROWS, int NSLOTS, int LOAD>
 __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     pkv_decode_kernel(const __grid_constant__ DecodeParams p,
@@ -381,9 +547,20 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int my_items = (int)blockIdx.x < p.num_items
-                             ? (p.num_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
-                             : 0;
+    AutoCursor acur;
+    acur.b = acur.b_end = 0;
+    if (p.auto_groups > 0 && warp == kConsumerWarps) {
+        acur = auto_init(p, lane);
+    }
+    __shared__ int s_my_items;
+    if (p.auto_groups > 0) {
+        if (warp == kConsumerWarps && lane == 0)
+            s_my_items = acur.b >= 0 ? acur.b_end - acur.b : 0;
+    } else if (threadIdx.x == 0) {
+        s_my_items = (int)blockIdx.x < p.num_items
+                         ? (p.num_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
+                         : 0;
+    }
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NSLOTS; ++s) {
@@ -399,6 +576,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
         fence_mbar_init();
     }
     __syncthreads();
+    const int my_items = s_my_items;
 
     if (warp == kConsumerWarps) {
         // ============================ producer warp ============================
@@ -418,9 +596,8 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
         bool aborted = false;
         int pid0 = -1;
         Item cur;
-        if (my_items > 0) cur = producer_item<BOX_ROWS>(p, blockIdx.x, lane, pid0);
+        if (my_items > 0) cur = producer_next<BOX_ROWS>(p, 0, lane, pid0, acur);
         for (int s = 0; s < my_items && !aborted; ++s) {
-            const int index = (int)blockIdx.x + s * (int)gridDim.x;
             if (s == my_items - 1) griddep_launch_dependents();
 
             // ---- publish the descriptor and the G query rows of this item
@@ -558,10 +735,10 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                 }
                 if (!fetched) {
                     fetched = true;
-                    nxt = producer_item<BOX_ROWS>(p, index + (int)gridDim.x, lane, nxt_pid0);
+                    nxt = producer_next<BOX_ROWS>(p, s + 1, lane, nxt_pid0, acur);
                 }
             }
-            if (!fetched) nxt = producer_item<BOX_ROWS>(p, index + (int)gridDim.x, lane, nxt_pid0);
+            if (!fetched) nxt = producer_next<BOX_ROWS>(p, s + 1, lane, nxt_pid0, acur);
             cur = nxt;
             pid0 = nxt_pid0;
         }
@@ -790,7 +967,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
         }
         consumer_bar_sync();
 
-        const bool rect = p.work_items == nullptr;
+        const bool rect = p.work_items == nullptr && p.auto_groups == 0;
         const bool direct = it.row_splits == 1;
         const bool write_direct_out = direct && p.state_out == nullptr && it.out_row >= 0 &&
                                       (!rect || it.tok_end > it.tok_begin);
@@ -872,6 +1049,67 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
 // (kernels/persistentkv_attention.cuh:719-784).  Rows whose single split was
 // already written by the decode kernel are skipped.  grid = (Hkv, B),
 // block = 128 (one thread per head_dim element).
+// Slots [s0, s1) of row `row` under the device schedule: 128 threads reduce
+// the total tile count and the piece counts of the earlier rows.
+__device__ __forceinline__ void auto_slot_range(const MergeParams& p, int row, int& s0, int& s1) {
+    __shared__ long long s_red[4];
+    __shared__ long long s_pre[4];
+    const int t = threadIdx.x;
+    const long long limit = (long long)p.max_pages * p.page_size;
+    auto tiles_of = [&](int b) -> int {
+        int seq = __ldg(p.seq_lens + b);
+        if (seq < 0) seq = 0;
+        if ((long long)seq > limit) seq = (int)limit;
+        return (seq + kTileTokens - 1) / kTileTokens;
+    };
+    auto block_sum = [&](long long v, long long* buf) -> long long {
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if ((t & 31) == 0) buf[t >> 5] = v;
+        __syncthreads();
+        const long long r = buf[0] + buf[1] + buf[2] + buf[3];
+        __syncthreads();
+        return r;
+    };
+    long long mine = 0;
+    for (int b = t; b < p.B; b += 128) mine += tiles_of(b);
+    const long long T = block_sum(mine, s_red);
+    // tile prefix of every row below `row`, then their piece counts
+    long long pre = 0;
+    for (int b = t; b < row; b += 128) pre += tiles_of(b);
+    const long long P_row = block_sum(pre, s_pre);
+    // pieces of rows < row need each row's own prefix: scan in blocks of 128
+    long long pieces_before = 0;
+    long long base = 0;
+    for (int b0 = 0; b0 < row; b0 += 128) {
+        const int b = b0 + t;
+        const int n = b < row ? tiles_of(b) : 0;
+        // inclusive scan of n over the block
+        long long x = n;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const long long y = __shfl_up_sync(0xffffffffu, x, off);
+            if ((t & 31) >= off) x += y;
+        }
+        if ((t & 31) == 31) s_red[t >> 5] = x;
+        __syncthreads();
+        long long warp_off = 0;
+        for (int w = 0; w < (t >> 5); ++w) warp_off += s_red[w];
+        const long long chunk_total = s_red[0] + s_red[1] + s_red[2] + s_red[3];
+        __syncthreads();
+        const long long pfx = base + warp_off + x - n;
+        int gf = 0, gl = -1;
+        if (b < row) auto_row_groups(pfx, n, T, p.auto_groups, gf, gl);
+        pieces_before += (b < row) ? (gl - gf + 1) : 0;
+        base += chunk_total;
+    }
+    const long long O_row = block_sum(pieces_before, s_red);
+    int gf, gl;
+    auto_row_groups(P_row, tiles_of(row), T, p.auto_groups, gf, gl);
+    s0 = (int)O_row;
+    s1 = (int)O_row + (gl - gf + 1);
+}
+
 template <int G, typename T>
 __global__ void __launch_bounds__(kHeadDim)
     pkv_merge_kernel(const __grid_constant__ MergeParams p) {
@@ -881,7 +1119,9 @@ __global__ void __launch_bounds__(kHeadDim)
     const int kvh = blockIdx.x;
     const int row = blockIdx.y;
     int s0, s1;
-    if (p.split_offsets != nullptr) {
+    if (p.auto_groups > 0) {
+        auto_slot_range(p, row, s0, s1);
+    } else if (p.split_offsets != nullptr) {
         s0 = __ldg(p.split_offsets + row);
         s1 = __ldg(p.split_offsets + row + 1);
     } else {

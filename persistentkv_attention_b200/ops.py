@@ -270,6 +270,57 @@ def paged_attention_workqueue_state(q_source, k_pages, v_pages, block_table, seq
         int(total_partial_slots), _DTYPES[q_source.dtype], _stream()))
 
 
+def paged_attention_auto(q_source, k_pages, v_pages, block_table, seq_lens, output, workspace,
+                         q_indices=None, out_indices=None, merge_counters=None) -> None:
+    """Paged decode with the device-side schedule (no work queue, no host builder).
+
+    Row b attends to ``seq_lens[b]`` tokens of ``block_table[b]``, reads
+    ``q_source[q_indices[b]]`` and writes ``output[out_indices[b]]`` (identity
+    when an index tensor is None).  ``merge_counters`` (zeroed int32
+    ``[B, Hkv]``) selects the fused merge.  ``workspace`` needs
+    ``auto_workspace_bytes(B, Hq, Hkv)`` bytes.  No counterpart in the reference.
+    """
+    _check_tensor(q_source, "q_source", tuple(_DTYPES), 3)
+    hkv, physical_pages = _check_kv(q_source, k_pages, v_pages, k_pages.size(2))
+    _check_tensor(block_table, "block_table", torch.int32, 2)
+    _check_tensor(seq_lens, "seq_lens", torch.int32, 1)
+    _check_tensor(output, "output", q_source.dtype, 3)
+    b = block_table.size(0)
+    hq, d = q_source.size(1), q_source.size(2)
+    if seq_lens.size(0) != b:
+        raise RuntimeError("seq_lens batch mismatch")
+    if not (output.size(1) == hq and output.size(2) == d):
+        raise RuntimeError("output shape must match q head dimensions")
+    ptrs = []
+    for name, t in (("q_indices", q_indices), ("out_indices", out_indices)):
+        if t is None:
+            ptrs.append(None)
+        else:
+            _check_tensor(t, name, torch.int32, 1)
+            if t.size(0) != b:
+                raise RuntimeError(f"{name} batch mismatch")
+            ptrs.append(t.data_ptr())
+    ctr = None
+    if merge_counters is not None:
+        _check_tensor(merge_counters, "merge_counters", torch.int32, 2)
+        if not (merge_counters.size(0) == b and merge_counters.size(1) == hkv):
+            raise RuntimeError("merge_counters shape mismatch")
+        ctr = merge_counters.data_ptr()
+    _check_supported_gqa(hq, hkv)
+    ws_ptr, ws_bytes = _workspace(workspace)
+    lib = _native.load()
+    _native.check(lib.pkv_paged_attention_auto(
+        q_source.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), block_table.data_ptr(),
+        seq_lens.data_ptr(), ptrs[0], ptrs[1], output.data_ptr(), ws_ptr, ws_bytes, ctr, b,
+        q_source.size(0), output.size(0), hq, hkv, d, physical_pages, k_pages.size(2),
+        block_table.size(1), _DTYPES[q_source.dtype], _stream()))
+
+
+def auto_workspace_bytes(batch: int, hq: int, hkv: int, sm_count: int = 0) -> int:
+    """Workspace of ``paged_attention_auto`` (sm_count 0: the current device)."""
+    return int(_native.load().pkv_auto_workspace_bytes(batch, hq, hkv, sm_count))
+
+
 def combine_states(states, output, out_indices=None) -> None:
     """Merges ``states[n_parts, B, Hq, 130]`` into ``output`` rows (LSE combine)."""
     _check_tensor(states, "states", torch.float32, 4)

@@ -81,7 +81,7 @@ class DecodeEngine:
     """Work-queue decode over one paged K/V pool on the current device."""
 
     def __init__(self, k_pages: torch.Tensor, v_pages: torch.Tensor, hq: int,
-                 router: Router | None = None, policy: str = "balanced", fused: bool = True,
+                 router: Router | None = None, policy: str = "device", fused: bool = True,
                  requested_splits: int = 0):
         self.k_pages = k_pages
         self.v_pages = v_pages
@@ -106,25 +106,39 @@ class DecodeEngine:
     # ---------------------------------------------------------------- planning
     def plan_step(self, seq_lens, block_rows: np.ndarray, q_indices=None,
                   out: torch.Tensor | None = None) -> HostPlan:
-        """Host metadata of one step into a pinned buffer (``out`` reuses one)."""
+        """Host metadata of one step into a pinned buffer (``out`` reuses one).
+
+        With ``policy="device"`` the step carries no work queue: the kernel
+        schedules itself from seq_lens."""
         seq = np.asarray(seq_lens, dtype=np.int32)
         b = seq.size
-        queue = self.router.build_workqueue(seq, b, self.policy, self.requested_splits)
+        if self.policy == "device":
+            items, offsets, n_items = None, np.zeros(b + 1, np.int32), 0
+            total_slots = b + self._auto_groups()
+        else:
+            queue = self.router.build_workqueue(seq, b, self.policy, self.requested_splits)
+            items, offsets, n_items = queue.work_items, queue.split_offsets, queue.num_items
+            total_slots = queue.total_slots
         mp = block_rows.shape[1]
-        size = _staging_size(b, mp, queue.num_items)
+        size = _staging_size(b, mp, n_items)
         if out is None or out.numel() < size:
             out = torch.empty(size, dtype=torch.int32, pin_memory=True)
         buf = out[:size]
-        plan = HostPlan(buf, b, mp, queue.num_items, queue.total_slots, int(seq.max(initial=1)),
+        plan = HostPlan(buf, b, mp, n_items, total_slots, int(seq.max(initial=1)),
                         int(seq.sum()))
         v = plan.views(buf)
         v["block_table"].numpy()[:] = block_rows
         v["seq_lens"].numpy()[:] = seq
         v["q_indices"].numpy()[:] = np.arange(b) if q_indices is None else q_indices
         v["out_indices"].numpy()[:] = np.arange(b)
-        v["split_offsets"].numpy()[:] = queue.split_offsets
-        v["work_items"].numpy()[:] = queue.work_items
+        v["split_offsets"].numpy()[:] = offsets
+        if items is not None:
+            v["work_items"].numpy()[:] = items
         return plan
+
+    def _auto_groups(self) -> int:
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        return max(1, (2 * sms) // self.hkv)
 
     def plan_from_trace(self, requests, state) -> HostPlan:
         """Plan of one reference-style trace step (q rows indexed by request id)."""
@@ -161,6 +175,12 @@ class DecodeEngine:
     def run(self, plan: StepPlan, q_source: torch.Tensor, out: torch.Tensor) -> None:
         f = plan.fields
         counters = self._counters[: plan.batch * self.hkv].view(plan.batch, self.hkv)
+        if self.policy == "device":
+            ops.paged_attention_auto(
+                q_source, self.k_pages, self.v_pages, f["block_table"], f["seq_lens"], out,
+                self._workspace, f["q_indices"], f["out_indices"],
+                counters if self.fused else None)
+            return
         ops.paged_attention_workqueue(
             q_source, self.k_pages, self.v_pages, f["block_table"], f["seq_lens"],
             f["work_items"], f["split_offsets"], counters, f["q_indices"], f["out_indices"], out,

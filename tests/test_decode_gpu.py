@@ -300,3 +300,68 @@ def test_reference_cuda_path_workqueue():
     rows = torch.from_numpy(c.out_indices).long().cuda()
     assert (ours[rows].float() - theirs[rows].float()).abs().max().item() < MAX_ERR
     assert_close(theirs, c.oracle(), "f16", "reference kernel vs oracle")
+
+
+def _run_auto(c, d, fused):
+    ws = torch.empty(ops.auto_workspace_bytes(len(c.seq_lens), c.hq, c.hkv) // 4, device="cuda")
+    out = torch.full((c.out_rows, c.hq, 128), float("nan"), device="cuda",
+                     dtype=d["q_source"].dtype)
+    counters = torch.zeros(len(c.seq_lens), c.hkv, device="cuda", dtype=torch.int32)
+    ops.paged_attention_auto(d["q_source"], d["k_pages"], d["v_pages"], d["block_table"],
+                             d["seq_lens"], out, ws, d["q_indices"], d["out_indices"],
+                             counters if fused else None)
+    torch.cuda.synchronize()
+    assert (counters == 0).all()
+    return out
+
+
+@pytest.mark.parametrize("fused", [False, True])
+@pytest.mark.parametrize("g,dtype,page", [(4, "f16", 16), (1, "f16", 8), (8, "bf16", 32),
+                                          (2, "bf16", 16), (4, "bf16", 64)])
+def test_auto_route(fused, g, dtype, page):
+    """Device-side schedule: equal-token groups, no work queue."""
+    lens = [0] + EDGE_LENS + [9000, 4096]
+    c = make_case(lens, hq=32, hkv=32 // g, page_size=page, dtype=dtype, seed=60 + g,
+                  indexed=True)
+    out = _run_auto(c, c.cuda(), fused)
+    assert_close(out, c.oracle(), dtype, f"auto fused={fused}")
+
+
+@pytest.mark.parametrize("fused", [False, True])
+def test_auto_route_many_rows(fused):
+    rng = np.random.default_rng(8)
+    lens = np.minimum(32768, np.maximum(1, (256 * rng.zipf(1.1, 200)))).tolist()
+    lens[5] = 0
+    c = make_case(lens, seed=61, holes=0.1)
+    out = _run_auto(c, c.cuda(), fused)
+    assert_close(out, c.oracle(), "f16", f"200 rows fused={fused}")
+
+
+def test_auto_route_all_rows_empty_and_graph():
+    c = make_case([0, 0, 0], seed=62)
+    out = _run_auto(c, c.cuda(), True)
+    assert (out.float() == 0).all()
+    c = make_case([5000, 100, 3000], seed=63)
+    d = c.cuda()
+    ws = torch.empty(ops.auto_workspace_bytes(3, 32, 8) // 4, device="cuda")
+    out = torch.zeros(3, 32, 128, device="cuda", dtype=torch.float16)
+    counters = torch.zeros(3, 8, device="cuda", dtype=torch.int32)
+
+    def step():
+        ops.paged_attention_auto(d["q_source"], d["k_pages"], d["v_pages"], d["block_table"],
+                                 d["seq_lens"], out, ws, None, None, counters)
+
+    step()
+    torch.cuda.synchronize()
+    first = out.clone()
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            step()
+    out.zero_()
+    graph.replay()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, first)
+    assert_close(out, c.oracle(), "f16")
