@@ -199,12 +199,115 @@ __device__ __forceinline__ void sync_merge() {
     }
 }
 
+// Slots per warp prefetched by the low-latency merge (register budget).
+template <int G>
+__host__ __device__ constexpr int merge_prefetch_slots() {
+    return G <= 4 ? 2 : 1;
+}
+
+// Low-latency form of merge_slots for n <= NW * merge_prefetch_slots<G>()
+// slots: the m / l values and every acc row are requested in one round trip
+// before any reduction.
+template <int G, typename T, int NW, bool kNamedBarrier>
+__device__ __forceinline__ void merge_slots_small(const float* __restrict__ pm,
+                                                  const float* __restrict__ pl,
+                                                  const float* __restrict__ pa, int s0, int n,
+                                                  int Hq, int qh0, const MergeSmem& sm, T* out,
+                                                  float* state) {
+    constexpr int NT = NW * 32;
+    constexpr int KP = merge_prefetch_slots<G>();
+    const int t = threadIdx.x % NT;
+    const int warp = t >> 5;
+    const int lane = t & 31;
+    const int sg = t / G;
+    const int g = t % G;
+    float mv = kNegFltMax, lv = 0.f;
+    if (sg < n) {
+        const size_t i = (size_t)(s0 + sg) * Hq + qh0 + g;
+        mv = __ldcg(pm + i);
+        lv = __ldcg(pl + i);
+    }
+    float4 a[KP][G];
+#pragma unroll
+    for (int k = 0; k < KP; ++k) {
+        const int slot = warp + k * NW;
+#pragma unroll
+        for (int gg = 0; gg < G; ++gg) {
+            a[k][gg] = slot < n ? __ldcg(reinterpret_cast<const float4*>(
+                                      pa + ((size_t)(s0 + slot) * Hq + qh0 + gg) * kHeadDim +
+                                      4 * lane))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    float* sm_m = sm.w;          // [n][8]
+    float* sm_l = sm.w + 256;    // [n][8]
+    if (sg < n) {
+        sm_m[sg * 8 + g] = mv;
+        sm_l[sg * 8 + g] = lv;
+    }
+    sync_merge<kNamedBarrier>();
+    float M[G], L[G];
+#pragma unroll
+    for (int gg = 0; gg < G; ++gg) {
+        float mx = kNegFltMax;
+        for (int s = 0; s < n; ++s) mx = fmaxf(mx, sm_m[s * 8 + gg]);
+        float ls = 0.f;
+        for (int s = 0; s < n; ++s)
+            ls = fmaf(fast_exp2((sm_m[s * 8 + gg] - mx) * kLog2e), sm_l[s * 8 + gg], ls);
+        M[gg] = mx;
+        L[gg] = ls;
+    }
+#pragma unroll
+    for (int gg = 0; gg < G; ++gg) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < KP; ++k) {
+            const int slot = warp + k * NW;
+            if (slot < n) {
+                const float w = fast_exp2((sm_m[slot * 8 + gg] - M[gg]) * kLog2e);
+                acc.x = fmaf(w, a[k][gg].x, acc.x);
+                acc.y = fmaf(w, a[k][gg].y, acc.y);
+                acc.z = fmaf(w, a[k][gg].z, acc.z);
+                acc.w = fmaf(w, a[k][gg].w, acc.w);
+            }
+        }
+        *reinterpret_cast<float4*>(sm.red + (warp * G + gg) * kHeadDim + 4 * lane) = acc;
+    }
+    sync_merge<kNamedBarrier>();
+    for (int idx = t; idx < G * kHeadDim; idx += NT) {
+        const int gg = idx / kHeadDim;
+        const int d = idx % kHeadDim;
+        float o = 0.f;
+#pragma unroll
+        for (int j = 0; j < NW; ++j) o += sm.red[(j * G + gg) * kHeadDim + d];
+        float Mg = M[0], Lg = L[0];
+#pragma unroll
+        for (int q = 1; q < G; ++q) {
+            Mg = q == gg ? M[q] : Mg;
+            Lg = q == gg ? L[q] : Lg;
+        }
+        if (state != nullptr) {
+            state[gg * kStateStride + 2 + d] = o;
+            if (d == 0) {
+                state[gg * kStateStride] = Mg;
+                state[gg * kStateStride + 1] = Lg;
+            }
+        } else if (out != nullptr) {
+            out[gg * kHeadDim + d] = ElemOps<T>::from_float(Lg > 0.f ? o / Lg : 0.f);
+        }
+    }
+}
+
 template <int G, typename T, int NW, bool kNamedBarrier>
 __device__ __forceinline__ void merge_slots(const float* __restrict__ pm,
                                             const float* __restrict__ pl,
                                             const float* __restrict__ pa, int s0, int n, int Hq,
                                             int qh0, const MergeSmem& sm, T* out,
                                             float* state) {
+    if (n <= NW * merge_prefetch_slots<G>()) {
+        merge_slots_small<G, T, NW, kNamedBarrier>(pm, pl, pa, s0, n, Hq, qh0, sm, out, state);
+        return;
+    }
     constexpr int NT = NW * 32;
     const int t = threadIdx.x % NT;
     const int warp = t >> 5;
@@ -393,15 +496,40 @@ __device__ __forceinline__ AutoCursor auto_init(const DecodeParams& p, int lane)
     return c;
 }
 
-// The next row piece of the cursor as a work item (lane-uniform).
-__device__ __forceinline__ Item auto_item(const DecodeParams& p, AutoCursor& c, bool report) {
-    Item it;
-    it.noop = false;
-    it.row = c.b;
-    it.kvh = c.kvh;
-    const int n = auto_row_tiles(p, c.b);
+// The next row piece of the cursor as a work item.  All global reads (length,
+// q / out row, and the page id of box `lane` of the piece's first batch, whose
+// position follows from the cursor alone) are issued before anything branches
+// on them, so they travel together.
+template <int BOX_ROWS>
+__device__ __forceinline__ Item auto_item(const DecodeParams& p, AutoCursor& c, int lane,
+                                          bool report, int& pid0) {
+    const int b = c.b;
+    const int seq_raw = __ldg(p.seq_lens + b);
+    const int qr = p.q_indices != nullptr ? __ldg(p.q_indices + b) : b;
+    const int orow = p.out_indices != nullptr ? __ldg(p.out_indices + b) : b;
+    const long long limit = (long long)p.max_pages * p.page_size;
+    const int seq = seq_raw < 0 ? 0 : ((long long)seq_raw > limit ? (int)limit : seq_raw);
+    const int n = (seq + kTileTokens - 1) / kTileTokens;
     int gf, gl;
     auto_row_groups(c.P, n, c.T, c.NG, gf, gl);
+    long long tb = 0, te = 0;
+    if (n > 0) {
+        const long long s0 = auto_group_start(c.g, c.T, c.NG);
+        const long long s1 = auto_group_start(c.g + 1, c.T, c.NG);
+        tb = (s0 > c.P ? s0 : c.P) - c.P;
+        te = ((c.P + n) < s1 ? (c.P + n) : s1) - c.P;
+    }
+    long long t_end = te * kTileTokens;
+    if (t_end > seq) t_end = seq;
+    Item it;
+    it.noop = false;
+    it.row = b;
+    it.kvh = c.kvh;
+    it.tok_begin = (int)(tb * kTileTokens);
+    it.tok_end = (int)(t_end > it.tok_begin ? t_end : it.tok_begin);
+    const int tok = it.tok_begin + lane * BOX_ROWS;
+    pid0 = tok < it.tok_end ? __ldg(p.block_table + (size_t)b * p.max_pages + tok / p.page_size)
+                            : -1;
     it.split = c.g - gf;
     it.row_splits = gl - gf + 1;
     it.slot = c.O + it.split;
@@ -410,28 +538,9 @@ __device__ __forceinline__ Item auto_item(const DecodeParams& p, AutoCursor& c, 
         it.slot = -1;
         it.row_splits = 2;
     }
-    long long tb = 0, te = 0;
-    if (n > 0) {
-        const long long s0 = auto_group_start(c.g, c.T, c.NG);
-        const long long s1 = auto_group_start(c.g + 1, c.T, c.NG);
-        tb = (s0 > c.P ? s0 : c.P) - c.P;
-        te = ((c.P + n) < s1 ? (c.P + n) : s1) - c.P;
-    }
-    int seq = __ldg(p.seq_lens + c.b);
-    const long long limit = (long long)p.max_pages * p.page_size;
-    if (seq < 0) seq = 0;
-    if ((long long)seq > limit) {
-        if (report) raise_error(p.error, kErrLogicalPage);
-        seq = (int)limit;
-    }
-    long long t_end = te * kTileTokens;
-    if (t_end > seq) t_end = seq;
-    it.tok_begin = (int)(tb * kTileTokens);
-    it.tok_end = (int)(t_end > it.tok_begin ? t_end : it.tok_begin);
-    const int qr = p.q_indices != nullptr ? __ldg(p.q_indices + c.b) : c.b;
+    if ((long long)seq_raw > limit && report) raise_error(p.error, kErrLogicalPage);
     it.q_row = (qr >= 0 && qr < p.q_rows) ? qr : -1;
     if (it.q_row < 0 && report) raise_error(p.error, kErrIndex);
-    const int orow = p.out_indices != nullptr ? __ldg(p.out_indices + c.b) : c.b;
     it.out_row = (orow >= 0 && orow < p.out_rows) ? orow : -1;
     if (it.out_row < 0 && report && p.out != nullptr) raise_error(p.error, kErrIndex);
     c.P += n;
@@ -505,14 +614,7 @@ __device__ __forceinline__ Item producer_item(const DecodeParams& p, int index, 
 template <int BOX_ROWS>
 __device__ __forceinline__ Item producer_next(const DecodeParams& p, int s, int lane, int& pid0,
                                               AutoCursor& cur) {
-    if (p.auto_groups > 0) {
-        const Item it = auto_item(p, cur, lane == 0);
-        const int tok = it.tok_begin + lane * BOX_ROWS;
-        pid0 = tok < it.tok_end
-                   ? __ldg(p.block_table + (size_t)it.row * p.max_pages + tok / p.page_size)
-                   : -1;
-        return it;
-    }
+    if (p.auto_groups > 0) return auto_item<BOX_ROWS>(p, cur, lane, lane == 0, pid0);
     return producer_item<BOX_ROWS>(p, (int)blockIdx.x + s * (int)gridDim.x, lane, pid0);
 }
 
@@ -547,19 +649,25 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // The producer resolves its schedule and its first item before the
+    // CTA-wide barrier, so those reads overlap the barrier setup.
     AutoCursor acur;
     acur.b = acur.b_end = 0;
-    if (p.auto_groups > 0 && warp == kConsumerWarps) {
-        acur = auto_init(p, lane);
-    }
+    Item first_item;
+    int first_pid0 = -1;
     __shared__ int s_my_items;
-    if (p.auto_groups > 0) {
-        if (warp == kConsumerWarps && lane == 0)
-            s_my_items = acur.b >= 0 ? acur.b_end - acur.b : 0;
-    } else if (threadIdx.x == 0) {
-        s_my_items = (int)blockIdx.x < p.num_items
-                         ? (p.num_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
-                         : 0;
+    if (warp == kConsumerWarps) {
+        int mine;
+        if (p.auto_groups > 0) {
+            acur = auto_init(p, lane);
+            mine = acur.b >= 0 ? acur.b_end - acur.b : 0;
+        } else {
+            mine = (int)blockIdx.x < p.num_items
+                       ? (p.num_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
+                       : 0;
+        }
+        if (mine > 0) first_item = producer_next<BOX_ROWS>(p, 0, lane, first_pid0, acur);
+        if (lane == 0) s_my_items = mine;
     }
 
     if (threadIdx.x == 0) {
@@ -594,9 +702,8 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
         const uint32_t q_base = smem_u32(s_q);
         uint32_t gstage = 0;
         bool aborted = false;
-        int pid0 = -1;
-        Item cur;
-        if (my_items > 0) cur = producer_next<BOX_ROWS>(p, 0, lane, pid0, acur);
+        int pid0 = first_pid0;
+        Item cur = first_item;
         for (int s = 0; s < my_items && !aborted; ++s) {
             if (s == my_items - 1) griddep_launch_dependents();
 
