@@ -399,10 +399,15 @@ def run_engine_arm(args) -> None:
     value = tokens / (total_ms / 1000.0)
     per_step_bytes = bytes_alg / args.steps / world
     achieved = per_step_bytes / (total_ms / args.steps / 1000.0) / 1e9
+    # DRAM traffic per launch: the ratio dram bytes / algorithmic bytes of a
+    # committed ncu capture of this workload, applied to this run's launches.
     traffic = None
     tpath = REPO / "profiles" / f"traffic_{args.workload}.json"
     if tpath.exists():
-        traffic = json.loads(tpath.read_text()).get("dram_bytes_per_launch")
+        ratio = json.loads(tpath.read_text()).get("traffic_over_algorithmic")
+        if ratio:
+            traffic = {"bytes_per_launch": ratio * per_step_bytes, "over_algorithmic": ratio,
+                       "source": f"profiles/traffic_{args.workload}.json (ncu capture)"}
     line = {
         "metric": "decode-step tokens/s", "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
