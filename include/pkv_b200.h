@@ -147,6 +147,20 @@ pkv_status pkv_paged_attention_auto(
     int physical_pages, int page_size, int max_pages,
     pkv_dtype dtype, void* stream);
 
+/* pkv_paged_attention_auto writing, instead of the normalised output, the
+ * combined (m, l, acc) state of each row to state_out[B][Hq][130] (layout of
+ * pkv_paged_attention_workqueue_state): the per-GPU step of sequence
+ * sharding.  Same workspace as pkv_paged_attention_auto.  No counterpart in
+ * the reference. */
+pkv_status pkv_paged_attention_auto_state(
+    const void* q_source, const void* k_pages, const void* v_pages,
+    const int32_t* block_table, const int32_t* seq_lens,
+    const int32_t* q_indices, float* state_out,
+    void* workspace, size_t workspace_bytes, int32_t* merge_counters,
+    int B, int q_rows, int Hq, int Hkv, int head_dim,
+    int physical_pages, int page_size, int max_pages,
+    pkv_dtype dtype, void* stream);
+
 /* Workspace bytes of pkv_paged_attention_auto: (B + NG) * Hq * 130 * 4 with
  * NG = 2 * sm_count / Hkv; sm_count <= 0 queries the current device. */
 size_t pkv_auto_workspace_bytes(int B, int Hq, int Hkv, int sm_count);

@@ -98,6 +98,11 @@ SIGNATURES = {
          c_int, c_int, c_int, c_int, c_int, _P],
     ),
     "pkv_auto_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "pkv_paged_attention_auto_state": (
+        c_int,
+        [_P, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, c_int, c_int, c_int, c_int, c_int,
+         c_int, c_int, c_int, c_int, _P],
+    ),
     "pkv_paged_attention_workqueue_noalloc": (
         c_int,
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int,

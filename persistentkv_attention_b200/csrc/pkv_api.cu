@@ -624,6 +624,15 @@ size_t pkv_auto_workspace_bytes(int B, int Hq, int Hkv, int sm_count) {
     return (size_t)slots * Hq * (kHeadDim + 2) * sizeof(float);
 }
 
+namespace {
+
+pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* q_indices,
+                       const int32_t* out_indices, void* output, float* state_out,
+                       void* workspace, size_t workspace_bytes, int32_t* merge_counters,
+                       int q_rows, int out_rows, void* stream);
+
+}  // namespace
+
 pkv_status pkv_paged_attention_auto(const void* q_source, const void* k_pages, const void* v_pages,
                                     const int32_t* block_table, const int32_t* seq_lens,
                                     const int32_t* q_indices, const int32_t* out_indices,
@@ -633,10 +642,38 @@ pkv_status pkv_paged_attention_auto(const void* q_source, const void* k_pages, c
                                     int page_size, int max_pages, pkv_dtype dtype, void* stream) {
     Common c{q_source, k_pages, v_pages, block_table, B, Hq, Hkv, head_dim,
              physical_pages, page_size, max_pages, dtype};
+    if (output == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "output must be a CUDA tensor");
+    return auto_common(c, seq_lens, q_indices, out_indices, output, nullptr, workspace,
+                       workspace_bytes, merge_counters, q_rows, out_rows, stream);
+}
+
+pkv_status pkv_paged_attention_auto_state(
+    const void* q_source, const void* k_pages, const void* v_pages, const int32_t* block_table,
+    const int32_t* seq_lens, const int32_t* q_indices, float* state_out, void* workspace,
+    size_t workspace_bytes, int32_t* merge_counters, int B, int q_rows, int Hq, int Hkv,
+    int head_dim, int physical_pages, int page_size, int max_pages, pkv_dtype dtype,
+    void* stream) {
+    Common c{q_source, k_pages, v_pages, block_table, B, Hq, Hkv, head_dim,
+             physical_pages, page_size, max_pages, dtype};
+    if (state_out == nullptr)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "state_out must be a CUDA tensor");
+    return auto_common(c, seq_lens, q_indices, nullptr, nullptr, state_out, workspace,
+                       workspace_bytes, merge_counters, q_rows, B, stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* q_indices,
+                       const int32_t* out_indices, void* output, float* state_out,
+                       void* workspace, size_t workspace_bytes, int32_t* merge_counters,
+                       int q_rows, int out_rows, void* stream) {
+    const int B = c.B, Hq = c.Hq, Hkv = c.Hkv;
+    const int max_pages = c.max_pages, page_size = c.page_size;
     pkv_status st = check_common(c);
     if (st != PKV_OK) return st;
     if (seq_lens == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "seq_lens must be a CUDA tensor");
-    if (output == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "output must be a CUDA tensor");
     if (q_rows <= 0 || out_rows <= 0)
         return fail(PKV_ERR_INVALID_ARGUMENT, "q and output must have at least one row");
     if (B == 0) return ok_status();
@@ -656,6 +693,7 @@ pkv_status pkv_paged_attention_auto(const void* q_source, const void* k_pages, c
     LaunchSpec ls;
     fill_common(ls, c);
     ls.dp.out = output;
+    ls.dp.state_out = state_out;
     ls.dp.seq_lens = seq_lens;
     ls.dp.q_indices = q_indices;
     ls.dp.out_indices = out_indices;
@@ -673,6 +711,10 @@ pkv_status pkv_paged_attention_auto(const void* q_source, const void* k_pages, c
     ls.merge = merge_counters == nullptr;
     return launch(ls, stream);
 }
+
+}  // namespace
+
+extern "C" {
 
 pkv_status pkv_paged_attention_workqueue_noalloc(
     const void* q_source, const void* k_pages, const void* v_pages, const int32_t* block_table,

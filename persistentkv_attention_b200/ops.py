@@ -316,6 +316,36 @@ def paged_attention_auto(q_source, k_pages, v_pages, block_table, seq_lens, outp
         block_table.size(1), _DTYPES[q_source.dtype], _stream()))
 
 
+def paged_attention_auto_state(q_source, k_pages, v_pages, block_table, seq_lens, state_out,
+                               workspace, q_indices=None, merge_counters=None) -> None:
+    """``paged_attention_auto`` writing each row's (m, l, acc) state to the float32
+    ``state_out[B, Hq, 130]`` (one GPU's part of a sequence-sharded decode)."""
+    _check_tensor(q_source, "q_source", tuple(_DTYPES), 3)
+    hkv, physical_pages = _check_kv(q_source, k_pages, v_pages, k_pages.size(2))
+    _check_tensor(block_table, "block_table", torch.int32, 2)
+    _check_tensor(seq_lens, "seq_lens", torch.int32, 1)
+    _check_tensor(state_out, "state_out", torch.float32, 3)
+    b = block_table.size(0)
+    hq, d = q_source.size(1), q_source.size(2)
+    if tuple(state_out.shape) != (b, hq, STATE_STRIDE):
+        raise RuntimeError("state_out must have shape [B, Hq, 130]")
+    qi = None
+    if q_indices is not None:
+        _check_tensor(q_indices, "q_indices", torch.int32, 1)
+        qi = q_indices.data_ptr()
+    ctr = None
+    if merge_counters is not None:
+        _check_tensor(merge_counters, "merge_counters", torch.int32, 2)
+        ctr = merge_counters.data_ptr()
+    _check_supported_gqa(hq, hkv)
+    ws_ptr, ws_bytes = _workspace(workspace)
+    _native.check(_native.load().pkv_paged_attention_auto_state(
+        q_source.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), block_table.data_ptr(),
+        seq_lens.data_ptr(), qi, state_out.data_ptr(), ws_ptr, ws_bytes, ctr, b,
+        q_source.size(0), hq, hkv, d, physical_pages, k_pages.size(2), block_table.size(1),
+        _DTYPES[q_source.dtype], _stream()))
+
+
 def auto_workspace_bytes(batch: int, hq: int, hkv: int, sm_count: int = 0) -> int:
     """Workspace of ``paged_attention_auto`` (sm_count 0: the current device)."""
     return int(_native.load().pkv_auto_workspace_bytes(batch, hq, hkv, sm_count))

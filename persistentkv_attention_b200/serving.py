@@ -186,6 +186,14 @@ class DecodeEngine:
             f["work_items"], f["split_offsets"], counters, f["q_indices"], f["out_indices"], out,
             self._workspace, plan.host.bucket, self.page_size, plan.host.total_slots, self.fused)
 
+    def run_state(self, plan: StepPlan, q_source: torch.Tensor, state_out: torch.Tensor) -> None:
+        """One decode of this GPU's pages into the (m, l, acc) state [B, Hq, 130]."""
+        f = plan.fields
+        counters = self._counters[: plan.batch * self.hkv].view(plan.batch, self.hkv)
+        ops.paged_attention_auto_state(
+            q_source, self.k_pages, self.v_pages, f["block_table"], f["seq_lens"], state_out,
+            self._workspace, f["q_indices"], counters if self.fused else None)
+
     def capture(self, plan: StepPlan, q_source: torch.Tensor, out: torch.Tensor,
                 stream: torch.cuda.Stream | None = None) -> torch.cuda.CUDAGraph:
         self.run(plan, q_source, out)          # first call outside capture (attributes, maps)

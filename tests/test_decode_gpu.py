@@ -365,3 +365,35 @@ def test_auto_route_all_rows_empty_and_graph():
     torch.cuda.synchronize()
     assert torch.equal(out, first)
     assert_close(out, c.oracle(), "f16")
+
+
+@pytest.mark.parametrize("fused", [False, True])
+@pytest.mark.parametrize("world", [2, 3, 5])
+def test_auto_state_sequence_shards(fused, world):
+    """Sequence sharding on the device-side schedule: each shard's (m, l, acc)
+    state from paged_attention_auto_state, merged by combine_states.  With 5
+    shards the 33-token row (3 pages) leaves two shards empty."""
+    from persistentkv_attention_b200 import dist as pdist
+
+    lens = [30000, 33, 4000, 0, 777]
+    c = make_case(lens, seed=64 + world, indexed=True)
+    d = c.cuda()
+    b = len(lens)
+    states = []
+    for rank in range(world):
+        bt, sl = pdist.shard_rows(c.block_table, c.seq_lens, 16, world, rank)
+        st = torch.full((b, 32, 130), float("nan"), device="cuda")
+        ws = torch.empty(ops.auto_workspace_bytes(b, 32, 8) // 4, device="cuda")
+        counters = torch.zeros(b, 8, device="cuda", dtype=torch.int32)
+        ops.paged_attention_auto_state(d["q_source"], d["k_pages"], d["v_pages"],
+                                       torch.from_numpy(bt).cuda(),
+                                       torch.from_numpy(sl).cuda(), st, ws, d["q_indices"],
+                                       counters if fused else None)
+        torch.cuda.synchronize()
+        assert not torch.isnan(st).any()
+        assert (counters == 0).all()
+        states.append(st)
+    out = torch.full((c.out_rows, 32, 128), float("nan"), device="cuda", dtype=torch.float16)
+    ops.combine_states(torch.stack(states), out, d["out_indices"])
+    torch.cuda.synchronize()
+    assert_close(out, c.oracle(), "f16", f"auto state x{world} fused={fused}")
