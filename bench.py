@@ -311,7 +311,7 @@ def run_engine_arm(args) -> None:
     barrier()
     with ClockSampler(local) as clocks:
         with torch.cuda.stream(stream):
-            torch.cuda._sleep(2_000_000)          # lets the host queue run ahead
+            torch.cuda._sleep(20_000_000)         # lets the host queue run ahead (~10 ms)
             for i, j in enumerate(sched[args.warmup:]):
                 flush(i)
                 ev[i][0].record(stream)
@@ -450,8 +450,10 @@ def run_engine_arm(args) -> None:
 
 def run_seq_shard_arm(args) -> None:
     """Config 4 across GPUs: every rank decodes its contiguous page range of the
-    active request into an (m, l, acc) state; the states are all-gathered over
-    NVLink (NCCL) and merged exactly on every rank (strong scaling)."""
+    active request, and the per-rank (m, l, acc) states are merged exactly on
+    every rank (strong scaling).  ``--exchange fused`` (default): one kernel
+    per step pushes the states to the peers over NVLink and merges them;
+    ``--exchange nccl``: state kernel, NCCL all-gather, combine kernel."""
     import datetime
 
     import torch.distributed as dist
@@ -477,22 +479,24 @@ def run_seq_shard_arm(args) -> None:
     flush = L2Flush(dev)
     stream = torch.cuda.Stream(dev)
     n = min(len(steps), args.steps + args.warmup)
+    fused = args.exchange == "fused"
     plans, states, outs, graphs = [], [], [], []
-    local_bytes = []
     for state in steps[:n]:
         full = engine.plan_from_trace(reqs, state)
         rows = full.views(full.buf)["block_table"].numpy()
         bt, sl = pdist.shard_rows(rows, state.lengths, PAGE, world, rank)
         plans.append(engine.upload(engine.plan_step(sl, bt, q_indices=np.asarray(state.active_ids))))
-        local_bytes.append(int(sl.sum()) * hkv * D * 2 * 2)
+    xg = pdist.make_exchange(HQ, hkv, max(p.batch for p in plans)) if fused else None
     for p in plans:
         st = torch.empty(p.batch, HQ, 130, dtype=torch.float32, device=dev)
         o = torch.empty(p.batch, HQ, D, dtype=torch.float16, device=dev)
-        engine.run_state(p, q_pool, st)
+        run = (lambda p=p, o=o: engine.run_sharded(p, q_pool, o, xg)) if fused else \
+            (lambda p=p, st=st: engine.run_state(p, q_pool, st))
+        run()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.stream(stream):
             with torch.cuda.graph(g, stream=stream):
-                engine.run_state(p, q_pool, st)
+                run()
         states.append(st)
         outs.append(o)
         graphs.append(g)
@@ -502,6 +506,8 @@ def run_seq_shard_arm(args) -> None:
 
     def step(j):
         graphs[j].replay()
+        if fused:
+            return
         if world > 1:
             dist.all_gather_into_tensor(gathered[j], states[j])
         else:
@@ -523,7 +529,8 @@ def run_seq_shard_arm(args) -> None:
     barrier()
     with ClockSampler(local) as clocks:
         with torch.cuda.stream(stream):
-            torch.cuda._sleep(2_000_000)
+            torch.cuda._sleep(20_000_000)     # host runs ahead: a host hiccup on one rank
+                                              # must not stall the coupled peer kernels
             for i, j in enumerate(sched[args.warmup:]):
                 flush(i)
                 ev[i][0].record(stream)
@@ -567,19 +574,28 @@ def run_seq_shard_arm(args) -> None:
             "config": {"workload": f"{args.workload}: {w['desc']}", "hq": HQ, "hkv": hkv,
                        "head_dim": D, "page_size": PAGE,
                        "parallelism": f"sequence-sharded x{world}: page ranges per GPU, "
-                                      f"(m, l, acc) all-gather over NCCL, LSE combine",
+                                      + ("(m, l, acc) pushed to peers over NVLink and merged "
+                                         "inside the decode kernel" if fused else
+                                         "(m, l, acc) all-gather over NCCL, LSE combine"),
                        "l2": "flushed before every step outside the timed intervals"},
             "hbm_gbs_per_gpu": achieved,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": None,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                         "kernel": "pkv_decode_kernel (state) + all-gather + combine"},
-            "gpu_launches": args.steps * 2, "correctness_max_abs_err": max_err,
+                         "kernel": "pkv_decode_kernel (fused exchange)" if fused else
+                                   "pkv_decode_kernel (state) + all-gather + combine"},
+            "gpu_launches": args.steps * (1 if fused else 2), "correctness_max_abs_err": max_err,
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
+    graphs.clear()
+    torch.cuda.synchronize()
     if world > 1:
-        graphs.clear()
+        dist.barrier()      # no peer kernel still stores into this rank's buffer
+    if xg is not None:
+        xg.close()
+    if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 
@@ -594,6 +610,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seq-shard", action="store_true",
                     help="shard each request's pages across the GPUs (config 4 strong scaling)")
+    ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused",
+                    help="--seq-shard state exchange: inside the decode kernel, or NCCL")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

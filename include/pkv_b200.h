@@ -161,6 +161,53 @@ pkv_status pkv_paged_attention_auto_state(
     int physical_pages, int page_size, int max_pages,
     pkv_dtype dtype, void* stream);
 
+/* ---- Sequence-sharded decode with the exchange fused into the kernel ----
+ * One long request (or a batch) is split by page range across `world` GPUs,
+ * one process per GPU.  Each rank decodes its pages with the device-side
+ * schedule; the CTA that finishes a (row, KV head) stores the G combined
+ * states straight into every peer's gather buffer over NVLink (CUDA IPC
+ * mappings, plain 8-byte peer stores that each carry a value and the step
+ * number, no multicast), waits (at most 2 s, else PKV_DEVERR_PEER) until
+ * every peer's words of that (row, KV head) in its own memory carry the
+ * step number and merges the world parts into the output row.  No NCCL call
+ * and no second launch per step.  Every rank must make the same sequence of
+ * calls with the same B, and start each within the wait limit of the
+ * others.  No counterpart in the reference, which has no multi-GPU path. */
+typedef struct pkv_exchange pkv_exchange;
+#define PKV_EXCHANGE_HANDLE_BYTES 64
+#define PKV_MAX_WORLD 8
+
+/* Device bytes of one rank's exchange buffer (0 for an invalid shape). */
+size_t pkv_exchange_bytes(int world, int max_batch, int Hq, int Hkv);
+
+/* Allocates this rank's exchange buffer on the current device and writes its
+ * PKV_EXCHANGE_HANDLE_BYTES IPC handle to handle_out (may be NULL when
+ * world == 1).  Gather every rank's handle, in rank order, and pass them to
+ * pkv_exchange_connect. */
+pkv_status pkv_exchange_create(int world, int rank, int max_batch, int Hq, int Hkv,
+                               pkv_exchange** out, void* handle_out);
+
+/* Maps the other ranks' buffers: handles = world * PKV_EXCHANGE_HANDLE_BYTES. */
+pkv_status pkv_exchange_connect(pkv_exchange* exchange, const void* handles);
+
+/* Synchronises the device, unmaps the peers and frees the buffer. */
+pkv_status pkv_exchange_destroy(pkv_exchange* exchange);
+
+/* One step of sharded decode: this rank's pages of every row (block_table /
+ * seq_lens hold only this rank's range; a row may have 0 tokens here),
+ * exchanged and merged into output[out_indices[b]] on every rank.
+ * merge_counters [B, Hkv] zeroed int32 is required; workspace as for
+ * pkv_paged_attention_auto. */
+pkv_status pkv_paged_attention_sharded(
+    const void* q_source, const void* k_pages, const void* v_pages,
+    const int32_t* block_table, const int32_t* seq_lens,
+    const int32_t* q_indices, const int32_t* out_indices, void* output,
+    void* workspace, size_t workspace_bytes, int32_t* merge_counters,
+    pkv_exchange* exchange,
+    int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim,
+    int physical_pages, int page_size, int max_pages,
+    pkv_dtype dtype, void* stream);
+
 /* Workspace bytes of pkv_paged_attention_auto: (B + NG) * Hq * 130 * 4 with
  * NG = 2 * sm_count / Hkv; sm_count <= 0 queries the current device. */
 size_t pkv_auto_workspace_bytes(int B, int Hq, int Hkv, int sm_count);
@@ -245,6 +292,7 @@ pkv_status pkv_device_error(uint32_t* code, int clear);
 #define PKV_DEVERR_SLOT        0x8u  /* partial slot >= total_partial_slots  */
 #define PKV_DEVERR_INDEX       0x10u /* q_indices / out_indices out of range */
 #define PKV_DEVERR_TIMEOUT     0x20u /* bounded pipeline wait expired        */
+#define PKV_DEVERR_PEER        0x40u /* a peer's sharded state did not arrive */
 
 /* ---------------------------------------------------------------------------
  * Host-side scheduler: work-queue builder and split-count router.

@@ -40,7 +40,11 @@ DEVERR_BITS = {
     0x8: "partial slot out of range",
     0x10: "q/out index out of range",
     0x20: "pipeline wait timed out",
+    0x40: "a peer's sharded state did not arrive in time",
 }
+
+EXCHANGE_HANDLE_BYTES = 64
+MAX_WORLD = 8
 
 
 class RouterParams(ctypes.Structure):
@@ -102,6 +106,16 @@ SIGNATURES = {
         c_int,
         [_P, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, c_int, c_int, c_int, c_int, c_int,
          c_int, c_int, c_int, c_int, _P],
+    ),
+    "pkv_exchange_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "pkv_exchange_create": (
+        c_int, [c_int, c_int, c_int, c_int, c_int, POINTER(c_void_p), c_void_p]),
+    "pkv_exchange_connect": (c_int, [c_void_p, c_void_p]),
+    "pkv_exchange_destroy": (c_int, [c_void_p]),
+    "pkv_paged_attention_sharded": (
+        c_int,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, _P, c_int, c_int, c_int, c_int,
+         c_int, c_int, c_int, c_int, c_int, c_int, _P],
     ),
     "pkv_paged_attention_workqueue_noalloc": (
         c_int,

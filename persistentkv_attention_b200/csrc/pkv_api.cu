@@ -264,6 +264,25 @@ pkv_status launch_typed(const LaunchSpec& ls, const CUtensorMap& tk, const CUten
     const int grid = ls.dp.auto_groups > 0
                          ? ls.dp.auto_groups * ls.dp.Hkv
                          : (ls.dp.num_items < resident ? ls.dp.num_items : resident);
+    if (ls.dp.xg_world > 0) {
+        // the sharded step waits on peers inside the kernel: every CTA of the
+        // launch must be able to be resident at once
+        static std::atomic<int> occupancy[kMaxDevices];
+        int occ = occupancy[dev & (kMaxDevices - 1)].load(std::memory_order_acquire);
+        if (occ == 0) {
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem) !=
+                cudaSuccess) {
+                cudaGetLastError();
+                occ = 0;
+            }
+            occupancy[dev & (kMaxDevices - 1)].store(occ, std::memory_order_release);
+        }
+        if (grid > occ * ds->sm_count) {
+            return fail(PKV_ERR_UNSUPPORTED,
+                        "sharded decode needs %d resident CTAs but the device holds %d", grid,
+                        occ * ds->sm_count);
+        }
+    }
     kern<<<grid, kThreads, smem, stream>>>(ls.dp, tk, tv);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess)
@@ -624,14 +643,50 @@ size_t pkv_auto_workspace_bytes(int B, int Hq, int Hkv, int sm_count) {
     return (size_t)slots * Hq * (kHeadDim + 2) * sizeof(float);
 }
 
+}  // extern "C"
+
+// One rank's end of the sharded-decode state exchange: a single device
+// allocation holding [counters | gather buffer of LL words], exported by CUDA
+// IPC and mapped from every other rank's process.
+struct pkv_exchange {
+    int world, rank, bcap, hq, hkv, device;
+    size_t counters_off, gather_off, bytes;
+    char* base;                // this rank's allocation
+    char* peer[kMaxWorld];     // every rank's allocation as seen from here
+    int connected;
+};
+
 namespace {
+
+void xg_layout(int world, int bcap, int hq, size_t* counters_off, size_t* gather_off,
+               size_t* bytes) {
+    *counters_off = 0;
+    *gather_off = 256;
+    const size_t words = (size_t)2 * world * bcap * hq * kStateStride;
+    *bytes = *gather_off + words * sizeof(unsigned long long);
+}
+
+void xg_fill(DecodeParams& dp, const pkv_exchange& x) {
+    dp.xg_world = x.world;
+    dp.xg_rank = x.rank;
+    dp.xg_bcap = x.bcap;
+    for (int r = 0; r < kMaxWorld; ++r) {
+        char* b = r < x.world ? x.peer[r] : nullptr;
+        dp.xg_gather[r] =
+            b != nullptr ? reinterpret_cast<unsigned long long*>(b + x.gather_off) : nullptr;
+    }
+    dp.xg_counters = reinterpret_cast<unsigned*>(x.base + x.counters_off);
+}
 
 pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* q_indices,
                        const int32_t* out_indices, void* output, float* state_out,
                        void* workspace, size_t workspace_bytes, int32_t* merge_counters,
-                       int q_rows, int out_rows, void* stream);
+                       int q_rows, int out_rows, void* stream,
+                       const pkv_exchange* xg = nullptr);
 
 }  // namespace
+
+extern "C" {
 
 pkv_status pkv_paged_attention_auto(const void* q_source, const void* k_pages, const void* v_pages,
                                     const int32_t* block_table, const int32_t* seq_lens,
@@ -668,7 +723,7 @@ namespace {
 pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* q_indices,
                        const int32_t* out_indices, void* output, float* state_out,
                        void* workspace, size_t workspace_bytes, int32_t* merge_counters,
-                       int q_rows, int out_rows, void* stream) {
+                       int q_rows, int out_rows, void* stream, const pkv_exchange* xg) {
     const int B = c.B, Hq = c.Hq, Hkv = c.Hkv;
     const int max_pages = c.max_pages, page_size = c.page_size;
     pkv_status st = check_common(c);
@@ -709,6 +764,7 @@ pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* 
     ls.dp.work_items = nullptr;
     partition_workspace(ls.dp, workspace, slots);
     ls.merge = merge_counters == nullptr;
+    if (xg != nullptr) xg_fill(ls.dp, *xg);
     return launch(ls, stream);
 }
 
@@ -811,6 +867,137 @@ pkv_status pkv_device_error(uint32_t* code, int clear) {
     }
     *code = value;
     return ok_status();
+}
+
+// ------------------------------------------------------------ sharded decode
+size_t pkv_exchange_bytes(int world, int max_batch, int Hq, int Hkv) {
+    if (world <= 0 || world > kMaxWorld || max_batch <= 0 || Hq <= 0 || Hkv <= 0) return 0;
+    size_t c, g, bytes;
+    xg_layout(world, max_batch, Hq, &c, &g, &bytes);
+    return bytes;
+}
+
+pkv_status pkv_exchange_create(int world, int rank, int max_batch, int Hq, int Hkv,
+                               pkv_exchange** out, void* handle_out) {
+    if (out == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "out must not be null");
+    *out = nullptr;
+    if (world <= 0 || world > kMaxWorld)
+        return fail(PKV_ERR_UNSUPPORTED, "world must be in [1, %d], got %d", kMaxWorld, world);
+    if (rank < 0 || rank >= world)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "rank %d outside [0, %d)", rank, world);
+    if (max_batch <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "invalid exchange shape");
+    if (world > 1 && handle_out == nullptr)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "handle_out must not be null when world > 1");
+    DeviceState* ds = nullptr;
+    pkv_status st = current_device(&ds);
+    if (st != PKV_OK) return st;
+    pkv_exchange* x = new pkv_exchange();
+    x->world = world;
+    x->rank = rank;
+    x->bcap = max_batch;
+    x->hq = Hq;
+    x->hkv = Hkv;
+    cudaGetDevice(&x->device);
+    xg_layout(world, max_batch, Hq, &x->counters_off, &x->gather_off, &x->bytes);
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&x->base), x->bytes);
+    if (e == cudaSuccess) e = cudaMemset(x->base, 0, x->bytes);
+    const unsigned init[2] = {1u, 0u};  // step 1 (zeroed words carry step 0), no CTA done
+    if (e == cudaSuccess)
+        e = cudaMemcpy(x->base + x->counters_off, init, sizeof(init), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && world > 1) {
+        cudaIpcMemHandle_t h;
+        e = cudaIpcGetMemHandle(&h, x->base);
+        if (e == cudaSuccess) std::memcpy(handle_out, &h, sizeof(h));
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        if (x->base != nullptr) cudaFree(x->base);
+        delete x;
+        return fail(PKV_ERR_CUDA, "exchange allocation failed: %s", cudaGetErrorString(e));
+    }
+    for (int r = 0; r < kMaxWorld; ++r) x->peer[r] = nullptr;
+    x->peer[rank] = x->base;
+    x->connected = world == 1;
+    *out = x;
+    return ok_status();
+}
+
+pkv_status pkv_exchange_connect(pkv_exchange* x, const void* handles) {
+    if (x == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "exchange must not be null");
+    if (x->connected) return ok_status();
+    if (handles == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "handles must not be null");
+    int dev = -1;
+    cudaGetDevice(&dev);
+    if (dev != x->device)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "exchange belongs to device %d, current is %d",
+                    x->device, dev);
+    const char* hs = static_cast<const char*>(handles);
+    for (int r = 0; r < x->world; ++r) {
+        if (r == x->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, hs + (size_t)r * PKV_EXCHANGE_HANDLE_BYTES, sizeof(h));
+        void* ptr = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            for (int q = 0; q < r; ++q) {
+                if (q != x->rank && x->peer[q] != nullptr) {
+                    cudaIpcCloseMemHandle(x->peer[q]);
+                    x->peer[q] = nullptr;
+                }
+            }
+            return fail(PKV_ERR_CUDA, "mapping rank %d's exchange buffer failed: %s", r,
+                        cudaGetErrorString(e));
+        }
+        x->peer[r] = static_cast<char*>(ptr);
+    }
+    x->connected = 1;
+    return ok_status();
+}
+
+pkv_status pkv_exchange_destroy(pkv_exchange* x) {
+    if (x == nullptr) return ok_status();
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (prev != x->device) cudaSetDevice(x->device);
+    cudaDeviceSynchronize();
+    for (int r = 0; r < x->world; ++r) {
+        if (r != x->rank && x->peer[r] != nullptr) cudaIpcCloseMemHandle(x->peer[r]);
+    }
+    cudaFree(x->base);
+    cudaGetLastError();
+    if (prev >= 0 && prev != x->device) cudaSetDevice(prev);
+    delete x;
+    return ok_status();
+}
+
+pkv_status pkv_paged_attention_sharded(
+    const void* q_source, const void* k_pages, const void* v_pages, const int32_t* block_table,
+    const int32_t* seq_lens, const int32_t* q_indices, const int32_t* out_indices, void* output,
+    void* workspace, size_t workspace_bytes, int32_t* merge_counters, pkv_exchange* exchange,
+    int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim, int physical_pages,
+    int page_size, int max_pages, pkv_dtype dtype, void* stream) {
+    if (exchange == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "exchange must not be null");
+    if (!exchange->connected)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "exchange is not connected to its peers");
+    if (output == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "output must be a CUDA tensor");
+    if (merge_counters == nullptr)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "sharded decode requires merge_counters");
+    if (B > exchange->bcap)
+        return fail(PKV_ERR_CAPACITY, "batch %d exceeds the exchange's capacity %d", B,
+                    exchange->bcap);
+    if (Hq != exchange->hq || Hkv != exchange->hkv)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "head counts differ from the exchange's");
+    int dev = -1;
+    cudaGetDevice(&dev);
+    if (dev != exchange->device)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "exchange belongs to device %d, current is %d",
+                    exchange->device, dev);
+    Common c{q_source, k_pages, v_pages, block_table, B, Hq, Hkv, head_dim,
+             physical_pages, page_size, max_pages, dtype};
+    return auto_common(c, seq_lens, q_indices, out_indices, output, nullptr, workspace,
+                       workspace_bytes, merge_counters, q_rows, out_rows, stream, exchange);
 }
 
 }  // extern "C"

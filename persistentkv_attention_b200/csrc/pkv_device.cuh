@@ -40,6 +40,29 @@ constexpr unsigned kErrWorkItem = 0x4u;
 constexpr unsigned kErrSlot = 0x8u;
 constexpr unsigned kErrIndex = 0x10u;
 constexpr unsigned kErrTimeout = 0x20u;
+constexpr unsigned kErrPeer = 0x40u;  // a peer's state did not arrive in time
+
+// Sharded decode: each rank's states reach the other ranks' memory through
+// plain peer stores over NVLink, flagged by a release store of the step
+// number; the owner polls with acquire loads, bounded like every other wait.
+constexpr unsigned long long kPeerWaitLimitNs = 2000000000ull;
+constexpr int kMaxWorld = 8;
+
+__device__ __forceinline__ void st_release_sys_u32(unsigned* addr, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* addr) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned ld_relaxed_gpu_u32(const unsigned* addr) {
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+    return v;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));

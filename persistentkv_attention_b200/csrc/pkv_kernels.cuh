@@ -48,6 +48,13 @@ struct DecodeParams {
     int context, num_splits, num_items, total_slots;
     int auto_groups;   // > 0: device-side schedule over auto_groups x Hkv CTAs
     float scale_log2;  // softmax scale * log2(e)
+    // Sequence-sharded decode with the state exchange fused in (xg_world > 0):
+    // rank r's gather buffer of LL words [2 parities][world][xg_bcap][Hq][130],
+    // mapped into this process for every rank, and this rank's
+    // {step number, finished-CTA count} pair.
+    unsigned long long* xg_gather[kMaxWorld];
+    unsigned* xg_counters;
+    int xg_world, xg_rank, xg_bcap;
 };
 
 struct MergeParams {
@@ -171,12 +178,74 @@ __device__ __forceinline__ Item load_item(const DecodeParams& p, int index, bool
     return it;
 }
 
+// ------------------------------------------------------------------ exchange sink
+// Sequence-sharded decode exchanges states in "LL" words: each 8-byte word
+// carries a float value in its low half and the step number in its high half,
+// written by one 64-bit store, so a reader that sees the current step number
+// also sees the value: no fence, no flag, no second round trip.
+__device__ __forceinline__ unsigned long long xg_pack(float v, unsigned epoch) {
+    return ((unsigned long long)epoch << 32) | (unsigned long long)__float_as_uint(v);
+}
+
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* addr,
+                                                   unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* addr) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
+    return v;
+}
+
+// Where a finished (row, KV head) state goes in sharded mode: word `off`
+// (head qh0 of this rank's part) of every rank's gather buffer, plus this
+// thread's own values, kept for its merge of the gathered parts.
+template <int G>
+struct XgSink {
+    unsigned long long* const* gather;  // every rank's buffer (kernel parameters)
+    size_t off;
+    int world, rank;
+    unsigned epoch;
+    float o[G], m[G], l[G];  // own (o, m, l) of the k-th (head, dim) of this thread
+};
+
+// Thread-level emission of one merged value: the normalised output, the
+// (m, l, acc) state row, or the LL words of every peer (own value kept).
+template <int G, typename T, bool kXg>
+__device__ __forceinline__ void emit_merged(int k, int gg, int d, float o, float M, float L,
+                                            T* out, float* state, XgSink<G>& xg) {
+    if constexpr (kXg) {
+        xg.o[k] = o;
+        xg.m[k] = M;
+        xg.l[k] = L;
+        for (int r = 0; r < xg.world; ++r) {
+            if (r == xg.rank) continue;
+            unsigned long long* w = xg.gather[r] + xg.off + gg * kStateStride;
+            st_relaxed_sys_u64(w + 2 + d, xg_pack(o, xg.epoch));
+            if (d == 0) {
+                st_relaxed_sys_u64(w, xg_pack(M, xg.epoch));
+                st_relaxed_sys_u64(w + 1, xg_pack(L, xg.epoch));
+            }
+        }
+    } else if (state != nullptr) {
+        state[gg * kStateStride + 2 + d] = o;
+        if (d == 0) {
+            state[gg * kStateStride] = M;
+            state[gg * kStateStride + 1] = L;
+        }
+    } else if (out != nullptr) {
+        out[gg * kHeadDim + d] = ElemOps<T>::from_float(L > 0.f ? o / L : 0.f);
+    }
+}
+
 // ------------------------------------------------------------------ merge
 // Segmented log-sum-exp merge of the partial states in slots [s0, s0 + n) for
 // the G query heads qh0 .. qh0+G-1 of one row (reference cuh:719-784 and the
-// fused merge :660-708).  Run by NW warps; memory-level parallel: m / l are
-// reduced across all threads, weights are staged in shared memory per chunk
-// of 64 slots, and acc rows are read as float4 by NW slot groups.
+// fused merge :660-708).  Run by NW = 4 warps, latency first: every m / l
+// value is requested in one round trip and reduced online, the slot weights
+// follow from shared memory, and the acc rows are read as float4, several
+// slots per warp in flight.
 constexpr int kMergeChunk = 64;
 
 template <int NW>
@@ -185,7 +254,7 @@ __host__ __device__ constexpr int merge_scratch_floats() {
 }
 
 struct MergeSmem {
-    float* w;     // [kMergeChunk][8] weights of the current chunk
+    float* w;     // [kMergeChunk][8] slot m values, then weights
     float* stat;  // [2][NW][8] per-warp max / l partials
     float* red;   // [NW][G][128] acc partials (16-byte aligned)
 };
@@ -208,14 +277,15 @@ __host__ __device__ constexpr int merge_prefetch_slots() {
 // Low-latency form of merge_slots for n <= NW * merge_prefetch_slots<G>()
 // slots: the m / l values and every acc row are requested in one round trip
 // before any reduction.
-template <int G, typename T, int NW, bool kNamedBarrier>
+template <int G, typename T, int NW, bool kNamedBarrier, bool kXg>
 __device__ __forceinline__ void merge_slots_small(const float* __restrict__ pm,
                                                   const float* __restrict__ pl,
                                                   const float* __restrict__ pa, int s0, int n,
                                                   int Hq, int qh0, const MergeSmem& sm, T* out,
-                                                  float* state) {
+                                                  float* state, XgSink<G>& xg) {
     constexpr int NT = NW * 32;
     constexpr int KP = merge_prefetch_slots<G>();
+    static_assert((G * kHeadDim) % NT == 0, "whole (head, dim) passes");
     const int t = threadIdx.x % NT;
     const int warp = t >> 5;
     const int lane = t & 31;
@@ -274,7 +344,9 @@ __device__ __forceinline__ void merge_slots_small(const float* __restrict__ pm,
         *reinterpret_cast<float4*>(sm.red + (warp * G + gg) * kHeadDim + 4 * lane) = acc;
     }
     sync_merge<kNamedBarrier>();
-    for (int idx = t; idx < G * kHeadDim; idx += NT) {
+#pragma unroll
+    for (int k = 0; k < G * kHeadDim / NT; ++k) {
+        const int idx = t + k * NT;
         const int gg = idx / kHeadDim;
         const int d = idx % kHeadDim;
         float o = 0.f;
@@ -286,70 +358,94 @@ __device__ __forceinline__ void merge_slots_small(const float* __restrict__ pm,
             Mg = q == gg ? M[q] : Mg;
             Lg = q == gg ? L[q] : Lg;
         }
-        if (state != nullptr) {
-            state[gg * kStateStride + 2 + d] = o;
-            if (d == 0) {
-                state[gg * kStateStride] = Mg;
-                state[gg * kStateStride + 1] = Lg;
-            }
-        } else if (out != nullptr) {
-            out[gg * kHeadDim + d] = ElemOps<T>::from_float(Lg > 0.f ? o / Lg : 0.f);
-        }
+        emit_merged<G, T, kXg>(k, gg, d, o, Mg, Lg, out, state, xg);
     }
 }
 
-template <int G, typename T, int NW, bool kNamedBarrier>
+// Online (max, sum) pair merge: (m, l) absorbs (m2, l2).
+__device__ __forceinline__ void online_absorb(float& m, float& l, float m2, float l2) {
+    const float mx = fmaxf(m, m2);
+    l = l * fast_exp2((m - mx) * kLog2e) + l2 * fast_exp2((m2 - mx) * kLog2e);
+    m = mx;
+}
+
+// kXg: the merged values go to the sharded exchange sink `xg` instead of
+// `out` / `state`.
+template <int G, typename T, int NW, bool kNamedBarrier, bool kXg>
 __device__ __forceinline__ void merge_slots(const float* __restrict__ pm,
                                             const float* __restrict__ pl,
                                             const float* __restrict__ pa, int s0, int n, int Hq,
-                                            int qh0, const MergeSmem& sm, T* out,
-                                            float* state) {
+                                            int qh0, const MergeSmem& sm, T* out, float* state,
+                                            XgSink<G>& xg) {
     if (n <= NW * merge_prefetch_slots<G>()) {
-        merge_slots_small<G, T, NW, kNamedBarrier>(pm, pl, pa, s0, n, Hq, qh0, sm, out, state);
+        merge_slots_small<G, T, NW, kNamedBarrier, kXg>(pm, pl, pa, s0, n, Hq, qh0, sm, out,
+                                                        state, xg);
         return;
     }
     constexpr int NT = NW * 32;
+    static_assert((G * kHeadDim) % NT == 0, "whole (head, dim) passes");
     const int t = threadIdx.x % NT;
     const int warp = t >> 5;
     const int lane = t & 31;
     constexpr int kSlotsPerPass = NT / G;
     const int g = t % G;  // fixed: the strides below are multiples of G
-    float mx = kNegFltMax;
-    for (int s = t / G; s < n; s += kSlotsPerPass)
-        mx = fmaxf(mx, __ldcg(pm + (size_t)(s0 + s) * Hq + qh0 + g));
+    // ---- one pass over m and l: loads issued together, reduced online
+    const bool keep_m = n <= kMergeChunk;  // slot m values stay in shared memory
+    float mt = kNegFltMax, lt = 0.f;
+    constexpr int kUnrollML = 4;
+    for (int s = t / G; s < n; s += kUnrollML * kSlotsPerPass) {
+        float mv[kUnrollML], lv[kUnrollML];
 #pragma unroll
-    for (int off = 16; off >= G; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    if (lane < G) sm.stat[warp * 8 + lane] = mx;
+        for (int u = 0; u < kUnrollML; ++u) {
+            const int su = s + u * kSlotsPerPass;
+            const size_t i = (size_t)(s0 + su) * Hq + qh0 + g;
+            mv[u] = su < n ? __ldcg(pm + i) : kNegFltMax;
+            lv[u] = su < n ? __ldcg(pl + i) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kUnrollML; ++u) {
+            const int su = s + u * kSlotsPerPass;
+            if (su < n) {
+                if (keep_m) sm.w[su * 8 + g] = mv[u];
+                online_absorb(mt, lt, mv[u], lv[u]);
+            }
+        }
+    }
+#pragma unroll
+    for (int off = 16; off >= G; off >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, mt, off);
+        const float l2 = __shfl_xor_sync(0xffffffffu, lt, off);
+        online_absorb(mt, lt, m2, l2);
+    }
+    if (lane < G) {
+        sm.stat[warp * 8 + lane] = mt;
+        sm.stat[NW * 8 + warp * 8 + lane] = lt;
+    }
     sync_merge<kNamedBarrier>();
-    float m_all[G];
+    float m_all[G], l_all[G];
 #pragma unroll
     for (int gg = 0; gg < G; ++gg) {
-        float v = sm.stat[gg];
+        float mm = sm.stat[gg], ll = sm.stat[NW * 8 + gg];
 #pragma unroll
-        for (int w = 1; w < NW; ++w) v = fmaxf(v, sm.stat[w * 8 + gg]);
-        m_all[gg] = v;
+        for (int w = 1; w < NW; ++w) online_absorb(mm, ll, sm.stat[w * 8 + gg], sm.stat[NW * 8 + w * 8 + gg]);
+        m_all[gg] = mm;
+        l_all[gg] = ll;
     }
     float m_mine = m_all[0];
 #pragma unroll
     for (int gg = 1; gg < G; ++gg) m_mine = gg == g ? m_all[gg] : m_mine;
-    float ls = 0.f;
-    for (int s = t / G; s < n; s += kSlotsPerPass) {
-        const size_t i = (size_t)(s0 + s) * Hq + qh0 + g;
-        ls = fmaf(fast_exp2((__ldcg(pm + i) - m_mine) * kLog2e), __ldcg(pl + i), ls);
-    }
-#pragma unroll
-    for (int off = 16; off >= G; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
-    if (lane < G) sm.stat[NW * 8 + warp * 8 + lane] = ls;
 
     float4 acc[G];
 #pragma unroll
     for (int gg = 0; gg < G; ++gg) acc[gg] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int c0 = 0; c0 < n; c0 += kMergeChunk) {
         const int cn = min(kMergeChunk, n - c0);
+        // weights of the chunk's slots (m values from shared memory when kept)
         for (int i = t; i < cn * G; i += NT) {
             const int s = i / G;  // i % G == g
-            sm.w[s * 8 + g] = fast_exp2(
-                (__ldcg(pm + (size_t)(s0 + c0 + s) * Hq + qh0 + g) - m_mine) * kLog2e);
+            const float mv = keep_m ? sm.w[s * 8 + g]
+                                    : __ldcg(pm + (size_t)(s0 + c0 + s) * Hq + qh0 + g);
+            sm.w[s * 8 + g] = fast_exp2((mv - m_mine) * kLog2e);
         }
         sync_merge<kNamedBarrier>();
 #pragma unroll 4
@@ -371,27 +467,21 @@ __device__ __forceinline__ void merge_slots(const float* __restrict__ pm,
     for (int gg = 0; gg < G; ++gg)
         *reinterpret_cast<float4*>(sm.red + (warp * G + gg) * kHeadDim + 4 * lane) = acc[gg];
     sync_merge<kNamedBarrier>();
-    for (int idx = t; idx < G * kHeadDim; idx += NT) {
+#pragma unroll
+    for (int k = 0; k < G * kHeadDim / NT; ++k) {
+        const int idx = t + k * NT;
         const int gg = idx / kHeadDim;
         const int d = idx % kHeadDim;
-        float l_all = 0.f, o = 0.f;
+        float o = 0.f;
 #pragma unroll
-        for (int j = 0; j < NW; ++j) {
-            l_all += sm.stat[NW * 8 + j * 8 + gg];
-            o += sm.red[(j * G + gg) * kHeadDim + d];
-        }
-        if (state != nullptr) {
-            state[gg * kStateStride + 2 + d] = o;
-            if (d == 0) {
-                float mv = sm.stat[gg];
+        for (int j = 0; j < NW; ++j) o += sm.red[(j * G + gg) * kHeadDim + d];
+        float Mg = m_all[0], Lg = l_all[0];
 #pragma unroll
-                for (int w = 1; w < NW; ++w) mv = fmaxf(mv, sm.stat[w * 8 + gg]);
-                state[gg * kStateStride] = mv;
-                state[gg * kStateStride + 1] = l_all;
-            }
-        } else if (out != nullptr) {
-            out[gg * kHeadDim + d] = ElemOps<T>::from_float(l_all > 0.f ? o / l_all : 0.f);
+        for (int q = 1; q < G; ++q) {
+            Mg = q == gg ? m_all[q] : Mg;
+            Lg = q == gg ? l_all[q] : Lg;
         }
+        emit_merged<G, T, kXg>(k, gg, d, o, Mg, Lg, out, state, xg);
     }
 }
 
@@ -618,6 +708,80 @@ __device__ __forceinline__ Item producer_next(const DecodeParams& p, int s, int 
     return producer_item<BOX_ROWS>(p, (int)blockIdx.x + s * (int)gridDim.x, lane, pid0);
 }
 
+// ---------------------------------------------------------------- sharded step
+// Gather buffer of rank r: [2 parities][world writers][xg_bcap rows][Hq][130]
+// LL words.  The sink of a finished (row, KV head) points at this rank's part
+// of it in every rank's buffer.
+template <int G>
+__device__ __forceinline__ void xg_make_sink(const DecodeParams& p, int row, int kvh,
+                                             unsigned epoch, XgSink<G>& xs) {
+    const size_t part = (size_t)p.xg_bcap * p.Hq * kStateStride;
+    xs.gather = p.xg_gather;
+    xs.off = ((size_t)(epoch & 1u) * p.xg_world + p.xg_rank) * part +
+             ((size_t)row * p.Hq + (size_t)kvh * G) * kStateStride;
+    xs.world = p.xg_world;
+    xs.rank = p.xg_rank;
+    xs.epoch = epoch;
+}
+
+// After emit_merged has pushed this thread's values to every peer: wait
+// (bounded) until every peer's words of the same (head, dim) values carry
+// this step's number in this rank's own buffer, merge the world parts
+// (log-sum-exp, own part from registers) and write the output row.  Rows are
+// finished in the same order on every rank and all CTAs of the launch are
+// resident, so each wait ends once the peers reach that row.
+template <int G, typename T>
+__device__ __forceinline__ void xg_collect(const DecodeParams& p, int row, int kvh, int out_row,
+                                           const XgSink<G>& xs, volatile int* s_flags) {
+    constexpr int NT = kConsumerWarps * 32;
+    const int t = threadIdx.x % NT;
+    const int world = p.xg_world;
+    const size_t part = (size_t)p.xg_bcap * p.Hq * kStateStride;
+    const unsigned long long* base =
+        p.xg_gather[p.xg_rank] + (size_t)(xs.epoch & 1u) * world * part +
+        ((size_t)row * p.Hq + (size_t)kvh * G) * kStateStride;
+    T* o = out_row >= 0 ? reinterpret_cast<T*>(p.out) + ((size_t)out_row * p.Hq + kvh * G) * kHeadDim
+                        : nullptr;
+    const unsigned long long start = global_timer_ns();
+#pragma unroll
+    for (int k = 0; k < G * kHeadDim / NT; ++k) {
+        const int idx = t + k * NT;
+        const int gg = idx / kHeadDim;
+        const int d = idx % kHeadDim;
+        float mx = xs.m[k], lsum = xs.l[k], osum = xs.o[k];
+        for (int r = 0; r < world; ++r) {
+            if (r == p.xg_rank) continue;
+            const unsigned long long* w = base + r * part + gg * kStateStride;
+            unsigned long long wm, wl, wa;
+            while (true) {
+                wm = ld_relaxed_sys_u64(w);
+                wl = ld_relaxed_sys_u64(w + 1);
+                wa = ld_relaxed_sys_u64(w + 2 + d);
+                if ((unsigned)(wm >> 32) == xs.epoch && (unsigned)(wl >> 32) == xs.epoch &&
+                    (unsigned)(wa >> 32) == xs.epoch)
+                    break;
+                if (s_flags[2] != 0) break;
+                if (global_timer_ns() - start > kPeerWaitLimitNs) {
+                    s_flags[2] = 1;
+                    raise_error(p.error, kErrPeer);
+                    break;
+                }
+            }
+            const float m2 = __uint_as_float((unsigned)wm);
+            const float l2 = __uint_as_float((unsigned)wl);
+            const float a2 = __uint_as_float((unsigned)wa);
+            const float mn = fmaxf(mx, m2);
+            const float w1 = fast_exp2((mx - mn) * kLog2e);
+            const float w2 = fast_exp2((m2 - mn) * kLog2e);
+            lsum = lsum * w1 + l2 * w2;
+            osum = osum * w1 + a2 * w2;
+            mx = mn;
+        }
+        if (o != nullptr && s_flags[2] == 0)
+            o[gg * kHeadDim + d] = ElemOps<T>::from_float(lsum > 0.f ? osum / lsum : 0.f);
+    }
+}
+
 template <int G, typename T, int BOX_ROWS, int NSLOTS, int LOAD>
 __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     pkv_decode_kernel(const __grid_constant__ DecodeParams p,
@@ -641,7 +805,8 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     uint64_t* desc_full = empty_bar + NSLOTS;
     uint64_t* desc_empty = desc_full + kDescSlots;
     uint8_t* s_flag_bytes = reinterpret_cast<uint8_t*>(desc_empty + kDescSlots);
-    volatile int* s_flags = reinterpret_cast<volatile int*>(s_flag_bytes);  // [0] abort, [1] last
+    // [0] abort, [1] last task of a row, [2] a peer exchange gave up
+    volatile int* s_flags = reinterpret_cast<volatile int*>(s_flag_bytes);
     float* s_mstat = reinterpret_cast<float*>(s_flag_bytes + 64);
     float* s_lstat = s_mstat + 2 * kConsumerWarps * 8;
     float* s_merge = s_lstat + 2 * kConsumerWarps * 8;
@@ -681,6 +846,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
         }
         s_flags[0] = 0;
         s_flags[1] = 0;
+        s_flags[2] = 0;
         fence_mbar_init();
     }
     __syncthreads();
@@ -875,6 +1041,11 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     uint32_t gbase = 0;
     int buf = 0;
     bool aborted = false;
+    // step number of a sharded launch: advanced only after every CTA of the
+    // launch has finished, so all CTAs read the same value here
+    const unsigned xg_epoch = p.xg_world > 0 ? ld_relaxed_gpu_u32(p.xg_counters) : 0u;
+    const bool state_mode = p.state_out != nullptr;
+    const bool xg_mode = p.xg_world > 0;
 
     for (int s = 0; s < my_items; ++s) {
         if (s == my_items - 1) griddep_launch_dependents();
@@ -1076,9 +1247,14 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
 
         const bool rect = p.work_items == nullptr && p.auto_groups == 0;
         const bool direct = it.row_splits == 1;
-        const bool write_direct_out = direct && p.state_out == nullptr && it.out_row >= 0 &&
+        const bool write_direct_out = direct && !state_mode && !xg_mode && it.out_row >= 0 &&
                                       (!rect || it.tok_end > it.tok_begin);
-        for (int idx = threadIdx.x; idx < G * kHeadDim; idx += kConsumerWarps * 32) {
+        XgSink<G> xs;
+        const bool xg_direct = direct && xg_mode && !aborted;
+        if (xg_direct) xg_make_sink<G>(p, it.row, it.kvh, xg_epoch, xs);
+#pragma unroll
+        for (int k = 0; k < G * kHeadDim / (kConsumerWarps * 32); ++k) {
+            const int idx = threadIdx.x + k * kConsumerWarps * 32;
             const int g = idx / kHeadDim;
             const int d = idx % kHeadDim;
             float mx = -INFINITY;
@@ -1094,7 +1270,9 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
             }
             const float mnat = mx == -INFINITY ? kNegFltMax : mx * kLn2;
             if (direct) {
-                if (p.state_out != nullptr) {
+                if (xg_direct) {
+                    emit_merged<G, T, true>(k, g, d, osum, mnat, lsum, nullptr, nullptr, xs);
+                } else if (state_mode) {
                     float* st =
                         p.state_out + ((size_t)it.row * p.Hq + it.kvh * G + g) * kStateStride;
                     st[2 + d] = osum;
@@ -1116,6 +1294,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                 }
             }
         }
+        if (xg_direct) xg_collect<G, T>(p, it.row, it.kvh, it.out_row, xs, s_flags);
         if (!direct && it.slot >= 0) {
             if (p.merge_counters != nullptr && !rect) {
                 // fused merge: the last task of this (row, kvh) merges all of
@@ -1136,18 +1315,42 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                     const int qh0 = it.kvh * G;
                     T* o = nullptr;
                     float* st = nullptr;
-                    if (p.state_out != nullptr) {
+                    const bool xg_merge = xg_mode && !aborted;
+                    if (xg_merge) {
+                        xg_make_sink<G>(p, it.row, it.kvh, xg_epoch, xs);
+                    } else if (state_mode) {
                         st = p.state_out + ((size_t)it.row * p.Hq + qh0) * kStateStride;
                     } else if (it.out_row >= 0) {
                         o = reinterpret_cast<T*>(p.out) + ((size_t)it.out_row * p.Hq + qh0) * kHeadDim;
                     }
-                    merge_slots<G, T, kConsumerWarps, true>(p.part_m, p.part_l, p.part_acc, it.slot - it.split,
-                                            it.row_splits, p.Hq, qh0, ms, o, st);
+                    if (xg_merge) {
+                        merge_slots<G, T, kConsumerWarps, true, true>(
+                            p.part_m, p.part_l, p.part_acc, it.slot - it.split, it.row_splits,
+                            p.Hq, qh0, ms, nullptr, nullptr, xs);
+                        xg_collect<G, T>(p, it.row, it.kvh, it.out_row, xs, s_flags);
+                    } else {
+                        merge_slots<G, T, kConsumerWarps, true, false>(
+                            p.part_m, p.part_l, p.part_acc, it.slot - it.split, it.row_splits,
+                            p.Hq, qh0, ms, o, st, xs);
+                    }
                     consumer_bar_sync();  // merge scratch aliases the combine buffers
                 }
             }
         }
         buf ^= 1;
+    }
+    if (p.xg_world > 0) {
+        // the last CTA to finish advances the step number for the next launch
+        consumer_bar_sync();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            const unsigned done = atomicAdd(p.xg_counters + 1, 1u);
+            if (done == gridDim.x - 1) {
+                p.xg_counters[1] = 0u;
+                __threadfence();
+                atomicAdd(p.xg_counters, 1u);
+            }
+        }
     }
 }
 
@@ -1254,7 +1457,9 @@ __global__ void __launch_bounds__(kHeadDim)
         o = reinterpret_cast<T*>(p.out) + ((size_t)orow * p.Hq + qh0) * kHeadDim;
     }
     MergeSmem ms{s_w, s_w + kMergeChunk * 8, s_red};
-    merge_slots<G, T, 4, false>(p.part_m, p.part_l, p.part_acc, s0, s1 - s0, p.Hq, qh0, ms, o, st);
+    XgSink<G> unused;
+    merge_slots<G, T, 4, false, false>(p.part_m, p.part_l, p.part_acc, s0, s1 - s0, p.Hq, qh0, ms,
+                                       o, st, unused);
 }
 
 // Merges n_parts blocks of combined states [n_parts][B][Hq][130] into the

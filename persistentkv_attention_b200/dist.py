@@ -103,3 +103,41 @@ class SequenceShardedDecoder:
             plan.host.total_slots, True)
         states = gather_states(st, self.group)
         ops.combine_states(states, out)
+
+
+def make_exchange(hq: int, hkv: int, max_batch: int, group=None):
+    """Creates this rank's ``ops.Exchange`` and maps every peer's buffer.
+
+    The IPC handles travel over the process group (``all_gather_object``);
+    a barrier makes sure every rank is connected before any kernel uses it."""
+    from . import ops
+
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    x = ops.Exchange(world, rank, max_batch, hq, hkv)
+    if world > 1:
+        handles = [None] * world
+        dist.all_gather_object(handles, x.handle, group=group)
+        x.connect(handles)
+        dist.barrier(group=group)
+    return x
+
+
+class FusedShardedDecoder:
+    """One rank of a sequence-sharded decode whose state exchange runs inside
+    the decode kernel (peer stores over NVLink, no NCCL call per step)."""
+
+    def __init__(self, engine, max_batch: int, group=None):
+        self.engine = engine
+        self.exchange = make_exchange(engine.hq, engine.hkv, max_batch, group)
+
+    def step(self, plan, q_source: torch.Tensor, out: torch.Tensor) -> None:
+        self.engine.run_sharded(plan, q_source, out, self.exchange)
+
+    def close(self, group=None) -> None:
+        """Frees the exchange once no rank's kernel can still store into it."""
+        torch.cuda.synchronize()
+        if dist.is_initialized() and dist.get_world_size(group) > 1:
+            dist.barrier(group=group)
+        self.exchange.close()
+

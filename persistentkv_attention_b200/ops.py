@@ -346,6 +346,97 @@ def paged_attention_auto_state(q_source, k_pages, v_pages, block_table, seq_lens
         _DTYPES[q_source.dtype], _stream()))
 
 
+class Exchange:
+    """This rank's end of the fused sharded-decode exchange (``pkv_exchange``).
+
+    Create one per rank on its own device, gather every rank's ``handle`` (in
+    rank order) and pass them to :meth:`connect`; ``world == 1`` needs no
+    connect.  ``close`` synchronises the device and frees the buffer: call it
+    only after every rank has synchronised its device (a barrier), since a
+    peer's kernel stores into this rank's buffer.
+    """
+
+    def __init__(self, world: int, rank: int, max_batch: int, hq: int, hkv: int):
+        import ctypes
+
+        lib = _native.load()
+        self._ptr = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(_native.EXCHANGE_HANDLE_BYTES)
+        _native.check(lib.pkv_exchange_create(world, rank, max_batch, hq, hkv,
+                                              ctypes.byref(self._ptr), buf))
+        self.handle = bytes(buf.raw)
+        self.world, self.rank, self.max_batch, self.hq, self.hkv = world, rank, max_batch, hq, hkv
+        self.device = torch.cuda.current_device()
+
+    def connect(self, handles) -> None:
+        """``handles``: every rank's ``handle`` bytes, in rank order."""
+        if len(handles) != self.world:
+            raise RuntimeError("one handle per rank is required")
+        blob = b"".join(bytes(h) for h in handles)
+        _native.check(_native.load().pkv_exchange_connect(self._ptr, blob))
+
+    @property
+    def ptr(self):
+        if not self._ptr:
+            raise RuntimeError("exchange is closed")
+        return self._ptr
+
+    def close(self) -> None:
+        if self._ptr:
+            _native.check(_native.load().pkv_exchange_destroy(self._ptr))
+            self._ptr = type(self._ptr)()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def exchange_bytes(world: int, max_batch: int, hq: int, hkv: int) -> int:
+    return int(_native.load().pkv_exchange_bytes(world, max_batch, hq, hkv))
+
+
+def paged_attention_sharded(q_source, k_pages, v_pages, block_table, seq_lens, output, workspace,
+                            merge_counters, exchange: Exchange, q_indices=None,
+                            out_indices=None) -> None:
+    """One step of sequence-sharded decode with the state exchange fused into
+    the kernel: ``block_table`` / ``seq_lens`` hold this rank's page range of
+    every row; every rank gets the merged ``output``.  All ranks must call it
+    with the same batch, in the same order.  No counterpart in the reference."""
+    _check_tensor(q_source, "q_source", tuple(_DTYPES), 3)
+    hkv, physical_pages = _check_kv(q_source, k_pages, v_pages, k_pages.size(2))
+    _check_tensor(block_table, "block_table", torch.int32, 2)
+    _check_tensor(seq_lens, "seq_lens", torch.int32, 1)
+    _check_tensor(output, "output", q_source.dtype, 3)
+    _check_tensor(merge_counters, "merge_counters", torch.int32, 2)
+    b = block_table.size(0)
+    hq, d = q_source.size(1), q_source.size(2)
+    if seq_lens.size(0) != b:
+        raise RuntimeError("seq_lens batch mismatch")
+    if not (output.size(1) == hq and output.size(2) == d):
+        raise RuntimeError("output shape must match q head dimensions")
+    if not (merge_counters.size(0) == b and merge_counters.size(1) == hkv):
+        raise RuntimeError("merge_counters shape mismatch")
+    ptrs = []
+    for name, t in (("q_indices", q_indices), ("out_indices", out_indices)):
+        if t is None:
+            ptrs.append(None)
+        else:
+            _check_tensor(t, name, torch.int32, 1)
+            if t.size(0) != b:
+                raise RuntimeError(f"{name} batch mismatch")
+            ptrs.append(t.data_ptr())
+    _check_supported_gqa(hq, hkv)
+    ws_ptr, ws_bytes = _workspace(workspace)
+    _native.check(_native.load().pkv_paged_attention_sharded(
+        q_source.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), block_table.data_ptr(),
+        seq_lens.data_ptr(), ptrs[0], ptrs[1], output.data_ptr(), ws_ptr, ws_bytes,
+        merge_counters.data_ptr(), exchange.ptr, b, q_source.size(0), output.size(0), hq, hkv, d,
+        physical_pages, k_pages.size(2), block_table.size(1), _DTYPES[q_source.dtype],
+        _stream()))
+
+
 def auto_workspace_bytes(batch: int, hq: int, hkv: int, sm_count: int = 0) -> int:
     """Workspace of ``paged_attention_auto`` (sm_count 0: the current device)."""
     return int(_native.load().pkv_auto_workspace_bytes(batch, hq, hkv, sm_count))

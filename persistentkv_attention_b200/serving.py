@@ -194,6 +194,16 @@ class DecodeEngine:
             q_source, self.k_pages, self.v_pages, f["block_table"], f["seq_lens"], state_out,
             self._workspace, f["q_indices"], counters if self.fused else None)
 
+    def run_sharded(self, plan: StepPlan, q_source: torch.Tensor, out: torch.Tensor,
+                    exchange) -> None:
+        """One sequence-sharded step: this GPU's pages, exchange and merge fused
+        into one launch (``ops.paged_attention_sharded``)."""
+        f = plan.fields
+        counters = self._counters[: plan.batch * self.hkv].view(plan.batch, self.hkv)
+        ops.paged_attention_sharded(
+            q_source, self.k_pages, self.v_pages, f["block_table"], f["seq_lens"], out,
+            self._workspace, counters, exchange, f["q_indices"], f["out_indices"])
+
     def capture(self, plan: StepPlan, q_source: torch.Tensor, out: torch.Tensor,
                 stream: torch.cuda.Stream | None = None) -> torch.cuda.CUDAGraph:
         self.run(plan, q_source, out)          # first call outside capture (attributes, maps)

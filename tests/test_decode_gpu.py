@@ -397,3 +397,60 @@ def test_auto_state_sequence_shards(fused, world):
     ops.combine_states(torch.stack(states), out, d["out_indices"])
     torch.cuda.synchronize()
     assert_close(out, c.oracle(), "f16", f"auto state x{world} fused={fused}")
+
+
+def test_sharded_fused_exchange_single_rank():
+    """The fused-exchange step with world 1: every CTA flags and merges its
+    own part; several launches (eager and graph-replayed) advance the step
+    number and alternate the gather-buffer parity."""
+    from persistentkv_attention_b200 import dist as pdist
+
+    x = ops.Exchange(1, 0, 8, 32, 8)
+    try:
+        cases = [make_case(lens, seed=70 + i, indexed=True)
+                 for i, lens in enumerate([[30000, 33, 0, 777], [5000], [1, 2, 3, 4, 5, 6, 7, 9000]])]
+        for c in cases:
+            d = c.cuda()
+            b = len(c.seq_lens)
+            bt, sl = pdist.shard_rows(c.block_table, c.seq_lens, 16, 1, 0)
+            ws = torch.empty(ops.auto_workspace_bytes(b, 32, 8) // 4, device="cuda")
+            counters = torch.zeros(b, 8, device="cuda", dtype=torch.int32)
+            out = torch.full((c.out_rows, 32, 128), float("nan"), device="cuda",
+                             dtype=torch.float16)
+            bt_d, sl_d = torch.from_numpy(bt).cuda(), torch.from_numpy(sl).cuda()
+
+            def step():
+                ops.paged_attention_sharded(d["q_source"], d["k_pages"], d["v_pages"], bt_d, sl_d,
+                                            out, ws, counters, x, d["q_indices"],
+                                            d["out_indices"])
+
+            for _ in range(3):
+                step()
+            torch.cuda.synchronize()
+            assert (counters == 0).all()
+            assert_close(out, c.oracle(), "f16", f"sharded x1 B{b}")
+            graph = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(graph, stream=s):
+                    step()
+            first = out.clone()
+            out.fill_(float("nan"))
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out[torch.from_numpy(c.out_indices).long().cuda()],
+                               first[torch.from_numpy(c.out_indices).long().cuda()])
+        # a batch beyond the exchange's capacity is refused before launch
+        c = make_case([100] * 9, seed=79)
+        d = c.cuda()
+        with pytest.raises(_native.PkvError) as err:
+            ops.paged_attention_sharded(
+                d["q_source"], d["k_pages"], d["v_pages"], d["block_table"], d["seq_lens"],
+                torch.empty(9, 32, 128, device="cuda", dtype=torch.float16),
+                torch.empty(ops.auto_workspace_bytes(9, 32, 8) // 4, device="cuda"),
+                torch.zeros(9, 8, device="cuda", dtype=torch.int32), x)
+        assert err.value.status == _native.PKV_ERR_CAPACITY
+    finally:
+        torch.cuda.synchronize()
+        x.close()
