@@ -15,9 +15,10 @@ Reported (one JSON line on rank 0):
               intervals around graph-replayed decode steps; before every step,
               outside the intervals, L2 is flushed by a 256 MiB write and a
               256 MiB read (so no dirty lines are left for the timed step);
-  e2e         tokens/s through the public operator API from pinned host
-              buffers: host work-queue build, H2D of q rows + metadata,
-              decode, D2H of the output, per step;
+  e2e         tokens/s through the public API from host buffers
+              (DecodeEngine.step_host -> pkv_engine_step_host): per step,
+              staging of lengths + block rows, H2D of metadata and pinned q
+              rows, decode, D2H of the output into pinned memory;
   roofline    algorithmic K/V bytes per step / step interval vs the measured
               HBM copy bandwidth;
   cpu_baseline the reference's own fp32 CPU decode (cpu_gqa_attention built
@@ -359,6 +360,8 @@ def run_engine_arm(args) -> None:
         v = plan.views(plan.buf)
         host_rows.append((list(state.lengths), v["block_table"].numpy().copy(),
                           torch.stack([q_host[r] for r in state.active_ids]).pin_memory()))
+    engine.reserve_host(scratch, max(len(r[0]) for r in host_rows),
+                        max(r[1].shape[1] for r in host_rows))
     with torch.cuda.stream(stream):
         for j in sched[: args.warmup]:
             lens, rows, qh = host_rows[j]

@@ -208,6 +208,37 @@ pkv_status pkv_paged_attention_sharded(
     int physical_pages, int page_size, int max_pages,
     pkv_dtype dtype, void* stream);
 
+/* ---- Native host step ----
+ * A decode engine over one paged K/V pool that takes a step from host
+ * buffers to host buffers in one call: it stages the block-table rows and
+ * lengths in its own pinned memory and runs pkv_paged_attention_auto with
+ * the fused merge on `stream`, the kernel reading metadata and query rows
+ * from pinned host memory and writing the output rows into out_host over
+ * the host link (no separate copies).  Synchronise `stream` before reading
+ * out_host.  q_host and out_host must be page-locked and mapped
+ * (cudaHostAlloc, or a framework's pinned allocator), else
+ * PKV_ERR_INVALID_ARGUMENT.  The native counterpart of the reference
+ * harness's per-step Python (tests/benchmark_serving_trace.py:838-946). */
+typedef struct pkv_engine pkv_engine;
+
+/* k_pages / v_pages: device pools [physical_pages][Hkv][page_size][128].
+ * Allocates device buffers for max_batch rows of up to max_pages pages. */
+pkv_status pkv_engine_create(const void* k_pages, const void* v_pages, int physical_pages,
+                             int Hq, int Hkv, int head_dim, int page_size, pkv_dtype dtype,
+                             int max_batch, int max_pages, pkv_engine** out);
+
+/* One step: row b attends to seq_lens[b] tokens of block_table[b][0..row_pages)
+ * (host int32, row stride row_pages), query q_host[b] ([B][Hq][128]) and
+ * writes out_host[b].  h2d_bytes / d2h_bytes (may be NULL) receive the bytes
+ * that cross the host link each way. */
+pkv_status pkv_engine_step_host(pkv_engine* engine, const int32_t* seq_lens,
+                                const int32_t* block_table, int B, int row_pages,
+                                const void* q_host, void* out_host, void* stream,
+                                size_t* h2d_bytes, size_t* d2h_bytes);
+
+/* Synchronises the device and frees the engine's buffers. */
+pkv_status pkv_engine_destroy(pkv_engine* engine);
+
 /* Workspace bytes of pkv_paged_attention_auto: (B + NG) * Hq * 130 * 4 with
  * NG = 2 * sm_count / Hkv; sm_count <= 0 queries the current device. */
 size_t pkv_auto_workspace_bytes(int B, int Hq, int Hkv, int sm_count);

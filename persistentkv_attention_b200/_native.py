@@ -107,6 +107,12 @@ SIGNATURES = {
         [_P, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, c_int, c_int, c_int, c_int, c_int,
          c_int, c_int, c_int, c_int, _P],
     ),
+    "pkv_engine_create": (
+        c_int, [_P, _P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                POINTER(c_void_p)]),
+    "pkv_engine_step_host": (
+        c_int, [_P, _P, _P, c_int, c_int, _P, _P, _P, POINTER(c_size_t), POINTER(c_size_t)]),
+    "pkv_engine_destroy": (c_int, [_P]),
     "pkv_exchange_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "pkv_exchange_create": (
         c_int, [c_int, c_int, c_int, c_int, c_int, POINTER(c_void_p), c_void_p]),

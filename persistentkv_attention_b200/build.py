@@ -23,7 +23,7 @@ BUILD_DIR = PKG_DIR / "_build"
 LIB_DIR = PKG_DIR / "lib"
 LIB_PATH = LIB_DIR / "libpkv_b200.so"
 
-SOURCES = ["pkv_api.cu", "pkv_sched.cpp"]
+SOURCES = ["pkv_api.cu", "pkv_sched.cpp", "pkv_engine.cpp"]
 HEADERS = ["pkv_device.cuh", "pkv_kernels.cuh"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden"]

@@ -56,6 +56,16 @@ pkv_status ok_status() {
     return PKV_OK;
 }
 
+}  // namespace
+
+namespace pkv_internal {
+// Error reporting shared with the other translation units of the library.
+pkv_status set_error(pkv_status st, const char* msg) { return fail(st, "%s", msg); }
+void clear_error() { t_last_error[0] = '\0'; }
+}  // namespace pkv_internal
+
+namespace {
+
 // ------------------------------------------------------------ device state
 struct DeviceState {
     std::atomic<int> ready{0};

@@ -1,0 +1,208 @@
+// pkv_engine.cpp -- native host step of the decode engine (declared in
+// include/pkv_b200.h): one call takes a decode step from host buffers to
+// host buffers.  It stages the step's metadata (block-table rows, lengths)
+// in its own pinned memory and launches the device-scheduled decode
+// (pkv_paged_attention_auto, fused merge) on the caller's stream with host
+// pointers: the kernel reads metadata and query rows from pinned host
+// memory and writes the output rows into the caller's pinned buffer over
+// PCIe / C2C.  No separate copy is queued, which saves each copy's launch
+// and completion latency (several microseconds apiece).
+//
+// The reference harness does the same per step from Python
+// (tests/benchmark_serving_trace.py:838-946, run_persistentkv_step: tensors
+// built on the host, copied, the extension called, the output read back);
+// this is its native counterpart for hosts that bind the C ABI directly.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "pkv_b200.h"
+
+namespace pkv_internal {
+// pkv_api.cu: records the message returned by pkv_last_error_message
+pkv_status set_error(pkv_status st, const char* msg);
+void clear_error();
+}  // namespace pkv_internal
+
+namespace {
+
+constexpr int kHeadDim = 128;
+constexpr int kStaging = 2;  // pinned metadata buffers in rotation
+
+pkv_status efail(pkv_status st, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    return pkv_internal::set_error(st, buf);
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+struct pkv_engine {
+    const void* k_pages;
+    const void* v_pages;
+    int physical_pages, hq, hkv, page_size, max_batch, max_pages, device;
+    pkv_dtype dtype;
+    size_t elem;
+    // device: workspace, then merge counters
+    char* dev;
+    void* d_ws;
+    size_t ws_bytes;
+    int32_t* d_counters;
+    // pinned staging [block table B * row_pages | seq_lens B] int32, read by
+    // the kernel in place
+    int32_t* h_meta[kStaging];
+    int32_t* dh_meta[kStaging];    // the same buffers as the device addresses them
+    cudaEvent_t staged[kStaging];  // the launch that read staging buffer i has finished
+    int next;
+    const void* checked[2];        // last q / out host pointers found page-locked
+    void* mapped[2];               // and their device addresses
+};
+
+extern "C" {
+
+pkv_status pkv_engine_create(const void* k_pages, const void* v_pages, int physical_pages,
+                             int Hq, int Hkv, int head_dim, int page_size, pkv_dtype dtype,
+                             int max_batch, int max_pages, pkv_engine** out) {
+    if (out == nullptr) return efail(PKV_ERR_INVALID_ARGUMENT, "out must not be null");
+    *out = nullptr;
+    if (k_pages == nullptr || v_pages == nullptr)
+        return efail(PKV_ERR_INVALID_ARGUMENT, "k_pages and v_pages must be device pointers");
+    if (head_dim != kHeadDim)
+        return efail(PKV_ERR_UNSUPPORTED, "PersistentKV extension currently requires d=128");
+    if (dtype != PKV_DTYPE_F16 && dtype != PKV_DTYPE_BF16)
+        return efail(PKV_ERR_UNSUPPORTED, "unsupported dtype");
+    if (physical_pages <= 0 || Hq <= 0 || Hkv <= 0 || page_size <= 0 || max_batch <= 0 ||
+        max_pages <= 0)
+        return efail(PKV_ERR_INVALID_ARGUMENT, "engine dimensions must be positive");
+    pkv_engine* e = new pkv_engine();
+    std::memset(e, 0, sizeof(*e));
+    e->k_pages = k_pages;
+    e->v_pages = v_pages;
+    e->physical_pages = physical_pages;
+    e->hq = Hq;
+    e->hkv = Hkv;
+    e->page_size = page_size;
+    e->max_batch = max_batch;
+    e->max_pages = max_pages;
+    e->dtype = dtype;
+    e->elem = 2;
+    cudaGetDevice(&e->device);
+    const size_t meta_bytes = (size_t)max_batch * (max_pages + 1) * sizeof(int32_t);
+    e->ws_bytes = pkv_auto_workspace_bytes(max_batch, Hq, Hkv, 0);
+    const size_t ctr_bytes = (size_t)max_batch * Hkv * sizeof(int32_t);
+    size_t off_c = align_up(e->ws_bytes, 256);
+    size_t total = off_c + ctr_bytes;
+    cudaError_t err = e->ws_bytes == 0 ? cudaErrorInvalidValue
+                                       : cudaMalloc(reinterpret_cast<void**>(&e->dev), total);
+    if (err == cudaSuccess) err = cudaMemset(e->dev + off_c, 0, ctr_bytes);
+    for (int i = 0; i < kStaging && err == cudaSuccess; ++i) {
+        err = cudaHostAlloc(reinterpret_cast<void**>(&e->h_meta[i]), meta_bytes,
+                            cudaHostAllocMapped);
+        if (err == cudaSuccess)
+            err = cudaHostGetDevicePointer(reinterpret_cast<void**>(&e->dh_meta[i]),
+                                           e->h_meta[i], 0);
+        if (err == cudaSuccess)
+            err = cudaEventCreateWithFlags(&e->staged[i], cudaEventDisableTiming);
+    }
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        pkv_engine_destroy(e);
+        return efail(PKV_ERR_CUDA, "engine allocation failed: %s", cudaGetErrorString(err));
+    }
+    e->d_ws = e->dev;
+    e->d_counters = reinterpret_cast<int32_t*>(e->dev + off_c);
+    *out = e;
+    pkv_internal::clear_error();
+    return PKV_OK;
+}
+
+pkv_status pkv_engine_step_host(pkv_engine* e, const int32_t* seq_lens,
+                                const int32_t* block_table, int B, int row_pages,
+                                const void* q_host, void* out_host, void* stream,
+                                size_t* h2d_bytes, size_t* d2h_bytes) {
+    if (e == nullptr) return efail(PKV_ERR_INVALID_ARGUMENT, "engine must not be null");
+    if (B < 0 || B > e->max_batch)
+        return efail(PKV_ERR_CAPACITY, "batch %d outside [0, %d]", B, e->max_batch);
+    if (row_pages <= 0 || row_pages > e->max_pages)
+        return efail(PKV_ERR_CAPACITY, "row_pages %d outside [1, %d]", row_pages, e->max_pages);
+    if (B > 0 && (seq_lens == nullptr || block_table == nullptr || q_host == nullptr ||
+                  out_host == nullptr))
+        return efail(PKV_ERR_INVALID_ARGUMENT, "host buffers must not be null");
+    if (h2d_bytes) *h2d_bytes = 0;
+    if (d2h_bytes) *d2h_bytes = 0;
+    if (B == 0) return PKV_OK;
+    // the kernel dereferences q_host / out_host: they must be page-locked
+    const void* host_ptrs[2] = {q_host, out_host};
+    for (int k = 0; k < 2; ++k) {
+        if (host_ptrs[k] == e->checked[k]) continue;
+        cudaPointerAttributes attr;
+        cudaError_t aerr = cudaPointerGetAttributes(&attr, host_ptrs[k]);
+        if (aerr != cudaSuccess || attr.type != cudaMemoryTypeHost ||
+            attr.devicePointer == nullptr) {
+            cudaGetLastError();
+            return efail(PKV_ERR_INVALID_ARGUMENT,
+                         "%s must be page-locked host memory mapped for the device "
+                         "(cudaHostAlloc / pinned)",
+                         k == 0 ? "q_host" : "out_host");
+        }
+        e->checked[k] = host_ptrs[k];
+        e->mapped[k] = attr.devicePointer;
+    }
+    // staging buffer: wait until the launch that last read it has finished
+    const int i = e->next;
+    e->next = (e->next + 1) % kStaging;
+    cudaError_t err = cudaEventSynchronize(e->staged[i]);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return efail(PKV_ERR_CUDA, "waiting for the staging buffer failed: %s",
+                     cudaGetErrorString(err));
+    }
+    int32_t* h = e->h_meta[i];
+    const size_t bt_words = (size_t)B * row_pages;
+    std::memcpy(h, block_table, bt_words * sizeof(int32_t));
+    std::memcpy(h + bt_words, seq_lens, (size_t)B * sizeof(int32_t));
+    const size_t meta_bytes = (bt_words + B) * sizeof(int32_t);
+    const size_t q_bytes = (size_t)B * e->hq * kHeadDim * e->elem;
+    int32_t* dh = e->dh_meta[i];
+    pkv_status st = pkv_paged_attention_auto(
+        e->mapped[0], e->k_pages, e->v_pages, dh, dh + bt_words, nullptr, nullptr, e->mapped[1],
+        e->d_ws,
+        e->ws_bytes, e->d_counters, B, B, B, e->hq, e->hkv, kHeadDim, e->physical_pages,
+        e->page_size, row_pages, e->dtype, stream);
+    if (st != PKV_OK) return st;  // message already recorded
+    err = cudaEventRecord(e->staged[i], static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return efail(PKV_ERR_CUDA, "event record failed: %s", cudaGetErrorString(err));
+    }
+    if (h2d_bytes) *h2d_bytes = meta_bytes + q_bytes;
+    if (d2h_bytes) *d2h_bytes = q_bytes;
+    pkv_internal::clear_error();
+    return PKV_OK;
+}
+
+pkv_status pkv_engine_destroy(pkv_engine* e) {
+    if (e == nullptr) return PKV_OK;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (prev != e->device) cudaSetDevice(e->device);
+    cudaDeviceSynchronize();
+    for (int i = 0; i < kStaging; ++i) {
+        if (e->staged[i] != nullptr) cudaEventDestroy(e->staged[i]);
+        if (e->h_meta[i] != nullptr) cudaFreeHost(e->h_meta[i]);
+    }
+    if (e->dev != nullptr) cudaFree(e->dev);
+    cudaGetLastError();
+    if (prev >= 0 && prev != e->device) cudaSetDevice(prev);
+    delete e;
+    return PKV_OK;
+}
+
+}  // extern "C"

@@ -90,7 +90,9 @@ def _workspace(workspace: torch.Tensor):
 
 
 def _stream() -> int:
-    return torch.cuda.current_stream().cuda_stream
+    """Raw ``cudaStream_t`` of the current stream on the current device (the
+    raw getter avoids building a ``torch.cuda.Stream`` object per call)."""
+    return torch._C._cuda_getCurrentRawStream(torch.cuda.current_device())
 
 
 def _positive(value: int, name: str) -> None:

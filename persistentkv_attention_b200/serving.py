@@ -204,6 +204,38 @@ class DecodeEngine:
             q_source, self.k_pages, self.v_pages, f["block_table"], f["seq_lens"], out,
             self._workspace, counters, exchange, f["q_indices"], f["out_indices"])
 
+    def _step_host_native(self, seq_lens, block_rows, q_host, out_host, scratch):
+        seq = np.ascontiguousarray(seq_lens, dtype=np.int32)
+        rows = np.ascontiguousarray(block_rows, dtype=np.int32)
+        b, width = rows.shape
+        if seq.shape != (b,):
+            raise RuntimeError("seq_lens batch mismatch")
+        if not (q_host.is_contiguous() and out_host.is_contiguous()):
+            raise RuntimeError("q_host and out_host must be contiguous")
+        if q_host.dtype != self.dtype or out_host.dtype != self.dtype:
+            raise RuntimeError("q_host / out_host dtype must match the K/V pool")
+        if (q_host.shape[0] < b or out_host.shape[0] < b or q_host.shape[1:] != (self.hq, HEAD_DIM)
+                or out_host.shape[1:] != (self.hq, HEAD_DIM)):
+            raise RuntimeError("q_host / out_host shape mismatch")
+        native = scratch.get("native")
+        if native is None or native.max_batch < b or native.max_pages < width:
+            # grow geometrically: re-creating the engine synchronises the device
+            mb = max(b, 2 * native.max_batch if native else b)
+            mp = max(width, 2 * native.max_pages if native else width)
+            native = self.reserve_host(scratch, mb, mp)
+        return native.step(seq, rows, q_host, out_host)
+
+    def reserve_host(self, scratch: dict, max_batch: int, max_pages: int) -> "NativeEngine":
+        """Sizes the native host-step engine kept in ``scratch`` for batches of
+        up to ``max_batch`` rows of ``max_pages`` pages (call before timing)."""
+        native = scratch.get("native")
+        if native is not None and native.max_batch >= max_batch and native.max_pages >= max_pages:
+            return native
+        if native is not None:
+            native.close()
+        native = scratch["native"] = NativeEngine(self, max_batch, max_pages)
+        return native
+
     def capture(self, plan: StepPlan, q_source: torch.Tensor, out: torch.Tensor,
                 stream: torch.cuda.Stream | None = None) -> torch.cuda.CUDAGraph:
         self.run(plan, q_source, out)          # first call outside capture (attributes, maps)
@@ -220,7 +252,12 @@ class DecodeEngine:
 
         ``q_host`` [B, Hq, 128] and ``out_host`` are pinned host tensors;
         ``scratch`` keeps the pinned staging and device buffers between calls.
+        With the device-side schedule the whole step is one native call
+        (``pkv_engine_step_host``); a host-built work queue takes the Python
+        path below.
         """
+        if self.policy == "device":
+            return self._step_host_native(seq_lens, block_rows, q_host, out_host, scratch)
         plan = self.plan_step(seq_lens, block_rows, out=scratch.get("stage"))
         scratch["stage"] = plan.buf if scratch.get("stage") is None or \
             scratch["stage"].numel() < plan.buf.numel() else scratch["stage"]
@@ -239,3 +276,50 @@ class DecodeEngine:
         h2d = plan.nbytes + b * self.hq * HEAD_DIM * q_host.element_size()
         d2h = b * self.hq * HEAD_DIM * out_host.element_size()
         return h2d, d2h
+
+
+class NativeEngine:
+    """``pkv_engine``: the C ABI's host-to-host decode step over an engine's pool."""
+
+    def __init__(self, engine: DecodeEngine, max_batch: int, max_pages: int):
+        import ctypes
+
+        from . import _native
+
+        self._ct = ctypes
+        self._lib = _native.load()
+        self._check = _native.check
+        self.max_batch, self.max_pages = max_batch, max_pages
+        self._ptr = ctypes.c_void_p()
+        dt = {torch.float16: _native.PKV_DTYPE_F16, torch.bfloat16: _native.PKV_DTYPE_BF16}
+        self._check(self._lib.pkv_engine_create(
+            engine.k_pages.data_ptr(), engine.v_pages.data_ptr(), engine.k_pages.shape[0],
+            engine.hq, engine.hkv, HEAD_DIM, engine.page_size, dt[engine.dtype], max_batch,
+            max_pages, ctypes.byref(self._ptr)))
+        self._h2d = ctypes.c_size_t()
+        self._d2h = ctypes.c_size_t()
+        self._h2d_ref = ctypes.byref(self._h2d)
+        self._d2h_ref = ctypes.byref(self._d2h)
+        self._step = self._lib.pkv_engine_step_host
+        self._keep = engine  # the pools must outlive the native engine
+
+    def step(self, seq: np.ndarray, rows: np.ndarray, q_host: torch.Tensor,
+             out_host: torch.Tensor) -> tuple[int, int]:
+        from .ops import _stream
+
+        self._check(self._step(
+            self._ptr, seq.ctypes.data, rows.ctypes.data, rows.shape[0], rows.shape[1],
+            q_host.data_ptr(), out_host.data_ptr(), _stream(), self._h2d_ref, self._d2h_ref))
+        return int(self._h2d.value), int(self._d2h.value)
+
+    def close(self) -> None:
+        if self._ptr:
+            self._check(self._lib.pkv_engine_destroy(self._ptr))
+            self._ptr = self._ct.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+

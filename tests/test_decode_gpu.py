@@ -454,3 +454,25 @@ def test_sharded_fused_exchange_single_rank():
     finally:
         torch.cuda.synchronize()
         x.close()
+
+
+def test_native_host_step():
+    """pkv_engine_step_host: host lengths / block rows / pinned q in, pinned
+    output out, one native call per step; batches grow the engine."""
+    from persistentkv_attention_b200.serving import DecodeEngine
+
+    c = make_case([7000, 1, 333, 4096, 0, 12000], seed=81)
+    d = c.cuda()
+    engine = DecodeEngine(d["k_pages"], d["v_pages"], 32)
+    want = c.oracle()
+    scratch = {}
+    q_host = c.q_source.clone().pin_memory()
+    out_host = torch.full((6, 32, 128), float("nan"), dtype=torch.float16).pin_memory()
+    for b in (2, 6, 3, 6):
+        out_host.fill_(float("nan"))
+        h2d, d2h = engine.step_host(c.seq_lens[:b], c.block_table[:b], q_host, out_host, scratch)
+        torch.cuda.current_stream().synchronize()
+        assert h2d == b * c.block_table.shape[1] * 4 + b * 4 + b * 32 * 128 * 2
+        assert d2h == b * 32 * 128 * 2
+        assert_close(out_host[:b], want[:b], "f16", f"native step B{b}")
+    scratch["native"].close()
