@@ -199,26 +199,32 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned 
 }
 
 // Where a finished (row, KV head) state goes in sharded mode: word `off`
-// (head qh0 of this rank's part) of every rank's gather buffer, plus this
-// thread's own values, kept for its merge of the gathered parts.
-template <int G>
+// (head qh0 of this rank's part) of every rank's gather buffer; this rank's
+// own values wait in shared memory (`own`, [G][130]) for the merge of the
+// gathered parts.
 struct XgSink {
     unsigned long long* const* gather;  // every rank's buffer (kernel parameters)
     size_t off;
+    float* own;
     int world, rank;
     unsigned epoch;
-    float o[G], m[G], l[G];  // own (o, m, l) of the k-th (head, dim) of this thread
 };
 
-// Thread-level emission of one merged value: the normalised output, the
-// (m, l, acc) state row, or the LL words of every peer (own value kept).
-template <int G, typename T, bool kXg>
-__device__ __forceinline__ void emit_merged(int k, int gg, int d, float o, float M, float L,
-                                            T* out, float* state, XgSink<G>& xg) {
+// Emission of one merged value (head gg, dim d; m and l ride with d == 0):
+// the normalised output, the (m, l, acc) state row, or the sharded sink.
+// These paths run once per row at the end of a launch, usually with a cold
+// instruction cache, so every caller loops over (head, dim) without
+// unrolling: smaller code costs fewer instruction-fetch misses.
+template <typename T, bool kXg>
+__device__ __forceinline__ void emit_merged(int gg, int d, float o, float M, float L, T* out,
+                                            float* state, const XgSink& xg) {
     if constexpr (kXg) {
-        xg.o[k] = o;
-        xg.m[k] = M;
-        xg.l[k] = L;
+        float* own = xg.own + gg * kStateStride;
+        own[2 + d] = o;
+        if (d == 0) {
+            own[0] = M;
+            own[1] = L;
+        }
         for (int r = 0; r < xg.world; ++r) {
             if (r == xg.rank) continue;
             unsigned long long* w = xg.gather[r] + xg.off + gg * kStateStride;
@@ -242,10 +248,9 @@ __device__ __forceinline__ void emit_merged(int k, int gg, int d, float o, float
 // ------------------------------------------------------------------ merge
 // Segmented log-sum-exp merge of the partial states in slots [s0, s0 + n) for
 // the G query heads qh0 .. qh0+G-1 of one row (reference cuh:719-784 and the
-// fused merge :660-708).  Run by NW = 4 warps, latency first: every m / l
-// value is requested in one round trip and reduced online, the slot weights
-// follow from shared memory, and the acc rows are read as float4, several
-// slots per warp in flight.
+// fused merge :660-708).  Run by NW warps; memory-level parallel: m / l are
+// reduced across all threads, weights are staged in shared memory per chunk
+// of 64 slots, and acc rows are read as float4 by NW slot groups.
 constexpr int kMergeChunk = 64;
 
 template <int NW>
@@ -254,7 +259,7 @@ __host__ __device__ constexpr int merge_scratch_floats() {
 }
 
 struct MergeSmem {
-    float* w;     // [kMergeChunk][8] slot m values, then weights
+    float* w;     // [kMergeChunk][8] weights of the current chunk
     float* stat;  // [2][NW][8] per-warp max / l partials
     float* red;   // [NW][G][128] acc partials (16-byte aligned)
 };
@@ -282,10 +287,9 @@ __device__ __forceinline__ void merge_slots_small(const float* __restrict__ pm,
                                                   const float* __restrict__ pl,
                                                   const float* __restrict__ pa, int s0, int n,
                                                   int Hq, int qh0, const MergeSmem& sm, T* out,
-                                                  float* state, XgSink<G>& xg) {
+                                                  float* state, const XgSink& xg) {
     constexpr int NT = NW * 32;
     constexpr int KP = merge_prefetch_slots<G>();
-    static_assert((G * kHeadDim) % NT == 0, "whole (head, dim) passes");
     const int t = threadIdx.x % NT;
     const int warp = t >> 5;
     const int lane = t & 31;
@@ -342,31 +346,21 @@ __device__ __forceinline__ void merge_slots_small(const float* __restrict__ pm,
             }
         }
         *reinterpret_cast<float4*>(sm.red + (warp * G + gg) * kHeadDim + 4 * lane) = acc;
+        if (t == 0) {  // per-head M / L for the emission loop
+            sm.stat[gg] = M[gg];
+            sm.stat[8 + gg] = L[gg];
+        }
     }
     sync_merge<kNamedBarrier>();
-#pragma unroll
-    for (int k = 0; k < G * kHeadDim / NT; ++k) {
-        const int idx = t + k * NT;
+#pragma unroll 1
+    for (int idx = t; idx < G * kHeadDim; idx += NT) {
         const int gg = idx / kHeadDim;
         const int d = idx % kHeadDim;
         float o = 0.f;
 #pragma unroll
         for (int j = 0; j < NW; ++j) o += sm.red[(j * G + gg) * kHeadDim + d];
-        float Mg = M[0], Lg = L[0];
-#pragma unroll
-        for (int q = 1; q < G; ++q) {
-            Mg = q == gg ? M[q] : Mg;
-            Lg = q == gg ? L[q] : Lg;
-        }
-        emit_merged<G, T, kXg>(k, gg, d, o, Mg, Lg, out, state, xg);
+        emit_merged<T, kXg>(gg, d, o, sm.stat[gg], sm.stat[8 + gg], out, state, xg);
     }
-}
-
-// Online (max, sum) pair merge: (m, l) absorbs (m2, l2).
-__device__ __forceinline__ void online_absorb(float& m, float& l, float m2, float l2) {
-    const float mx = fmaxf(m, m2);
-    l = l * fast_exp2((m - mx) * kLog2e) + l2 * fast_exp2((m2 - mx) * kLog2e);
-    m = mx;
 }
 
 // kXg: the merged values go to the sharded exchange sink `xg` instead of
@@ -376,76 +370,46 @@ __device__ __forceinline__ void merge_slots(const float* __restrict__ pm,
                                             const float* __restrict__ pl,
                                             const float* __restrict__ pa, int s0, int n, int Hq,
                                             int qh0, const MergeSmem& sm, T* out, float* state,
-                                            XgSink<G>& xg) {
+                                            const XgSink& xg) {
     if (n <= NW * merge_prefetch_slots<G>()) {
         merge_slots_small<G, T, NW, kNamedBarrier, kXg>(pm, pl, pa, s0, n, Hq, qh0, sm, out,
                                                         state, xg);
         return;
     }
     constexpr int NT = NW * 32;
-    static_assert((G * kHeadDim) % NT == 0, "whole (head, dim) passes");
     const int t = threadIdx.x % NT;
     const int warp = t >> 5;
     const int lane = t & 31;
     constexpr int kSlotsPerPass = NT / G;
     const int g = t % G;  // fixed: the strides below are multiples of G
-    // ---- one pass over m and l: loads issued together, reduced online
-    const bool keep_m = n <= kMergeChunk;  // slot m values stay in shared memory
-    float mt = kNegFltMax, lt = 0.f;
-    constexpr int kUnrollML = 4;
-    for (int s = t / G; s < n; s += kUnrollML * kSlotsPerPass) {
-        float mv[kUnrollML], lv[kUnrollML];
+    float mx = kNegFltMax;
+    for (int s = t / G; s < n; s += kSlotsPerPass)
+        mx = fmaxf(mx, __ldcg(pm + (size_t)(s0 + s) * Hq + qh0 + g));
 #pragma unroll
-        for (int u = 0; u < kUnrollML; ++u) {
-            const int su = s + u * kSlotsPerPass;
-            const size_t i = (size_t)(s0 + su) * Hq + qh0 + g;
-            mv[u] = su < n ? __ldcg(pm + i) : kNegFltMax;
-            lv[u] = su < n ? __ldcg(pl + i) : 0.f;
-        }
-#pragma unroll
-        for (int u = 0; u < kUnrollML; ++u) {
-            const int su = s + u * kSlotsPerPass;
-            if (su < n) {
-                if (keep_m) sm.w[su * 8 + g] = mv[u];
-                online_absorb(mt, lt, mv[u], lv[u]);
-            }
-        }
-    }
-#pragma unroll
-    for (int off = 16; off >= G; off >>= 1) {
-        const float m2 = __shfl_xor_sync(0xffffffffu, mt, off);
-        const float l2 = __shfl_xor_sync(0xffffffffu, lt, off);
-        online_absorb(mt, lt, m2, l2);
-    }
-    if (lane < G) {
-        sm.stat[warp * 8 + lane] = mt;
-        sm.stat[NW * 8 + warp * 8 + lane] = lt;
-    }
+    for (int off = 16; off >= G; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane < G) sm.stat[warp * 8 + lane] = mx;
     sync_merge<kNamedBarrier>();
-    float m_all[G], l_all[G];
+    float m_mine = sm.stat[g];
 #pragma unroll
-    for (int gg = 0; gg < G; ++gg) {
-        float mm = sm.stat[gg], ll = sm.stat[NW * 8 + gg];
-#pragma unroll
-        for (int w = 1; w < NW; ++w) online_absorb(mm, ll, sm.stat[w * 8 + gg], sm.stat[NW * 8 + w * 8 + gg]);
-        m_all[gg] = mm;
-        l_all[gg] = ll;
+    for (int w = 1; w < NW; ++w) m_mine = fmaxf(m_mine, sm.stat[w * 8 + g]);
+    float ls = 0.f;
+    for (int s = t / G; s < n; s += kSlotsPerPass) {
+        const size_t i = (size_t)(s0 + s) * Hq + qh0 + g;
+        ls = fmaf(fast_exp2((__ldcg(pm + i) - m_mine) * kLog2e), __ldcg(pl + i), ls);
     }
-    float m_mine = m_all[0];
 #pragma unroll
-    for (int gg = 1; gg < G; ++gg) m_mine = gg == g ? m_all[gg] : m_mine;
+    for (int off = 16; off >= G; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+    if (lane < G) sm.stat[NW * 8 + warp * 8 + lane] = ls;
 
     float4 acc[G];
 #pragma unroll
     for (int gg = 0; gg < G; ++gg) acc[gg] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int c0 = 0; c0 < n; c0 += kMergeChunk) {
         const int cn = min(kMergeChunk, n - c0);
-        // weights of the chunk's slots (m values from shared memory when kept)
         for (int i = t; i < cn * G; i += NT) {
             const int s = i / G;  // i % G == g
-            const float mv = keep_m ? sm.w[s * 8 + g]
-                                    : __ldcg(pm + (size_t)(s0 + c0 + s) * Hq + qh0 + g);
-            sm.w[s * 8 + g] = fast_exp2((mv - m_mine) * kLog2e);
+            sm.w[s * 8 + g] = fast_exp2(
+                (__ldcg(pm + (size_t)(s0 + c0 + s) * Hq + qh0 + g) - m_mine) * kLog2e);
         }
         sync_merge<kNamedBarrier>();
 #pragma unroll 4
@@ -467,21 +431,18 @@ __device__ __forceinline__ void merge_slots(const float* __restrict__ pm,
     for (int gg = 0; gg < G; ++gg)
         *reinterpret_cast<float4*>(sm.red + (warp * G + gg) * kHeadDim + 4 * lane) = acc[gg];
     sync_merge<kNamedBarrier>();
-#pragma unroll
-    for (int k = 0; k < G * kHeadDim / NT; ++k) {
-        const int idx = t + k * NT;
+#pragma unroll 1
+    for (int idx = t; idx < G * kHeadDim; idx += NT) {
         const int gg = idx / kHeadDim;
         const int d = idx % kHeadDim;
-        float o = 0.f;
+        float l_all = 0.f, o = 0.f, mv = kNegFltMax;
 #pragma unroll
-        for (int j = 0; j < NW; ++j) o += sm.red[(j * G + gg) * kHeadDim + d];
-        float Mg = m_all[0], Lg = l_all[0];
-#pragma unroll
-        for (int q = 1; q < G; ++q) {
-            Mg = q == gg ? m_all[q] : Mg;
-            Lg = q == gg ? l_all[q] : Lg;
+        for (int j = 0; j < NW; ++j) {
+            l_all += sm.stat[NW * 8 + j * 8 + gg];
+            o += sm.red[(j * G + gg) * kHeadDim + d];
+            mv = fmaxf(mv, sm.stat[j * 8 + gg]);
         }
-        emit_merged<G, T, kXg>(k, gg, d, o, Mg, Lg, out, state, xg);
+        emit_merged<T, kXg>(gg, d, o, mv, l_all, out, state, xg);
     }
 }
 
@@ -663,7 +624,8 @@ constexpr size_t decode_smem_bytes() {
            (2 * NSLOTS + 2 * kDescSlots) * sizeof(uint64_t) + 64 +
            2 * 2 * kConsumerWarps * 8 * sizeof(float) +
            2 * DecodeSmem<G>::kMergeFloats * sizeof(float) +
-           merge_scratch_floats<kConsumerWarps>() * sizeof(float);
+           merge_scratch_floats<kConsumerWarps>() * sizeof(float) +
+           (size_t)G * kStateStride * sizeof(float) /* sharded own state */;
 }
 
 // How the producer warp moves K/V pages into the ring.
@@ -713,28 +675,31 @@ __device__ __forceinline__ Item producer_next(const DecodeParams& p, int s, int 
 // LL words.  The sink of a finished (row, KV head) points at this rank's part
 // of it in every rank's buffer.
 template <int G>
-__device__ __forceinline__ void xg_make_sink(const DecodeParams& p, int row, int kvh,
-                                             unsigned epoch, XgSink<G>& xs) {
+__device__ __forceinline__ XgSink xg_make_sink(const DecodeParams& p, int row, int kvh,
+                                               unsigned epoch, float* own) {
     const size_t part = (size_t)p.xg_bcap * p.Hq * kStateStride;
+    XgSink xs;
     xs.gather = p.xg_gather;
     xs.off = ((size_t)(epoch & 1u) * p.xg_world + p.xg_rank) * part +
              ((size_t)row * p.Hq + (size_t)kvh * G) * kStateStride;
+    xs.own = own;
     xs.world = p.xg_world;
     xs.rank = p.xg_rank;
     xs.epoch = epoch;
+    return xs;
 }
 
-// After emit_merged has pushed this thread's values to every peer: wait
-// (bounded) until every peer's words of the same (head, dim) values carry
-// this step's number in this rank's own buffer, merge the world parts
-// (log-sum-exp, own part from registers) and write the output row.  Rows are
-// finished in the same order on every rank and all CTAs of the launch are
-// resident, so each wait ends once the peers reach that row.
+// After emit_merged has pushed this rank's values to every peer and kept
+// them in shared memory: wait (bounded) until every peer's words of the same
+// values carry this step's number in this rank's own buffer, merge the world
+// parts (log-sum-exp) and write the output row.  Rows are finished in the
+// same order on every rank and all CTAs of the launch are resident, so each
+// wait ends once the peers reach that row.  Called by the consumer threads.
 template <int G, typename T>
 __device__ __forceinline__ void xg_collect(const DecodeParams& p, int row, int kvh, int out_row,
-                                           const XgSink<G>& xs, volatile int* s_flags) {
+                                           const XgSink& xs, volatile int* s_flags) {
     constexpr int NT = kConsumerWarps * 32;
-    const int t = threadIdx.x % NT;
+    consumer_bar_sync();  // own m / l of each head are written by its d == 0 thread
     const int world = p.xg_world;
     const size_t part = (size_t)p.xg_bcap * p.Hq * kStateStride;
     const unsigned long long* base =
@@ -743,12 +708,12 @@ __device__ __forceinline__ void xg_collect(const DecodeParams& p, int row, int k
     T* o = out_row >= 0 ? reinterpret_cast<T*>(p.out) + ((size_t)out_row * p.Hq + kvh * G) * kHeadDim
                         : nullptr;
     const unsigned long long start = global_timer_ns();
-#pragma unroll
-    for (int k = 0; k < G * kHeadDim / NT; ++k) {
-        const int idx = t + k * NT;
+#pragma unroll 1
+    for (int idx = threadIdx.x % NT; idx < G * kHeadDim; idx += NT) {
         const int gg = idx / kHeadDim;
         const int d = idx % kHeadDim;
-        float mx = xs.m[k], lsum = xs.l[k], osum = xs.o[k];
+        const float* own = xs.own + gg * kStateStride;
+        float mx = own[0], lsum = own[1], osum = own[2 + d];
         for (int r = 0; r < world; ++r) {
             if (r == p.xg_rank) continue;
             const unsigned long long* w = base + r * part + gg * kStateStride;
@@ -780,6 +745,7 @@ __device__ __forceinline__ void xg_collect(const DecodeParams& p, int row, int k
         if (o != nullptr && s_flags[2] == 0)
             o[gg * kHeadDim + d] = ElemOps<T>::from_float(lsum > 0.f ? osum / lsum : 0.f);
     }
+    consumer_bar_sync();  // the own-state buffer is reused by the next row
 }
 
 template <int G, typename T, int BOX_ROWS, int NSLOTS, int LOAD>
@@ -811,6 +777,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     float* s_lstat = s_mstat + 2 * kConsumerWarps * 8;
     float* s_merge = s_lstat + 2 * kConsumerWarps * 8;
     float* s_mw = s_merge + 2 * DecodeSmem<G>::kMergeFloats;  // merge weights + stats
+    float* s_own = s_mw + merge_scratch_floats<kConsumerWarps>();  // [G][130] sharded own state
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -1249,12 +1216,11 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
         const bool direct = it.row_splits == 1;
         const bool write_direct_out = direct && !state_mode && !xg_mode && it.out_row >= 0 &&
                                       (!rect || it.tok_end > it.tok_begin);
-        XgSink<G> xs;
         const bool xg_direct = direct && xg_mode && !aborted;
-        if (xg_direct) xg_make_sink<G>(p, it.row, it.kvh, xg_epoch, xs);
-#pragma unroll
-        for (int k = 0; k < G * kHeadDim / (kConsumerWarps * 32); ++k) {
-            const int idx = threadIdx.x + k * kConsumerWarps * 32;
+        XgSink xs{};
+        if (xg_mode) xs = xg_make_sink<G>(p, it.row, it.kvh, xg_epoch, s_own);
+#pragma unroll 1
+        for (int idx = threadIdx.x; idx < G * kHeadDim; idx += kConsumerWarps * 32) {
             const int g = idx / kHeadDim;
             const int d = idx % kHeadDim;
             float mx = -INFINITY;
@@ -1271,7 +1237,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
             const float mnat = mx == -INFINITY ? kNegFltMax : mx * kLn2;
             if (direct) {
                 if (xg_direct) {
-                    emit_merged<G, T, true>(k, g, d, osum, mnat, lsum, nullptr, nullptr, xs);
+                    emit_merged<T, true>(g, d, osum, mnat, lsum, nullptr, nullptr, xs);
                 } else if (state_mode) {
                     float* st =
                         p.state_out + ((size_t)it.row * p.Hq + it.kvh * G + g) * kStateStride;
@@ -1317,7 +1283,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                     float* st = nullptr;
                     const bool xg_merge = xg_mode && !aborted;
                     if (xg_merge) {
-                        xg_make_sink<G>(p, it.row, it.kvh, xg_epoch, xs);
+                        // the sink was built at the item's start
                     } else if (state_mode) {
                         st = p.state_out + ((size_t)it.row * p.Hq + qh0) * kStateStride;
                     } else if (it.out_row >= 0) {
@@ -1457,7 +1423,7 @@ __global__ void __launch_bounds__(kHeadDim)
         o = reinterpret_cast<T*>(p.out) + ((size_t)orow * p.Hq + qh0) * kHeadDim;
     }
     MergeSmem ms{s_w, s_w + kMergeChunk * 8, s_red};
-    XgSink<G> unused;
+    const XgSink unused{};
     merge_slots<G, T, 4, false, false>(p.part_m, p.part_l, p.part_acc, s0, s1 - s0, p.Hq, qh0, ms,
                                        o, st, unused);
 }
