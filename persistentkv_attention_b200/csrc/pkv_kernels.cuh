@@ -273,15 +273,18 @@ __device__ __forceinline__ void sync_merge() {
     }
 }
 
-// Slots per warp prefetched by the low-latency merge (register budget).
+// Slots per warp loaded at once by the low-latency merge (register budget:
+// KP x G float4 per thread).
 template <int G>
 __host__ __device__ constexpr int merge_prefetch_slots() {
-    return G <= 4 ? 2 : 1;
+    return G <= 4 ? 4 : 2;
 }
 
 // Low-latency form of merge_slots for n <= NW * merge_prefetch_slots<G>()
-// slots: the m / l values and every acc row are requested in one round trip
-// before any reduction.
+// slots (16 for G <= 4): every m / l value and every acc row is requested in
+// one round trip; the per-head max and l-sum are reduced across all threads
+// (warp shuffles, then one shared-memory step), each warp weights its own
+// slots' acc rows in registers, and the warps' sums meet in shared memory.
 template <int G, typename T, int NW, bool kNamedBarrier, bool kXg>
 __device__ __forceinline__ void merge_slots_small(const float* __restrict__ pm,
                                                   const float* __restrict__ pl,
@@ -290,10 +293,11 @@ __device__ __forceinline__ void merge_slots_small(const float* __restrict__ pm,
                                                   float* state, const XgSink& xg) {
     constexpr int NT = NW * 32;
     constexpr int KP = merge_prefetch_slots<G>();
+    static_assert(NT / G >= NW * KP, "one (slot, head) pair per thread covers every slot");
     const int t = threadIdx.x % NT;
     const int warp = t >> 5;
     const int lane = t & 31;
-    const int sg = t / G;
+    const int sg = t / G;  // slot of this thread's m / l pair
     const int g = t % G;
     float mv = kNegFltMax, lv = 0.f;
     if (sg < n) {
@@ -313,24 +317,29 @@ __device__ __forceinline__ void merge_slots_small(const float* __restrict__ pm,
                                 : make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
-    float* sm_m = sm.w;          // [n][8]
-    float* sm_l = sm.w + 256;    // [n][8]
-    if (sg < n) {
-        sm_m[sg * 8 + g] = mv;
-        sm_l[sg * 8 + g] = lv;
-    }
+    // per-head max over all slots
+    float mx = mv;
+#pragma unroll
+    for (int off = 16; off >= G; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (sg < n) sm.w[sg * 8 + g] = mv;
+    if (lane < G) sm.stat[warp * 8 + lane] = mx;
     sync_merge<kNamedBarrier>();
-    float M[G], L[G];
+    float M[G];
 #pragma unroll
     for (int gg = 0; gg < G; ++gg) {
-        float mx = kNegFltMax;
-        for (int s = 0; s < n; ++s) mx = fmaxf(mx, sm_m[s * 8 + gg]);
-        float ls = 0.f;
-        for (int s = 0; s < n; ++s)
-            ls = fmaf(fast_exp2((sm_m[s * 8 + gg] - mx) * kLog2e), sm_l[s * 8 + gg], ls);
-        M[gg] = mx;
-        L[gg] = ls;
+        float v = sm.stat[gg];
+#pragma unroll
+        for (int w = 1; w < NW; ++w) v = fmaxf(v, sm.stat[w * 8 + gg]);
+        M[gg] = v;
     }
+    float m_mine = M[0];
+#pragma unroll
+    for (int gg = 1; gg < G; ++gg) m_mine = gg == g ? M[gg] : m_mine;
+    // per-head l-sum, and this warp's weighted acc rows
+    float ls = sg < n ? fast_exp2((mv - m_mine) * kLog2e) * lv : 0.f;
+#pragma unroll
+    for (int off = 16; off >= G; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+    if (lane < G) sm.stat[NW * 8 + warp * 8 + lane] = ls;
 #pragma unroll
     for (int gg = 0; gg < G; ++gg) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -338,7 +347,7 @@ __device__ __forceinline__ void merge_slots_small(const float* __restrict__ pm,
         for (int k = 0; k < KP; ++k) {
             const int slot = warp + k * NW;
             if (slot < n) {
-                const float w = fast_exp2((sm_m[slot * 8 + gg] - M[gg]) * kLog2e);
+                const float w = fast_exp2((sm.w[slot * 8 + gg] - M[gg]) * kLog2e);
                 acc.x = fmaf(w, a[k][gg].x, acc.x);
                 acc.y = fmaf(w, a[k][gg].y, acc.y);
                 acc.z = fmaf(w, a[k][gg].z, acc.z);
@@ -346,20 +355,20 @@ __device__ __forceinline__ void merge_slots_small(const float* __restrict__ pm,
             }
         }
         *reinterpret_cast<float4*>(sm.red + (warp * G + gg) * kHeadDim + 4 * lane) = acc;
-        if (t == 0) {  // per-head M / L for the emission loop
-            sm.stat[gg] = M[gg];
-            sm.stat[8 + gg] = L[gg];
-        }
     }
     sync_merge<kNamedBarrier>();
 #pragma unroll 1
     for (int idx = t; idx < G * kHeadDim; idx += NT) {
         const int gg = idx / kHeadDim;
         const int d = idx % kHeadDim;
-        float o = 0.f;
+        float l_all = 0.f, o = 0.f, mg = kNegFltMax;
 #pragma unroll
-        for (int j = 0; j < NW; ++j) o += sm.red[(j * G + gg) * kHeadDim + d];
-        emit_merged<T, kXg>(gg, d, o, sm.stat[gg], sm.stat[8 + gg], out, state, xg);
+        for (int j = 0; j < NW; ++j) {
+            l_all += sm.stat[NW * 8 + j * 8 + gg];
+            o += sm.red[(j * G + gg) * kHeadDim + d];
+            mg = fmaxf(mg, sm.stat[j * 8 + gg]);
+        }
+        emit_merged<T, kXg>(gg, d, o, mg, l_all, out, state, xg);
     }
 }
 
