@@ -246,6 +246,11 @@ __device__ __forceinline__ void emit_merged(int gg, int d, float o, float M, flo
 }
 
 // ------------------------------------------------------------------ merge
+// Segmented log-sum-exp merge of the partial states in slots [s0, s0 + n) for
+// the G query heads qh0 .. qh0+G-1 of one row (reference cuh:719-784 and the
+// fused merge :660-708).  Run by NW warps; memory-level parallel: m / l are
+// reduced across all threads, weights are staged in shared memory per chunk
+// of 64 slots, and acc rows are read as float4 by NW slot groups.
 constexpr int kMergeChunk = 64;
 
 template <int NW>
@@ -268,110 +273,168 @@ __device__ __forceinline__ void sync_merge() {
     }
 }
 
-// Slots per warp loaded at once by the merge (register budget: KP x G float4
-// per thread).
+// Slots per warp loaded at once by the low-latency merge (register budget:
+// KP x G float4 per thread).
 template <int G>
 __host__ __device__ constexpr int merge_prefetch_slots() {
-    return G <= 4 ? 4 : 1;
+    return G <= 4 ? 4 : 2;
 }
 
-// Segmented log-sum-exp merge of the partial states in slots [s0, s0 + n) for
-// the G query heads qh0 .. qh0+G-1 of one row (reference cuh:719-784 and the
-// fused merge :660-708), run by NW warps.  The slots go in chunks of
-// CH = NW * KP (16 for G <= 4): every m / l value and acc row of a chunk is
-// requested in one round trip, the chunk's per-head max is reduced across all
-// threads (shuffles, then one shared-memory step), and running (max, l, acc)
-// states are rescaled online, so a row costs one memory round trip per 16
-// pieces.  The warps' sums meet in shared memory at the end.  One compact
-// code path: it runs once per row at the end of a launch, usually from a
-// cold instruction cache.  kXg: the merged values go to the sharded exchange
-// sink `xg` instead of `out` / `state`.
+// Low-latency form of merge_slots for n <= NW * merge_prefetch_slots<G>()
+// slots (16 for G <= 4): every m / l value and every acc row is requested in
+// one round trip; the per-head max and l-sum are reduced across all threads
+// (warp shuffles, then one shared-memory step), each warp weights its own
+// slots' acc rows in registers, and the warps' sums meet in shared memory.
+template <int G, typename T, int NW, bool kNamedBarrier, bool kXg>
+__device__ __forceinline__ void merge_slots_small(const float* __restrict__ pm,
+                                                  const float* __restrict__ pl,
+                                                  const float* __restrict__ pa, int s0, int n,
+                                                  int Hq, int qh0, const MergeSmem& sm, T* out,
+                                                  float* state, const XgSink& xg) {
+    constexpr int NT = NW * 32;
+    constexpr int KP = merge_prefetch_slots<G>();
+    static_assert(NT / G >= NW * KP, "one (slot, head) pair per thread covers every slot");
+    const int t = threadIdx.x % NT;
+    const int warp = t >> 5;
+    const int lane = t & 31;
+    const int sg = t / G;  // slot of this thread's m / l pair
+    const int g = t % G;
+    float mv = kNegFltMax, lv = 0.f;
+    if (sg < n) {
+        const size_t i = (size_t)(s0 + sg) * Hq + qh0 + g;
+        mv = __ldcg(pm + i);
+        lv = __ldcg(pl + i);
+    }
+    float4 a[KP][G];
+#pragma unroll
+    for (int k = 0; k < KP; ++k) {
+        const int slot = warp + k * NW;
+#pragma unroll
+        for (int gg = 0; gg < G; ++gg) {
+            a[k][gg] = slot < n ? __ldcg(reinterpret_cast<const float4*>(
+                                      pa + ((size_t)(s0 + slot) * Hq + qh0 + gg) * kHeadDim +
+                                      4 * lane))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    // per-head max over all slots
+    float mx = mv;
+#pragma unroll
+    for (int off = 16; off >= G; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (sg < n) sm.w[sg * 8 + g] = mv;
+    if (lane < G) sm.stat[warp * 8 + lane] = mx;
+    sync_merge<kNamedBarrier>();
+    float M[G];
+#pragma unroll
+    for (int gg = 0; gg < G; ++gg) {
+        float v = sm.stat[gg];
+#pragma unroll
+        for (int w = 1; w < NW; ++w) v = fmaxf(v, sm.stat[w * 8 + gg]);
+        M[gg] = v;
+    }
+    float m_mine = M[0];
+#pragma unroll
+    for (int gg = 1; gg < G; ++gg) m_mine = gg == g ? M[gg] : m_mine;
+    // per-head l-sum, and this warp's weighted acc rows
+    float ls = sg < n ? fast_exp2((mv - m_mine) * kLog2e) * lv : 0.f;
+#pragma unroll
+    for (int off = 16; off >= G; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+    if (lane < G) sm.stat[NW * 8 + warp * 8 + lane] = ls;
+#pragma unroll
+    for (int gg = 0; gg < G; ++gg) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < KP; ++k) {
+            const int slot = warp + k * NW;
+            if (slot < n) {
+                const float w = fast_exp2((sm.w[slot * 8 + gg] - M[gg]) * kLog2e);
+                acc.x = fmaf(w, a[k][gg].x, acc.x);
+                acc.y = fmaf(w, a[k][gg].y, acc.y);
+                acc.z = fmaf(w, a[k][gg].z, acc.z);
+                acc.w = fmaf(w, a[k][gg].w, acc.w);
+            }
+        }
+        *reinterpret_cast<float4*>(sm.red + (warp * G + gg) * kHeadDim + 4 * lane) = acc;
+    }
+    sync_merge<kNamedBarrier>();
+#pragma unroll 1
+    for (int idx = t; idx < G * kHeadDim; idx += NT) {
+        const int gg = idx / kHeadDim;
+        const int d = idx % kHeadDim;
+        float l_all = 0.f, o = 0.f, mg = kNegFltMax;
+#pragma unroll
+        for (int j = 0; j < NW; ++j) {
+            l_all += sm.stat[NW * 8 + j * 8 + gg];
+            o += sm.red[(j * G + gg) * kHeadDim + d];
+            mg = fmaxf(mg, sm.stat[j * 8 + gg]);
+        }
+        emit_merged<T, kXg>(gg, d, o, mg, l_all, out, state, xg);
+    }
+}
+
+// kXg: the merged values go to the sharded exchange sink `xg` instead of
+// `out` / `state`.
 template <int G, typename T, int NW, bool kNamedBarrier, bool kXg>
 __device__ __forceinline__ void merge_slots(const float* __restrict__ pm,
                                             const float* __restrict__ pl,
                                             const float* __restrict__ pa, int s0, int n, int Hq,
                                             int qh0, const MergeSmem& sm, T* out, float* state,
                                             const XgSink& xg) {
+    if (n <= NW * merge_prefetch_slots<G>()) {
+        merge_slots_small<G, T, NW, kNamedBarrier, kXg>(pm, pl, pa, s0, n, Hq, qh0, sm, out,
+                                                        state, xg);
+        return;
+    }
     constexpr int NT = NW * 32;
-    constexpr int KP = merge_prefetch_slots<G>();
-    constexpr int CH = NW * KP;
-    static_assert(NT / G >= CH, "one (slot, head) pair per thread covers a chunk");
-    static_assert(CH <= kMergeChunk, "a chunk's m values fit the weight scratch");
     const int t = threadIdx.x % NT;
     const int warp = t >> 5;
     const int lane = t & 31;
-    const int sg = t / G;  // chunk slot of this thread's m / l pair
-    const int g = t % G;
-    float M[G];
+    constexpr int kSlotsPerPass = NT / G;
+    const int g = t % G;  // fixed: the strides below are multiples of G
+    float mx = kNegFltMax;
+    for (int s = t / G; s < n; s += kSlotsPerPass)
+        mx = fmaxf(mx, __ldcg(pm + (size_t)(s0 + s) * Hq + qh0 + g));
+#pragma unroll
+    for (int off = 16; off >= G; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane < G) sm.stat[warp * 8 + lane] = mx;
+    sync_merge<kNamedBarrier>();
+    float m_mine = sm.stat[g];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) m_mine = fmaxf(m_mine, sm.stat[w * 8 + g]);
+    float ls = 0.f;
+    for (int s = t / G; s < n; s += kSlotsPerPass) {
+        const size_t i = (size_t)(s0 + s) * Hq + qh0 + g;
+        ls = fmaf(fast_exp2((__ldcg(pm + i) - m_mine) * kLog2e), __ldcg(pl + i), ls);
+    }
+#pragma unroll
+    for (int off = 16; off >= G; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+    if (lane < G) sm.stat[NW * 8 + warp * 8 + lane] = ls;
+
     float4 acc[G];
 #pragma unroll
-    for (int gg = 0; gg < G; ++gg) {
-        M[gg] = kNegFltMax;
-        acc[gg] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    float lt = 0.f;  // this thread's share of head g's l-sum, relative to M[g]
-    for (int c0 = 0; c0 < n; c0 += CH) {
-        const int cn = min(CH, n - c0);
-        float mv = kNegFltMax, lv = 0.f;
-        if (sg < cn) {
-            const size_t i = (size_t)(s0 + c0 + sg) * Hq + qh0 + g;
-            mv = __ldcg(pm + i);
-            lv = __ldcg(pl + i);
+    for (int gg = 0; gg < G; ++gg) acc[gg] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c0 = 0; c0 < n; c0 += kMergeChunk) {
+        const int cn = min(kMergeChunk, n - c0);
+        for (int i = t; i < cn * G; i += NT) {
+            const int s = i / G;  // i % G == g
+            sm.w[s * 8 + g] = fast_exp2(
+                (__ldcg(pm + (size_t)(s0 + c0 + s) * Hq + qh0 + g) - m_mine) * kLog2e);
         }
-        float4 a[KP][G];
-#pragma unroll
-        for (int k = 0; k < KP; ++k) {
-            const int slot = warp + k * NW;
+        sync_merge<kNamedBarrier>();
+#pragma unroll 4
+        for (int s = warp; s < cn; s += NW) {
+            const float* row = pa + ((size_t)(s0 + c0 + s) * Hq + qh0) * kHeadDim + 4 * lane;
 #pragma unroll
             for (int gg = 0; gg < G; ++gg) {
-                a[k][gg] = slot < cn
-                               ? __ldcg(reinterpret_cast<const float4*>(
-                                     pa + ((size_t)(s0 + c0 + slot) * Hq + qh0 + gg) * kHeadDim +
-                                     4 * lane))
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(row + gg * kHeadDim));
+                const float w = sm.w[s * 8 + gg];
+                acc[gg].x = fmaf(w, v.x, acc[gg].x);
+                acc[gg].y = fmaf(w, v.y, acc[gg].y);
+                acc[gg].z = fmaf(w, v.z, acc[gg].z);
+                acc[gg].w = fmaf(w, v.w, acc[gg].w);
             }
         }
-        float mx = mv;
-#pragma unroll
-        for (int off = 16; off >= G; off >>= 1)
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-        if (sg < cn) sm.w[sg * 8 + g] = mv;
-        if (lane < G) sm.stat[warp * 8 + lane] = mx;
         sync_merge<kNamedBarrier>();
-#pragma unroll
-        for (int gg = 0; gg < G; ++gg) {
-            float mn = M[gg];  // new running max of head gg
-#pragma unroll
-            for (int w = 0; w < NW; ++w) mn = fmaxf(mn, sm.stat[w * 8 + gg]);
-            const float sc = fast_exp2((M[gg] - mn) * kLog2e);
-            if (gg == g)
-                lt = lt * sc + (sg < cn ? fast_exp2((mv - mn) * kLog2e) * lv : 0.f);
-            float4 s = make_float4(acc[gg].x * sc, acc[gg].y * sc, acc[gg].z * sc,
-                                   acc[gg].w * sc);
-#pragma unroll
-            for (int k = 0; k < KP; ++k) {
-                const int slot = warp + k * NW;
-                if (slot < cn) {
-                    const float w = fast_exp2((sm.w[slot * 8 + gg] - mn) * kLog2e);
-                    s.x = fmaf(w, a[k][gg].x, s.x);
-                    s.y = fmaf(w, a[k][gg].y, s.y);
-                    s.z = fmaf(w, a[k][gg].z, s.z);
-                    s.w = fmaf(w, a[k][gg].w, s.w);
-                }
-            }
-            acc[gg] = s;
-            M[gg] = mn;
-        }
-        sync_merge<kNamedBarrier>();  // the next chunk rewrites sm.w / sm.stat
-    }
-#pragma unroll
-    for (int off = 16; off >= G; off >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, off);
-    if (lane < G) sm.stat[NW * 8 + warp * 8 + lane] = lt;
-    if (t < G) {
-        float mg = M[0];
-#pragma unroll
-        for (int gg = 1; gg < G; ++gg) mg = gg == t ? M[gg] : mg;
-        sm.stat[t] = mg;
     }
 #pragma unroll
     for (int gg = 0; gg < G; ++gg)
@@ -381,13 +444,14 @@ __device__ __forceinline__ void merge_slots(const float* __restrict__ pm,
     for (int idx = t; idx < G * kHeadDim; idx += NT) {
         const int gg = idx / kHeadDim;
         const int d = idx % kHeadDim;
-        float l_all = 0.f, o = 0.f;
+        float l_all = 0.f, o = 0.f, mv = kNegFltMax;
 #pragma unroll
         for (int j = 0; j < NW; ++j) {
             l_all += sm.stat[NW * 8 + j * 8 + gg];
             o += sm.red[(j * G + gg) * kHeadDim + d];
+            mv = fmaxf(mv, sm.stat[j * 8 + gg]);
         }
-        emit_merged<T, kXg>(gg, d, o, sm.stat[gg], l_all, out, state, xg);
+        emit_merged<T, kXg>(gg, d, o, mv, l_all, out, state, xg);
     }
 }
 
