@@ -2,7 +2,8 @@
 """Decode-step benchmark of the B200 paged decode-attention engine.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
-                    [--impl engine|reference]
+                    [--impl engine|reference] [--trace-file FILE]
+                    [--seq-shard [--exchange fused|nccl]]
 
 A step is one continuous-batching decode step of a seeded synthetic trace
 (default: BASELINE config 2, B8 uniform [512, 8192] tokens, Hq 32 / Hkv 8,
@@ -164,10 +165,19 @@ class L2Flush:
 
 
 # ------------------------------------------------------------------ workload
+TRACE_FILE = None  # --trace-file: request specs of an external trace replace the synthetic lengths
+
+
 def build_workload(name: str, rank: int, steps_needed: int):
-    w = WORKLOADS[name]
+    w = dict(WORKLOADS[name])
+    specs = None
+    if TRACE_FILE is not None:
+        specs = tr.load_trace_specs(TRACE_FILE, w["requests"], PAGE)
+        w["requests"] = len(specs)
+        w["desc"] = f"trace file {Path(TRACE_FILE).name} ({len(specs)} requests), " \
+                    f"{w['max_active']} active, holes {w['hole']}"
     reqs, physical = tr.build_requests(w["trace"], w["requests"], w["max_active"], SEED + rank,
-                                       w["hole"], 0, PAGE)
+                                       w["hole"], 0, PAGE, specs=specs)
     steps = tr.build_steps(reqs, w["max_active"])
     steps = steps[: max(1, min(len(steps), max(steps_needed, 48)))]
     return w, reqs, physical, steps
@@ -608,6 +618,9 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=48)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="uniform_8k")
+    ap.add_argument("--trace-file", default=None,
+                    help="CSV / JSON request specs (prompt_len, decode_len, arrival) replacing "
+                         "the workload's synthetic lengths; its batch shape and holes stay")
     ap.add_argument("--impl", choices=["engine", "reference"], default="engine")
     ap.add_argument("--no-fused", action="store_true", help="separate PDL merge kernel")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -618,6 +631,8 @@ def main() -> None:
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    global TRACE_FILE
+    TRACE_FILE = args.trace_file
     if args.impl == "reference":
         run_reference_arm(args)
     elif args.seq_shard:

@@ -13,9 +13,14 @@ same jobs for this engine:
   device-resident ``StepPlan``;
 * ``run``        -- one work-queue decode call (fused merge by default);
 * ``capture``    -- a CUDA graph of ``run`` for replay;
-* ``step_host``  -- the end-to-end call a server makes: plan on the host,
-  copy q rows and metadata from pinned host memory, decode, copy the output
-  back to pinned host memory.
+* ``step_host``  -- the end-to-end call a server makes: one native call
+  (``pkv_engine_step_host``) from host metadata and pinned q rows to pinned
+  output rows.
+
+``StepGraph`` goes one step further for a serving loop whose q / output
+buffers stay put: one CUDA graph, captured once, holds the metadata upload
+and the device-scheduled decode, and is replayed for every step whatever
+the lengths (the device schedule needs no host work queue).
 """
 
 from __future__ import annotations
@@ -322,4 +327,112 @@ class NativeEngine:
             self.close()
         except Exception:
             pass
+
+
+class StepGraph:
+    """One captured CUDA graph per engine for every decode step of up to
+    ``max_batch`` rows of up to ``max_pages`` pages.
+
+    The graph copies one step's metadata from a pinned staging buffer into
+    fixed device buffers and runs ``paged_attention_auto`` (fused merge) on
+    them, reading ``self.q`` and writing ``self.out``.  ``step`` writes the
+    staging buffer and replays: no capture, no host work queue and one launch
+    call per step.  Rows beyond the step's batch get length 0, read q row 0
+    and write a spare output row, so the captured batch size never changes.
+    Two staging buffers and two graphs alternate; a buffer is rewritten only
+    after the replay that read it has finished.
+    """
+
+    def __init__(self, engine: DecodeEngine, max_batch: int, max_pages: int, q_rows: int,
+                 out_rows: int, stream: torch.cuda.Stream | None = None):
+        self.engine = engine
+        self.max_batch, self.max_pages = max_batch, max_pages
+        self.q_rows, self.out_rows = q_rows, out_rows
+        dev, hq = engine.device, engine.hq
+        self.q = torch.zeros(q_rows, hq, HEAD_DIM, dtype=engine.dtype, device=dev)
+        self._out = torch.zeros(out_rows + 1, hq, HEAD_DIM, dtype=engine.dtype, device=dev)
+        self.out = self._out[:out_rows]
+        b, mp = max_batch, max_pages
+        self._words = b * mp + 3 * b
+        self._dev = torch.zeros(self._words, dtype=torch.int32, device=dev)
+        self._ws = torch.empty(ops.auto_workspace_bytes(b, hq, engine.hkv) // 4,
+                               dtype=torch.float32, device=dev)
+        self._counters = torch.zeros(b, engine.hkv, dtype=torch.int32, device=dev)
+        bt = self._dev[: b * mp].view(b, mp)
+        sl = self._dev[b * mp: b * mp + b]
+        qi = self._dev[b * mp + b: b * mp + 2 * b]
+        oi = self._dev[b * mp + 2 * b:]
+        self._stage = [torch.zeros(self._words, dtype=torch.int32).pin_memory() for _ in range(2)]
+        self._done = [torch.cuda.Event() for _ in range(2)]
+        self._graphs = []
+        self._stream = stream or torch.cuda.Stream(dev)
+        for i in range(2):
+            self._fill(i, np.zeros(0, np.int32), np.zeros((0, 1), np.int32), None, None)
+
+            def run(i=i):
+                self._dev.copy_(self._stage[i], non_blocking=True)
+                ops.paged_attention_auto(self.q, engine.k_pages, engine.v_pages, bt, sl,
+                                         self._out, self._ws, qi, oi, self._counters)
+
+            with torch.cuda.stream(self._stream):
+                run()  # first call outside capture (kernel attributes, maps)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=self._stream):
+                    run()
+            self._graphs.append(graph)
+        self._stream.synchronize()
+        self._next = 0
+
+    def _fill(self, i, seq_lens, block_rows, q_indices, out_indices) -> None:
+        b, mp = self.max_batch, self.max_pages
+        n, width = block_rows.shape
+        if n > b or width > mp:
+            raise RuntimeError(f"step of {n} rows x {width} pages exceeds the graph's "
+                               f"{b} x {mp}")
+        v = self._stage[i].numpy()
+        bt = v[: b * mp].reshape(b, mp)
+        bt[:n, :width] = block_rows
+        bt[:n, width:] = block_rows[:, -1:] if width else 0
+        bt[n:] = 0
+        v[b * mp: b * mp + b] = 0
+        v[b * mp: b * mp + n] = seq_lens
+        qi = v[b * mp + b: b * mp + 2 * b]
+        qi[:] = 0
+        qi[:n] = np.arange(n) if q_indices is None else q_indices
+        oi = v[b * mp + 2 * b:]
+        oi[:] = self.out_rows            # the spare row
+        oi[:n] = np.arange(n) if out_indices is None else out_indices
+
+    def step(self, seq_lens, block_rows: np.ndarray, q_indices=None, out_indices=None) -> None:
+        """Queues one decode step on the graph's stream (``self.q`` -> ``self.out``),
+        ordered after the work already queued on the caller's current stream.
+
+        ``block_rows`` [B, width] and ``seq_lens`` [B] are host int32; q_indices /
+        out_indices (host, default identity) select rows of ``self.q`` / ``self.out``.
+        Synchronise the stream (or wait on it) before reading ``self.out``."""
+        rows = np.ascontiguousarray(block_rows, dtype=np.int32)
+        seq = np.ascontiguousarray(seq_lens, dtype=np.int32)
+        if rows.ndim != 2 or seq.shape != (rows.shape[0],):
+            raise RuntimeError("block_rows must be [B, width] and seq_lens [B]")
+        if int(seq.max(initial=0)) > rows.shape[1] * self.engine.page_size:
+            raise RuntimeError("a row is longer than its block-table row")
+        for name, idx, limit in (("q_indices", q_indices, self.q_rows),
+                                 ("out_indices", out_indices, self.out_rows)):
+            if idx is not None:
+                idx = np.asarray(idx)
+                if idx.shape != seq.shape or (idx.size and (idx.min() < 0 or idx.max() >= limit)):
+                    raise RuntimeError(f"{name} out of range")
+        i = self._next
+        self._next ^= 1
+        self._done[i].synchronize()      # the replay that last read staging i is over
+        self._fill(i, seq, rows, q_indices, out_indices)
+        # after whatever the caller queued on its stream (q rows written, ...)
+        self._stream.wait_stream(torch.cuda.current_stream(self.engine.device))
+        with torch.cuda.stream(self._stream):
+            self._graphs[i].replay()
+            self._done[i].record(self._stream)
+
+    @property
+    def stream(self) -> torch.cuda.Stream:
+        return self._stream
 

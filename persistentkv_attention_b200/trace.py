@@ -3,9 +3,10 @@
 Restates the trace mechanics of the reference's serving harness
 (tests/benchmark_serving_trace.py): ``rounded_length`` (:159-160),
 ``make_lengths`` (:163-195), ``build_requests`` (:232-282) and ``build_steps``
-(:285-298) -- same seeded torch CPU generators, same page-universe permutation
-with holes, same admission rule -- and adds the length distributions of the
-benchmark configurations of this engine:
+(:285-298) and ``load_trace_specs`` (:198-229, external trace files) -- same
+seeded torch CPU generators, same page-universe permutation with holes, same
+admission rule -- and adds the length distributions of the benchmark
+configurations of this engine:
 
 * ``uniform_8k``  -- prompt U[512, 8192], decode U[16, 96]        (config 2)
 * ``bimodal_32k`` -- 75% U[512, 2048] / 25% U[16384, 32768]       (config 3)
@@ -112,6 +113,45 @@ def make_lengths(trace: str, requests: int, seed: int, page_size: int = 16):
             raise ValueError(f"unknown trace: {trace}")
         result.append((rounded_length(prompt, page_size), decode))
     return result
+
+
+def load_trace_specs(path, limit: int, page_size: int = 16):
+    """Request specs of an external trace file, like the reference's
+    ``load_trace_specs`` (tests/benchmark_serving_trace.py:198-229).
+
+    A ``.json`` file holds a list of objects; anything else is read as CSV
+    with a header.  Each row gives ``prompt_len`` (or ``prompt``) and
+    ``decode_len`` (or ``decode``), optionally ``arrival`` (or
+    ``arrival_step``; default: the row index).  At most ``limit`` rows are
+    read; prompts are rounded up to whole pages.  Returns a list of
+    (arrival, prompt_len, decode_len) for ``build_requests(specs=...)``.
+    """
+    import csv
+    import json
+    from pathlib import Path
+
+    path = Path(path)
+    if path.suffix.lower() == ".json":
+        raw = json.loads(path.read_text())
+        if not isinstance(raw, list):
+            raise ValueError("--trace-file JSON must contain a list of request objects")
+        rows = raw
+    else:
+        with path.open(newline="") as handle:
+            rows = list(csv.DictReader(handle))
+    specs = []
+    for index, row in enumerate(rows[:limit]):
+        try:
+            prompt = int(row.get("prompt_len", row.get("prompt", "")))
+            decode = int(row.get("decode_len", row.get("decode", "")))
+        except ValueError as error:
+            raise ValueError("trace-file rows must define integer prompt_len/prompt and "
+                             "decode_len/decode fields") from error
+        arrival = int(row.get("arrival", row.get("arrival_step", index)))
+        specs.append((arrival, rounded_length(prompt, page_size), decode))
+    if not specs:
+        raise ValueError(f"trace file produced no requests: {path}")
+    return specs
 
 
 def build_requests(trace: str, requests: int, max_active: int, seed: int, hole_fraction: float,

@@ -21,6 +21,8 @@ Fixtures written (all small):
   queues of ``compile_persistentkv_metadata``.
 * ``traces.json`` -- ``make_lengths`` / ``build_requests`` / ``build_steps``
   outputs for each reference trace.
+* ``trace_files.json`` -- ``load_trace_specs`` and the requests / steps built
+  from the committed ``trace_specs.csv`` / ``trace_specs.json``.
 """
 
 from __future__ import annotations
@@ -177,6 +179,26 @@ def make_traces(h) -> None:
     (HERE / "traces.json").write_text(json.dumps(out))
 
 
+def make_trace_files(h) -> None:
+    """The reference's ``load_trace_specs`` + ``build_requests(trace_file=...)``
+    + ``build_steps`` on the two committed trace files."""
+    out = []
+    for name, limit, max_active, seed, hole in (("trace_specs.csv", 100, 3, 20260624, 0.1),
+                                                ("trace_specs.json", 4, 2, 20260625, 0.0)):
+        path = HERE / name
+        specs = h.load_trace_specs(path, limit)
+        reqs, physical = h.build_requests("uniform", limit, max_active, seed, hole, 0, path)
+        steps = h.build_steps(reqs, max_active)
+        out.append({
+            "file": name, "limit": limit, "max_active": max_active, "seed": seed, "hole": hole,
+            "specs": [[s.arrival, s.prompt_len, s.decode_len] for s in specs],
+            "physical_pages": physical,
+            "pages": [list(r.physical_pages) for r in reqs],
+            "steps": [[s.step, list(s.active_ids), list(s.lengths)] for s in steps],
+        })
+    (HERE / "trace_files.json").write_text(json.dumps(out))
+
+
 def main() -> None:
     if not ref.ref_cpu_available():
         raise SystemExit("build oracle/_ref first: python -m oracle.build_ref --skip-torch-ext")
@@ -184,6 +206,7 @@ def main() -> None:
     h = load_harness()
     make_scheduler(h)
     make_traces(h)
+    make_trace_files(h)
     for p in sorted(HERE.glob("*.*")):
         print(p.name, p.stat().st_size)
 

@@ -476,3 +476,30 @@ def test_native_host_step():
         assert d2h == b * 32 * 128 * 2
         assert_close(out_host[:b], want[:b], "f16", f"native step B{b}")
     scratch["native"].close()
+
+
+def test_step_graph_reused_across_steps():
+    """StepGraph: one captured graph (metadata upload + device-scheduled decode)
+    replayed for steps of different batch sizes and lengths."""
+    from persistentkv_attention_b200.serving import DecodeEngine, StepGraph
+
+    c = make_case([9000, 33, 4096, 1, 700, 12000, 0, 2500], seed=91, indexed=True)
+    d = c.cuda()
+    engine = DecodeEngine(d["k_pages"], d["v_pages"], 32)
+    sg = StepGraph(engine, max_batch=8, max_pages=c.block_table.shape[1], q_rows=c.out_rows,
+                   out_rows=c.out_rows)
+    sg.q.copy_(d["q_source"])
+    kf, vf, qf = (t.float().numpy() for t in (c.k_pages, c.v_pages, c.q_source))
+    steps = [[0, 1, 2], [3, 4, 5, 6, 7], list(range(8)), [5]]
+    for n, rows in enumerate(steps):
+        lens = c.seq_lens[rows] // (1 + n % 2)
+        width = max(1, int(np.ceil(lens.max(initial=1) / 16)))
+        table = c.block_table[rows][:, :width]
+        qi, oi = c.q_indices[rows], c.out_indices[rows]
+        sg.out.fill_(float("nan"))
+        sg.step(lens, table, qi, oi)
+        sg.stream.synchronize()
+        want = po.paged_decode(qf, kf, vf, table, seq_lens=lens, q_indices=qi, out_indices=oi,
+                               out_rows=c.out_rows)
+        assert_close(sg.out, want, "f16", f"graph step {n}")
+    assert len(sg._graphs) == 2
