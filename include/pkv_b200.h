@@ -208,6 +208,28 @@ pkv_status pkv_paged_attention_sharded(
     int physical_pages, int page_size, int max_pages,
     pkv_dtype dtype, void* stream);
 
+/* ---- KV append (the write side of a decode step) ----
+ * Writes one new token per row into the paged pools: row b's k_new[b] /
+ * v_new[b] ([B][Hkv][128], same 16-bit dtype as the pools) land at token
+ * position positions[b] of its block-table row (page slot positions[b] /
+ * page_size, offset positions[b] % page_size).  With a free-page list
+ * (free_pages, device int32, a stack whose top is free_pages[*free_count-1]),
+ * every row whose token opens a page takes one: the opening rows in row
+ * order take free_pages[*free_count - 1], [*free_count - 2], ..., the page id
+ * is written into block_table, and *free_count is lowered by the pages
+ * taken.  counters: one zeroed int32, left zero.  Without a list
+ * (free_pages NULL) every page must already be in block_table.  Rows whose
+ * position is beyond max_pages * page_size, whose page id is outside the
+ * pool or that find the list empty set PKV_DEVERR_LOGICAL_PAGE /
+ * PKV_DEVERR_PAGE_ID / PKV_DEVERR_NO_PAGE and write nothing.  No counterpart
+ * in the reference, whose pool is pre-filled and whose lengths grow over
+ * reserved pages (tests/benchmark_serving_trace.py:253-263, :1245-1251). */
+pkv_status pkv_kv_append(const void* k_new, const void* v_new, void* k_pages, void* v_pages,
+                         int32_t* block_table, const int32_t* positions,
+                         const int32_t* free_pages, int32_t* free_count, int32_t* counters,
+                         int B, int Hkv, int head_dim, int physical_pages, int page_size,
+                         int max_pages, pkv_dtype dtype, void* stream);
+
 /* ---- Native host step ----
  * A decode engine over one paged K/V pool that takes a step from host
  * buffers to host buffers in one call: it stages the block-table rows and
@@ -324,6 +346,7 @@ pkv_status pkv_device_error(uint32_t* code, int clear);
 #define PKV_DEVERR_INDEX       0x10u /* q_indices / out_indices out of range */
 #define PKV_DEVERR_TIMEOUT     0x20u /* bounded pipeline wait expired        */
 #define PKV_DEVERR_PEER        0x40u /* a peer's sharded state did not arrive */
+#define PKV_DEVERR_NO_PAGE     0x80u /* KV append: free-page list exhausted   */
 
 /* ---------------------------------------------------------------------------
  * Host-side scheduler: work-queue builder and split-count router.

@@ -204,3 +204,53 @@ def error_stats(got, ref) -> tuple[float, float]:
     mask = ~np.isnan(ref)
     diff = np.abs(got[mask] - ref[mask])
     return float(diff.max(initial=0.0)), float(diff.mean() if diff.size else 0.0)
+
+
+def kv_append(k_new, v_new, k_pages, v_pages, block_table, positions, free_pages=None,
+              free_count=None):
+    """CPU restatement of ``pkv_kv_append`` (in place on numpy arrays).
+
+    Row b writes k_new[b] / v_new[b] at token positions[b] of its block-table
+    row.  With a free list, the rows whose token opens a page (position %
+    page_size == 0), in row order, take free_pages[free_count - 1],
+    free_pages[free_count - 2], ...; the page id goes into the block table.
+    Rows with an invalid position, an out-of-pool page or no free page left
+    write nothing.  Returns (new free_count, error bits) with the bits of
+    ``pkv_device_error`` (0x1 page id, 0x2 position, 0x80 list exhausted).
+    The reference has no append: its pool is pre-filled
+    (tests/benchmark_serving_trace.py:253-263); this follows the C ABI's
+    documented semantics.
+    """
+    page = k_pages.shape[2]
+    num_pages = k_pages.shape[0]
+    max_pages = block_table.shape[1]
+    errors = 0
+    taken = 0
+    avail = int(free_count) if free_pages is not None else 0
+    for b, pos in enumerate(np.asarray(positions)):
+        pos = int(pos)
+        if pos < 0 or pos >= max_pages * page:
+            errors |= 0x2
+            continue
+        slot = pos // page
+        if free_pages is not None and pos % page == 0:
+            k = avail - 1 - taken
+            taken += 1
+            if k < 0:
+                errors |= 0x80
+                continue
+            pid = int(free_pages[k])
+            if pid < 0 or pid >= num_pages:
+                errors |= 0x1
+                continue
+            block_table[b, slot] = pid
+        else:
+            pid = int(block_table[b, slot])
+            if pid < 0 or pid >= num_pages:
+                errors |= 0x1
+                continue
+        k_pages[pid, :, pos % page, :] = k_new[b]
+        v_pages[pid, :, pos % page, :] = v_new[b]
+    new_count = avail - min(taken, avail) if free_pages is not None else free_count
+    return new_count, errors
+

@@ -41,6 +41,7 @@ DEVERR_BITS = {
     0x10: "q/out index out of range",
     0x20: "pipeline wait timed out",
     0x40: "a peer's sharded state did not arrive in time",
+    0x80: "KV append: free-page list exhausted",
 }
 
 EXCHANGE_HANDLE_BYTES = 64
@@ -107,6 +108,9 @@ SIGNATURES = {
         [_P, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, c_int, c_int, c_int, c_int, c_int,
          c_int, c_int, c_int, c_int, _P],
     ),
+    "pkv_kv_append": (
+        c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int,
+                c_int, _P]),
     "pkv_engine_create": (
         c_int, [_P, _P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                 POINTER(c_void_p)]),

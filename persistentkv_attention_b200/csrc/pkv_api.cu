@@ -879,6 +879,57 @@ pkv_status pkv_device_error(uint32_t* code, int clear) {
     return ok_status();
 }
 
+// ------------------------------------------------------------ KV append
+pkv_status pkv_kv_append(const void* k_new, const void* v_new, void* k_pages, void* v_pages,
+                         int32_t* block_table, const int32_t* positions,
+                         const int32_t* free_pages, int32_t* free_count, int32_t* counters,
+                         int B, int Hkv, int head_dim, int physical_pages, int page_size,
+                         int max_pages, pkv_dtype dtype, void* stream) {
+    if (k_new == nullptr || v_new == nullptr)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "k_new and v_new must be CUDA tensors");
+    if (k_pages == nullptr || v_pages == nullptr)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "k_pages and v_pages must be CUDA tensors");
+    if (block_table == nullptr || positions == nullptr)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "block_table and positions must be CUDA tensors");
+    if (free_pages != nullptr && (free_count == nullptr || counters == nullptr))
+        return fail(PKV_ERR_INVALID_ARGUMENT,
+                    "a free-page list needs free_count and zeroed counters");
+    if (dtype != PKV_DTYPE_F16 && dtype != PKV_DTYPE_BF16)
+        return fail(PKV_ERR_UNSUPPORTED, "k_new has wrong dtype");
+    if (head_dim != kHeadDim)
+        return fail(PKV_ERR_UNSUPPORTED, "PersistentKV extension currently requires d=128");
+    if (B < 0 || Hkv <= 0 || physical_pages <= 0 || page_size <= 0 || max_pages <= 0)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "invalid append shape");
+    if ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new) |
+         reinterpret_cast<uintptr_t>(k_pages) | reinterpret_cast<uintptr_t>(v_pages)) & 15u)
+        return fail(PKV_ERR_MISALIGNED, "k_new, v_new and the pools must be 16-byte aligned");
+    if (B == 0) return ok_status();
+    DeviceState* ds = nullptr;
+    pkv_status st = current_device(&ds);
+    if (st != PKV_OK) return st;
+    AppendParams ap;
+    ap.k_new = static_cast<const uint8_t*>(k_new);
+    ap.v_new = static_cast<const uint8_t*>(v_new);
+    ap.k_pages = static_cast<uint8_t*>(k_pages);
+    ap.v_pages = static_cast<uint8_t*>(v_pages);
+    ap.block_table = block_table;
+    ap.positions = positions;
+    ap.free_pages = free_pages;
+    ap.free_count = free_count;
+    ap.counters = counters;
+    ap.error = ds->error_word;
+    ap.B = B;
+    ap.Hkv = Hkv;
+    ap.num_pages = physical_pages;
+    ap.page_size = page_size;
+    ap.max_pages = max_pages;
+    pkv_kv_append_kernel<<<B, 128, 0, static_cast<cudaStream_t>(stream)>>>(ap);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess)
+        return fail(PKV_ERR_CUDA, "append launch failed: %s", cudaGetErrorString(e));
+    return ok_status();
+}
+
 // ------------------------------------------------------------ sharded decode
 size_t pkv_exchange_bytes(int world, int max_batch, int Hq, int Hkv) {
     if (world <= 0 || world > kMaxWorld || max_batch <= 0 || Hq <= 0 || Hkv <= 0) return 0;

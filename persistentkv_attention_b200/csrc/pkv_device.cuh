@@ -41,10 +41,11 @@ constexpr unsigned kErrSlot = 0x8u;
 constexpr unsigned kErrIndex = 0x10u;
 constexpr unsigned kErrTimeout = 0x20u;
 constexpr unsigned kErrPeer = 0x40u;  // a peer's state did not arrive in time
+constexpr unsigned kErrNoPage = 0x80u;  // KV append: the free-page list ran out
 
 // Sharded decode: each rank's states reach the other ranks' memory through
-// plain peer stores over NVLink, flagged by a release store of the step
-// number; the owner polls with acquire loads, bounded like every other wait.
+// plain peer stores over NVLink as 8-byte words carrying the step number;
+// the owner polls them, bounded like every other wait.
 constexpr unsigned long long kPeerWaitLimitNs = 2000000000ull;
 constexpr int kMaxWorld = 8;
 

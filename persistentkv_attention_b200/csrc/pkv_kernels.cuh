@@ -1467,4 +1467,116 @@ __global__ void __launch_bounds__(kHeadDim)
     o[d] = ElemOps<T>::from_float(lsum > 0.f ? osum / lsum : 0.f);
 }
 
+// ------------------------------------------------------------------ KV append
+// One new token per row written into the paged pool: the write side of a
+// decode step.  Row b writes its token at position p = positions[b]: page
+// slot j = p / page_size of its block-table row, offset p % page_size.  A
+// token that opens a page (p % page_size == 0) takes a page from the free
+// list when one is given: the rows that open a page, in row order, take
+// free_pages[free_count - 1], free_pages[free_count - 2], ...  (deterministic
+// whatever the CTA order), and the page id is written into the block table.
+// The last CTA to finish lowers *free_count by the pages taken and resets its
+// counter.  grid = B, block = 128; each CTA copies Hkv x 256 B of K and of V
+// with 16-byte stores.
+struct AppendParams {
+    const uint8_t* k_new;  // [B][Hkv][128] 16-bit elements
+    const uint8_t* v_new;
+    uint8_t* k_pages;      // [P][Hkv][page][128]
+    uint8_t* v_pages;
+    int32_t* block_table;  // [B][max_pages]
+    const int32_t* positions;
+    const int32_t* free_pages;  // [free_capacity] or null (pages already mapped)
+    int32_t* free_count;        // [1]
+    int32_t* counters;          // [1] zeroed; finished CTAs
+    unsigned* error;
+    int B, Hkv, num_pages, page_size, max_pages;
+};
+
+__global__ void __launch_bounds__(128) pkv_kv_append_kernel(const __grid_constant__ AppendParams p) {
+    __shared__ int s_red[4];
+    __shared__ int s_page, s_avail;
+    const int b = blockIdx.x;
+    const int t = threadIdx.x;
+    const int pos = __ldg(p.positions + b);
+    const bool pos_ok = pos >= 0 && pos < p.max_pages * p.page_size;
+    const bool opens = pos_ok && p.free_pages != nullptr && pos % p.page_size == 0;
+    // rank of this row among the earlier rows that open a page, and the total
+    int before = 0, total = 0;
+    if (p.free_pages != nullptr) {
+        for (int r = t; r < p.B; r += 128) {
+            const int q = __ldg(p.positions + r);
+            const int o = (q >= 0 && q < p.max_pages * p.page_size && q % p.page_size == 0) ? 1 : 0;
+            before += r < b ? o : 0;
+            total += o;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            before += __shfl_xor_sync(0xffffffffu, before, off);
+            total += __shfl_xor_sync(0xffffffffu, total, off);
+        }
+        if ((t & 31) == 0) s_red[t >> 5] = before;
+        __syncthreads();
+        before = s_red[0] + s_red[1] + s_red[2] + s_red[3];
+        __syncthreads();
+        if ((t & 31) == 0) s_red[t >> 5] = total;
+        __syncthreads();
+        total = s_red[0] + s_red[1] + s_red[2] + s_red[3];
+    }
+    if (t == 0) {
+        int page = -1;
+        const int avail = p.free_pages != nullptr ? *p.free_count : 0;
+        s_avail = avail;
+        if (!pos_ok) {
+            raise_error(p.error, kErrLogicalPage);
+        } else if (opens) {
+            const int k = avail - 1 - before;
+            if (k < 0) {
+                raise_error(p.error, kErrNoPage);
+            } else {
+                page = __ldg(p.free_pages + k);
+                if (page < 0 || page >= p.num_pages) {
+                    raise_error(p.error, kErrPageId);
+                    page = -1;
+                } else {
+                    p.block_table[(size_t)b * p.max_pages + pos / p.page_size] = page;
+                }
+            }
+        } else {
+            page = p.block_table[(size_t)b * p.max_pages + pos / p.page_size];
+            if (page < 0 || page >= p.num_pages) {
+                raise_error(p.error, kErrPageId);
+                page = -1;
+            }
+        }
+        s_page = page;
+    }
+    __syncthreads();
+    const int page = s_page;
+    if (page >= 0) {
+        const int off = pos % p.page_size;
+        const int chunks = p.Hkv * (kRowBytes / 16);  // 16-byte pieces of one token row set
+        for (int c = t; c < chunks; c += 128) {
+            const int kvh = c / (kRowBytes / 16);
+            const int piece = c % (kRowBytes / 16);
+            const size_t src = ((size_t)b * p.Hkv + kvh) * kRowBytes + piece * 16;
+            const size_t dst =
+                (((size_t)page * p.Hkv + kvh) * p.page_size + off) * kRowBytes + piece * 16;
+            *reinterpret_cast<uint4*>(p.k_pages + dst) =
+                __ldg(reinterpret_cast<const uint4*>(p.k_new + src));
+            *reinterpret_cast<uint4*>(p.v_pages + dst) =
+                __ldg(reinterpret_cast<const uint4*>(p.v_new + src));
+        }
+    }
+    if (p.free_pages != nullptr && t == 0) {
+        // every CTA has read *free_count above; the last one to get here updates it
+        __threadfence();
+        const int done = atomicAdd(p.counters, 1);
+        if (done == p.B - 1) {
+            *p.counters = 0;
+            const int taken = min(total, s_avail);
+            *p.free_count = s_avail - taken;
+        }
+    }
+}
+
 }  // namespace pkv

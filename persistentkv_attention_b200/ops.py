@@ -439,6 +439,43 @@ def paged_attention_sharded(q_source, k_pages, v_pages, block_table, seq_lens, o
         _stream()))
 
 
+def kv_append(k_new, v_new, k_pages, v_pages, block_table, positions, free_pages=None,
+              free_count=None, counters=None) -> None:
+    """Writes one new token per row into the paged pools (``pkv_kv_append``).
+
+    ``k_new`` / ``v_new`` [B, Hkv, 128] (the pools' dtype) land at token
+    ``positions[b]`` of row b.  With ``free_pages`` (int32 stack), ``free_count``
+    (int32 [1]) and zeroed ``counters`` (int32 [1]), rows whose token opens a
+    page take pages from the top of the stack in row order and record them in
+    ``block_table``.  No counterpart in the reference."""
+    dt = k_pages.dtype
+    _check_tensor(k_new, "k_new", dt, 3)
+    _check_tensor(v_new, "v_new", dt, 3)
+    _check_tensor(k_pages, "k_pages", tuple(_DTYPES), 4)
+    _check_tensor(v_pages, "v_pages", dt, 4)
+    _check_tensor(block_table, "block_table", torch.int32, 2)
+    _check_tensor(positions, "positions", torch.int32, 1)
+    b, hkv, d = k_new.shape
+    if tuple(v_new.shape) != (b, hkv, d) or k_pages.size(1) != hkv or d != HEAD_DIM:
+        raise RuntimeError("k_new / v_new shape must be [B, Hkv, 128] matching the pools")
+    if tuple(v_pages.shape) != tuple(k_pages.shape):
+        raise RuntimeError("v_pages shape mismatch")
+    if block_table.size(0) != b or positions.size(0) != b:
+        raise RuntimeError("block_table / positions batch mismatch")
+    fp = fc = ctr = None
+    if free_pages is not None:
+        _check_tensor(free_pages, "free_pages", torch.int32, 1)
+        if free_count is None or counters is None:
+            raise RuntimeError("a free-page list needs free_count and counters")
+        _check_tensor(free_count, "free_count", torch.int32, 1)
+        _check_tensor(counters, "counters", torch.int32, 1)
+        fp, fc, ctr = free_pages.data_ptr(), free_count.data_ptr(), counters.data_ptr()
+    _native.check(_native.load().pkv_kv_append(
+        k_new.data_ptr(), v_new.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(),
+        block_table.data_ptr(), positions.data_ptr(), fp, fc, ctr, b, hkv, d, k_pages.size(0),
+        k_pages.size(2), block_table.size(1), _DTYPES[dt], _stream()))
+
+
 def auto_workspace_bytes(batch: int, hq: int, hkv: int, sm_count: int = 0) -> int:
     """Workspace of ``paged_attention_auto`` (sm_count 0: the current device)."""
     return int(_native.load().pkv_auto_workspace_bytes(batch, hq, hkv, sm_count))

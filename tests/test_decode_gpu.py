@@ -10,6 +10,7 @@ from oracle import ref as ref_artefacts
 from persistentkv_attention_b200 import _native, ops
 from persistentkv_attention_b200.scheduler import Router
 from tests.golden.make_golden import smoke_inputs
+from tests.helpers import DT as DT_
 from tests.helpers import MAX_ERR, assert_close, make_case
 
 pytestmark = pytest.mark.gpu
@@ -503,3 +504,73 @@ def test_step_graph_reused_across_steps():
                                out_rows=c.out_rows)
         assert_close(sg.out, want, "f16", f"graph step {n}")
     assert len(sg._graphs) == 2
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_kv_append_matches_oracle(dtype):
+    """KV append, bit-exact against the CPU restatement: rows that open a page
+    take pages from the free list in row order; the others write into pages
+    already mapped; then a decode over the appended tokens matches the oracle."""
+    gen = torch.Generator().manual_seed(95)
+    P, hkv, page, mp = 64, 8, 16, 8
+    k_pages = torch.randn(P, hkv, page, 128, generator=gen).to(DT_[dtype])
+    v_pages = torch.randn(P, hkv, page, 128, generator=gen).to(DT_[dtype])
+    B = 6
+    table = np.full((B, mp), 0, np.int32)
+    table[:, 0] = np.arange(B)            # every row owns one page already
+    table[:, 1] = np.arange(B) + 10
+    positions = np.array([16, 5, 32, 31, 0, 17], np.int32)   # rows 0, 2, 4 open a page
+    table[4, 0] = 0                       # row 4 opens page slot 0 (will be overwritten)
+    free = np.array([40, 41, 42, 43, 44], np.int32)
+    k_new = torch.randn(B, hkv, 128, generator=gen).to(DT_[dtype])
+    v_new = torch.randn(B, hkv, 128, generator=gen).to(DT_[dtype])
+    # oracle on copies (bit patterns carried through float32 views of 16-bit values)
+    kp_o, vp_o = k_pages.clone(), v_pages.clone()
+    tab_o = table.copy()
+    cnt_o, err_o = po.kv_append(k_new.numpy() if dtype == "f16" else k_new.view(torch.int16).numpy(),
+                                v_new.numpy() if dtype == "f16" else v_new.view(torch.int16).numpy(),
+                                kp_o.numpy() if dtype == "f16" else kp_o.view(torch.int16).numpy(),
+                                vp_o.numpy() if dtype == "f16" else vp_o.view(torch.int16).numpy(),
+                                tab_o, positions, free, 4)
+    dk, dv = k_pages.cuda(), v_pages.cuda()
+    dtab = torch.from_numpy(table).cuda()
+    fc = torch.tensor([4], dtype=torch.int32, device="cuda")
+    ctr = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.kv_append(k_new.cuda(), v_new.cuda(), dk, dv, dtab, torch.from_numpy(positions).cuda(),
+                  torch.from_numpy(free).cuda(), fc, ctr)
+    torch.cuda.synchronize()
+    assert err_o == 0 and cnt_o == 1
+    assert int(fc.item()) == cnt_o and int(ctr.item()) == 0
+    assert np.array_equal(dtab.cpu().numpy(), tab_o)
+    assert torch.equal(dk.cpu(), kp_o) and torch.equal(dv.cpu(), vp_o)
+    # the appended tokens are attended to by the decode
+    lens = positions + 1
+    q = torch.randn(B, 32, 128, generator=gen).to(DT_[dtype])
+    out = torch.empty(B, 32, 128, dtype=DT_[dtype], device="cuda")
+    ws = torch.empty(ops.auto_workspace_bytes(B, 32, hkv) // 4, device="cuda")
+    ops.paged_attention_auto(q.cuda(), dk, dv, dtab, torch.from_numpy(lens).cuda(), out, ws,
+                             merge_counters=torch.zeros(B, hkv, dtype=torch.int32, device="cuda"))
+    torch.cuda.synchronize()
+    want = po.paged_decode(q.float().numpy(), kp_o.float().numpy(), vp_o.float().numpy(), tab_o,
+                           seq_lens=lens)
+    assert_close(out, want, dtype, "decode after append")
+
+
+def test_kv_append_errors_are_flagged():
+    """List exhausted, position beyond the table, page outside the pool: the
+    rows write nothing and set their device error bits; no fault."""
+    P, hkv, page, mp = 8, 2, 16, 2
+    dk = torch.zeros(P, hkv, page, 128, dtype=torch.float16, device="cuda")
+    dv = torch.zeros_like(dk)
+    tab = torch.tensor([[1, 0], [99, 0], [2, 0], [3, 0]], dtype=torch.int32, device="cuda")
+    pos = torch.tensor([16, 3, 64, 32], dtype=torch.int32, device="cuda")   # 16 opens, 64 is past
+    k_new = torch.ones(4, hkv, 128, dtype=torch.float16, device="cuda")
+    free = torch.tensor([5], dtype=torch.int32, device="cuda")
+    fc = torch.tensor([0], dtype=torch.int32, device="cuda")               # empty list
+    ctr = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.kv_append(k_new, k_new, dk, dv, tab, pos, free, fc, ctr)
+    torch.cuda.synchronize()
+    code = _native.device_error(clear=True)
+    assert code & 0x80 and code & 0x2 and code & 0x1
+    assert float(dk.abs().sum()) == 0.0
+    assert int(fc.item()) == 0 and int(ctr.item()) == 0
