@@ -18,8 +18,9 @@ Reported (one JSON line on rank 0):
               256 MiB read (so no dirty lines are left for the timed step);
   e2e         tokens/s through the public API from host buffers
               (DecodeEngine.step_host -> pkv_engine_step_host): per step,
-              staging of lengths + block rows, H2D of metadata and pinned q
-              rows, decode, D2H of the output into pinned memory;
+              staging of lengths + block rows, a stage-in kernel copying
+              metadata and pinned q rows to the device, the decode (launched
+              behind it), output rows written into pinned host memory;
   roofline    algorithmic K/V bytes per step / step interval vs the measured
               HBM copy bandwidth;
   cpu_baseline the reference's own fp32 CPU decode (cpu_gqa_attention built

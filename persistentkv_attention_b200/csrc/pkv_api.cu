@@ -244,6 +244,7 @@ int box_rows_for(int page_size) { return page_size % 16 == 0 ? 16 : 8; }
 struct LaunchSpec {
     DecodeParams dp;
     bool merge;       // run the separate merge kernel after decode
+    bool pdl = false; // decode may launch early behind the previous kernel (it waits on it)
     int G;
     int box_rows;
     pkv_dtype dtype;
@@ -293,10 +294,27 @@ pkv_status launch_typed(const LaunchSpec& ls, const CUtensorMap& tk, const CUten
                         occ * ds->sm_count);
         }
     }
-    kern<<<grid, kThreads, smem, stream>>>(ls.dp, tk, tv);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess)
+    cudaError_t e;
+    if (ls.pdl) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, kern, ls.dp, tk, tv);
+    } else {
+        kern<<<grid, kThreads, smem, stream>>>(ls.dp, tk, tv);
+        e = cudaGetLastError();
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
         return fail(PKV_ERR_CUDA, "decode launch failed: %s", cudaGetErrorString(e));
+    }
     if (ls.merge) {
         MergeParams mp;
         mp.part_m = ls.dp.part_m;
@@ -692,7 +710,7 @@ pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* 
                        const int32_t* out_indices, void* output, float* state_out,
                        void* workspace, size_t workspace_bytes, int32_t* merge_counters,
                        int q_rows, int out_rows, void* stream,
-                       const pkv_exchange* xg = nullptr);
+                       const pkv_exchange* xg = nullptr, bool pdl = false);
 
 }  // namespace
 
@@ -733,7 +751,8 @@ namespace {
 pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* q_indices,
                        const int32_t* out_indices, void* output, float* state_out,
                        void* workspace, size_t workspace_bytes, int32_t* merge_counters,
-                       int q_rows, int out_rows, void* stream, const pkv_exchange* xg) {
+                       int q_rows, int out_rows, void* stream, const pkv_exchange* xg,
+                       bool pdl) {
     const int B = c.B, Hq = c.Hq, Hkv = c.Hkv;
     const int max_pages = c.max_pages, page_size = c.page_size;
     pkv_status st = check_common(c);
@@ -775,6 +794,7 @@ pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* 
     partition_workspace(ls.dp, workspace, slots);
     ls.merge = merge_counters == nullptr;
     if (xg != nullptr) xg_fill(ls.dp, *xg);
+    ls.pdl = pdl;
     return launch(ls, stream);
 }
 
@@ -878,6 +898,49 @@ pkv_status pkv_device_error(uint32_t* code, int clear) {
     *code = value;
     return ok_status();
 }
+
+// ------------------------------------------------------------ staged host step
+}  // extern "C"
+
+namespace pkv_internal {
+
+// Copies the host step's metadata and q rows (mapped pinned memory) into
+// device buffers with a short multi-CTA kernel; reading them from 296 CTAs
+// over the host link costs far more.  Sizes in bytes, multiples of 16.
+pkv_status stage_in(const void* src0, void* dst0, size_t bytes0, const void* src1, void* dst1,
+                    size_t bytes1, void* stream) {
+    const long long n0 = (long long)(bytes0 / 16), n1 = (long long)(bytes1 / 16);
+    const long long per_cta = 256LL * kStageInUnroll;
+    int grid = (int)((n0 + n1 + per_cta - 1) / per_cta);
+    if (grid < 1) grid = 1;
+    if (grid > 148) grid = 148;
+    pkv_stage_in_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint4*>(src0), static_cast<uint4*>(dst0), n0,
+        static_cast<const uint4*>(src1), static_cast<uint4*>(dst1), n1);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess)
+        return fail(PKV_ERR_CUDA, "stage-in launch failed: %s", cudaGetErrorString(e));
+    return ok_status();
+}
+
+// pkv_paged_attention_auto launched with programmatic dependent launch: its
+// CTAs start while the preceding stage-in kernel runs and wait for it before
+// their first metadata read.
+pkv_status auto_after_stage(const void* q_source, const void* k_pages, const void* v_pages,
+                            const int32_t* block_table, const int32_t* seq_lens, void* output,
+                            void* workspace, size_t workspace_bytes, int32_t* merge_counters,
+                            int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim,
+                            int physical_pages, int page_size, int max_pages, pkv_dtype dtype,
+                            void* stream) {
+    Common c{q_source, k_pages, v_pages, block_table, B, Hq, Hkv, head_dim,
+             physical_pages, page_size, max_pages, dtype};
+    return auto_common(c, seq_lens, nullptr, nullptr, output, nullptr, workspace,
+                       workspace_bytes, merge_counters, q_rows, out_rows, stream, nullptr, true);
+}
+
+}  // namespace pkv_internal
+
+extern "C" {
 
 // ------------------------------------------------------------ KV append
 pkv_status pkv_kv_append(const void* k_new, const void* v_new, void* k_pages, void* v_pages,

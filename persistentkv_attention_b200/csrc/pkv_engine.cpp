@@ -1,12 +1,13 @@
 // pkv_engine.cpp -- native host step of the decode engine (declared in
 // include/pkv_b200.h): one call takes a decode step from host buffers to
 // host buffers.  It stages the step's metadata (block-table rows, lengths)
-// in its own pinned memory and launches the device-scheduled decode
-// (pkv_paged_attention_auto, fused merge) on the caller's stream with host
-// pointers: the kernel reads metadata and query rows from pinned host
-// memory and writes the output rows into the caller's pinned buffer over
-// PCIe / C2C.  No separate copy is queued, which saves each copy's launch
-// and completion latency (several microseconds apiece).
+// in its own mapped pinned memory; a short multi-CTA stage-in kernel copies
+// metadata and the caller's pinned q rows to device buffers (a DMA copy
+// costs several microseconds of launch and completion latency apiece, and
+// reading host memory from every decode CTA costs far more); the
+// device-scheduled decode (fused merge) follows with programmatic dependent
+// launch, so its launch overlaps the stage-in, and writes the output rows
+// straight into the caller's pinned buffer.
 //
 // The reference harness does the same per step from Python
 // (tests/benchmark_serving_trace.py:838-946, run_persistentkv_step: tensors
@@ -24,6 +25,14 @@ namespace pkv_internal {
 // pkv_api.cu: records the message returned by pkv_last_error_message
 pkv_status set_error(pkv_status st, const char* msg);
 void clear_error();
+pkv_status stage_in(const void* src0, void* dst0, size_t bytes0, const void* src1, void* dst1,
+                    size_t bytes1, void* stream);
+pkv_status auto_after_stage(const void* q_source, const void* k_pages, const void* v_pages,
+                            const int32_t* block_table, const int32_t* seq_lens, void* output,
+                            void* workspace, size_t workspace_bytes, int32_t* merge_counters,
+                            int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim,
+                            int physical_pages, int page_size, int max_pages, pkv_dtype dtype,
+                            void* stream);
 }  // namespace pkv_internal
 
 namespace {
@@ -50,13 +59,15 @@ struct pkv_engine {
     int physical_pages, hq, hkv, page_size, max_batch, max_pages, device;
     pkv_dtype dtype;
     size_t elem;
-    // device: workspace, then merge counters
+    // device: staged metadata, staged q rows, workspace, merge counters
     char* dev;
+    int32_t* d_meta;
+    void* d_q;
     void* d_ws;
     size_t ws_bytes;
     int32_t* d_counters;
     // pinned staging [block table B * row_pages | seq_lens B] int32, read by
-    // the kernel in place
+    // the stage-in kernel
     int32_t* h_meta[kStaging];
     int32_t* dh_meta[kStaging];    // the same buffers as the device addresses them
     cudaEvent_t staged[kStaging];  // the launch that read staging buffer i has finished
@@ -94,10 +105,15 @@ pkv_status pkv_engine_create(const void* k_pages, const void* v_pages, int physi
     e->dtype = dtype;
     e->elem = 2;
     cudaGetDevice(&e->device);
-    const size_t meta_bytes = (size_t)max_batch * (max_pages + 1) * sizeof(int32_t);
+    // staging rounded up to whole 16-byte chunks for the stage-in copy
+    const size_t meta_bytes =
+        align_up((size_t)max_batch * (max_pages + 1) * sizeof(int32_t), 16);
+    const size_t q_bytes = (size_t)max_batch * Hq * kHeadDim * e->elem;
     e->ws_bytes = pkv_auto_workspace_bytes(max_batch, Hq, Hkv, 0);
     const size_t ctr_bytes = (size_t)max_batch * Hkv * sizeof(int32_t);
-    size_t off_c = align_up(e->ws_bytes, 256);
+    size_t off_q = align_up(meta_bytes, 256);
+    size_t off_ws = align_up(off_q + q_bytes, 256);
+    size_t off_c = align_up(off_ws + e->ws_bytes, 256);
     size_t total = off_c + ctr_bytes;
     cudaError_t err = e->ws_bytes == 0 ? cudaErrorInvalidValue
                                        : cudaMalloc(reinterpret_cast<void**>(&e->dev), total);
@@ -116,7 +132,9 @@ pkv_status pkv_engine_create(const void* k_pages, const void* v_pages, int physi
         pkv_engine_destroy(e);
         return efail(PKV_ERR_CUDA, "engine allocation failed: %s", cudaGetErrorString(err));
     }
-    e->d_ws = e->dev;
+    e->d_meta = reinterpret_cast<int32_t*>(e->dev);
+    e->d_q = e->dev + off_q;
+    e->d_ws = e->dev + off_ws;
     e->d_counters = reinterpret_cast<int32_t*>(e->dev + off_c);
     *out = e;
     pkv_internal::clear_error();
@@ -170,9 +188,12 @@ pkv_status pkv_engine_step_host(pkv_engine* e, const int32_t* seq_lens,
     std::memcpy(h + bt_words, seq_lens, (size_t)B * sizeof(int32_t));
     const size_t meta_bytes = (bt_words + B) * sizeof(int32_t);
     const size_t q_bytes = (size_t)B * e->hq * kHeadDim * e->elem;
-    int32_t* dh = e->dh_meta[i];
-    pkv_status st = pkv_paged_attention_auto(
-        e->mapped[0], e->k_pages, e->v_pages, dh, dh + bt_words, nullptr, nullptr, e->mapped[1],
+    pkv_status st = pkv_internal::stage_in(e->dh_meta[i], e->d_meta, align_up(meta_bytes, 16),
+                                           e->mapped[0], e->d_q, q_bytes, stream);
+    if (st != PKV_OK) return st;
+    // nothing between the two launches: the decode starts behind the stage-in
+    st = pkv_internal::auto_after_stage(
+        e->d_q, e->k_pages, e->v_pages, e->d_meta, e->d_meta + bt_words, e->mapped[1],
         e->d_ws,
         e->ws_bytes, e->d_counters, B, B, B, e->hq, e->hkv, kHeadDim, e->physical_pages,
         e->page_size, row_pages, e->dtype, stream);

@@ -790,6 +790,9 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // Launched behind a stage-in kernel (programmatic dependent launch), the
+    // CTA starts early and waits here for its metadata; otherwise a no-op.
+    griddep_wait();
     // The producer resolves its schedule and its first item before the
     // CTA-wide barrier, so those reads overlap the barrier setup.
     AutoCursor acur;
@@ -1465,6 +1468,38 @@ __global__ void __launch_bounds__(kHeadDim)
     }
     T* o = reinterpret_cast<T*>(out) + ((size_t)orow * Hq + qh) * kHeadDim;
     o[d] = ElemOps<T>::from_float(lsum > 0.f ? osum / lsum : 0.f);
+}
+
+// ------------------------------------------------------------------ stage-in
+// Copies n0 + n1 16-byte chunks (src0 -> dst0, then src1 -> dst1), each
+// thread keeping kStageInUnroll loads in flight: for sources in mapped host
+// memory, where one round trip is microseconds.
+constexpr int kStageInUnroll = 4;
+
+__global__ void __launch_bounds__(256)
+    pkv_stage_in_kernel(const uint4* __restrict__ src0, uint4* __restrict__ dst0, long long n0,
+                        const uint4* __restrict__ src1, uint4* __restrict__ dst1, long long n1) {
+    const long long total = n0 + n1;
+    const long long stride = (long long)gridDim.x * 256;
+    for (long long base = (long long)blockIdx.x * 256 + threadIdx.x; base < total;
+         base += stride * kStageInUnroll) {
+        uint4 v[kStageInUnroll];
+#pragma unroll
+        for (int k = 0; k < kStageInUnroll; ++k) {
+            const long long i = base + k * stride;
+            if (i < total) v[k] = i < n0 ? src0[i] : src1[i - n0];
+        }
+#pragma unroll
+        for (int k = 0; k < kStageInUnroll; ++k) {
+            const long long i = base + k * stride;
+            if (i < total) {
+                if (i < n0)
+                    dst0[i] = v[k];
+                else
+                    dst1[i - n0] = v[k];
+            }
+        }
+    }
 }
 
 // ------------------------------------------------------------------ KV append
