@@ -49,16 +49,6 @@ constexpr unsigned kErrNoPage = 0x80u;  // KV append: the free-page list ran out
 constexpr unsigned long long kPeerWaitLimitNs = 2000000000ull;
 constexpr int kMaxWorld = 8;
 
-__device__ __forceinline__ void st_release_sys_u32(unsigned* addr, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* addr) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
-    return v;
-}
-
 __device__ __forceinline__ unsigned ld_relaxed_gpu_u32(const unsigned* addr) {
     unsigned v;
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
