@@ -258,6 +258,8 @@ pkv_status launch_typed(const LaunchSpec& ls, const CUtensorMap& tk, const CUten
                         cudaStream_t stream, DeviceState* ds) {
     auto kern = pkv_decode_kernel<G, T, BR, kSlots, kLoadMode>;
     const size_t smem = decode_smem_bytes<G, kSlots>();
+    // the device schedule's grid (2 CTAs per SM) must be resident in one wave
+    static_assert(decode_fits_two_per_sm<G, kSlots>(), "decode CTA too large for 2 per SM");
     static std::atomic<unsigned long long> attr_done{0ull};
     int dev = 0;
     cudaGetDevice(&dev);

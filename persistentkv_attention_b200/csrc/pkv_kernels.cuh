@@ -633,8 +633,13 @@ constexpr size_t decode_smem_bytes() {
            (2 * NSLOTS + 2 * kDescSlots) * sizeof(uint64_t) + 64 +
            2 * 2 * kConsumerWarps * 8 * sizeof(float) +
            2 * DecodeSmem<G>::kMergeFloats * sizeof(float) +
-           merge_scratch_floats<kConsumerWarps>() * sizeof(float) +
-           (size_t)G * kStateStride * sizeof(float) /* sharded own state */;
+           merge_scratch_floats<kConsumerWarps>() * sizeof(float);
+}
+
+// Two decode CTAs share an SM (228 KB of shared memory, 1 KB reserved per CTA).
+template <int G, int NSLOTS>
+constexpr bool decode_fits_two_per_sm() {
+    return 2 * (decode_smem_bytes<G, NSLOTS>() + 1024) <= 228 * 1024;
 }
 
 // How the producer warp moves K/V pages into the ring.
@@ -786,7 +791,10 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     float* s_lstat = s_mstat + 2 * kConsumerWarps * 8;
     float* s_merge = s_lstat + 2 * kConsumerWarps * 8;
     float* s_mw = s_merge + 2 * DecodeSmem<G>::kMergeFloats;  // merge weights + stats
-    float* s_own = s_mw + merge_scratch_floats<kConsumerWarps>();  // [G][130] sharded own state
+    // [G][130] sharded own state lives in the half of the combine double
+    // buffer that the item's own combine loop does not read: half 1 after a
+    // merge (whose shared sums use half 0), else the half opposite `buf`.
+    static_assert(G * kStateStride <= DecodeSmem<G>::kMergeFloats, "own state fits");
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -1230,7 +1238,10 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                                       (!rect || it.tok_end > it.tok_begin);
         const bool xg_direct = direct && xg_mode && !aborted;
         XgSink xs{};
-        if (xg_mode) xs = xg_make_sink<G>(p, it.row, it.kvh, xg_epoch, s_own);
+        if (xg_mode) {
+            float* own = (direct && buf == 1) ? s_merge : s_merge + DecodeSmem<G>::kMergeFloats;
+            xs = xg_make_sink<G>(p, it.row, it.kvh, xg_epoch, own);
+        }
 #pragma unroll 1
         for (int idx = threadIdx.x; idx < G * kHeadDim; idx += kConsumerWarps * 32) {
             const int g = idx / kHeadDim;
