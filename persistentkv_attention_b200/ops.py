@@ -89,10 +89,15 @@ def _workspace(workspace: torch.Tensor):
     return workspace.data_ptr(), workspace.numel() * workspace.element_size()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream() -> int:
     """Raw ``cudaStream_t`` of the current stream on the current device (the
     raw getter avoids building a ``torch.cuda.Stream`` object per call)."""
-    return torch._C._cuda_getCurrentRawStream(torch.cuda.current_device())
+    if _raw_stream is not None:
+        return _raw_stream(torch.cuda.current_device())
+    return torch.cuda.current_stream().cuda_stream
 
 
 def _positive(value: int, name: str) -> None:

@@ -166,3 +166,33 @@ def test_engine_traces(trace):
         assert all(len(s.active_ids) == 64 for s in steps)
     used = sorted(p for r in reqs for p in r.physical_pages)
     assert len(used) == len(set(used)) and max(used) < physical
+
+
+def test_step_graph_staging_layout():
+    """StepGraph's staging of one step (host side only): rows beyond the batch
+    get length 0, q row 0 and the spare output row; short rows are padded with
+    their last page."""
+    import numpy as np
+    import torch
+
+    from persistentkv_attention_b200.serving import StepGraph
+
+    sg = StepGraph.__new__(StepGraph)
+    sg.max_batch, sg.max_pages, sg.q_rows, sg.out_rows = 4, 5, 6, 7
+    sg._words = 4 * 5 + 3 * 4
+    sg._stage = [torch.full((sg._words,), -9, dtype=torch.int32)]
+    rows = np.array([[3, 4], [7, 8]], np.int32)
+    sg._fill(0, np.array([20, 9], np.int32), rows, np.array([5, 2]), np.array([1, 0]))
+    v = sg._stage[0].numpy()
+    bt = v[:20].reshape(4, 5)
+    assert bt[0].tolist() == [3, 4, 4, 4, 4] and bt[1].tolist() == [7, 8, 8, 8, 8]
+    assert (bt[2:] == 0).all()
+    assert v[20:24].tolist() == [20, 9, 0, 0]
+    assert v[24:28].tolist() == [5, 2, 0, 0]
+    assert v[28:32].tolist() == [1, 0, 7, 7]
+    try:
+        sg._fill(0, np.zeros(5, np.int32), np.zeros((5, 2), np.int32), None, None)
+    except RuntimeError as e:
+        assert "exceeds" in str(e)
+    else:
+        raise AssertionError("oversized step accepted")
