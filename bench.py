@@ -294,7 +294,20 @@ def run_engine_arm(args) -> None:
     k_pages = torch.randn(physical, hkv, PAGE, D, generator=gen, device=dev).to(tdt)
     v_pages = torch.randn(physical, hkv, PAGE, D, generator=gen, device=dev).to(tdt)
     q_pool = torch.randn(w["requests"], HQ, D, generator=gen, device=dev).to(tdt)
-    engine = DecodeEngine(k_pages, v_pages, HQ, fused=not args.no_fused)
+    kv_elem = 2
+    kv_scales = None
+    if args.kv_fp8:
+        # e4m3 cache with per-tensor scales; the pools below hold the
+        # dequantised values for the correctness gate and the CPU baseline
+        kv_scales = (float(k_pages.abs().max()) / 448.0, float(v_pages.abs().max()) / 448.0)
+        k8 = (k_pages.float() / kv_scales[0]).to(torch.float8_e4m3fn)
+        v8 = (v_pages.float() / kv_scales[1]).to(torch.float8_e4m3fn)
+        k_pages = (k8.float() * kv_scales[0]).to(tdt)
+        v_pages = (v8.float() * kv_scales[1]).to(tdt)
+        kv_elem = 1
+        engine = DecodeEngine(k8, v8, HQ, fused=not args.no_fused, kv_scales=kv_scales)
+    else:
+        engine = DecodeEngine(k_pages, v_pages, HQ, fused=not args.no_fused)
     flush = L2Flush(dev)
     stream = torch.cuda.Stream(dev)
 
@@ -334,7 +347,7 @@ def run_engine_arm(args) -> None:
         barrier()
     times_ms = [a.elapsed_time(b) for a, b in ev]
     tokens = sum(plans[j].batch for j in sched[args.warmup:])
-    bytes_alg = sum(kv_bytes(steps[j], hkv) for j in sched[args.warmup:])
+    bytes_alg = sum(kv_bytes(steps[j], hkv, kv_elem) for j in sched[args.warmup:])
     total_ms = sum(times_ms)
     launches = args.steps * (1 if not args.no_fused else 2)
     code = _native.device_error(clear=True)
@@ -376,15 +389,16 @@ def run_engine_arm(args) -> None:
         v = plan.views(plan.buf)
         host_rows.append((list(state.lengths), v["block_table"].numpy().copy(),
                           torch.stack([q_host[r] for r in state.active_ids]).pin_memory()))
-    engine.reserve_host(scratch, max(len(r[0]) for r in host_rows),
-                        max(r[1].shape[1] for r in host_rows))
+    if not engine.kv8:
+        engine.reserve_host(scratch, max(len(r[0]) for r in host_rows),
+                            max(r[1].shape[1] for r in host_rows))
     with torch.cuda.stream(stream):
-        for j in sched[: args.warmup]:
+        for j in (sched[: args.warmup] if not engine.kv8 else []):
             lens, rows, qh = host_rows[j]
             engine.step_host(lens, rows, qh, out_host, scratch)
             stream.synchronize()
         barrier()
-        for i, j in enumerate(sched[args.warmup:]):
+        for i, j in enumerate(sched[args.warmup:] if not engine.kv8 else []):
             lens, rows, qh = host_rows[j]
             flush(i)
             stream.synchronize()
@@ -395,7 +409,7 @@ def run_engine_arm(args) -> None:
             bi += h
             bo += d
         barrier()
-    e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev)
+    e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev) if not engine.kv8 else 0.0
 
     # ---- aggregate over ranks (max time, summed tokens)
     stats = torch.tensor([total_ms, e2e_ms, float(tokens), float(bytes_alg)], dtype=torch.float64,
@@ -422,7 +436,8 @@ def run_engine_arm(args) -> None:
     # committed ncu capture of this workload, applied to this run's launches.
     traffic = None
     tpath = REPO / "profiles" / f"traffic_{args.workload}.json"
-    if tpath.exists() and hkv == 8 and args.dtype == "f16" and TRACE_FILE is None:
+    if (tpath.exists() and hkv == 8 and args.dtype == "f16" and TRACE_FILE is None
+            and not args.kv_fp8):
         ratio = json.loads(tpath.read_text()).get("traffic_over_algorithmic")
         if ratio:
             traffic = {"bytes_per_launch": ratio * per_step_bytes, "over_algorithmic": ratio,
@@ -431,7 +446,7 @@ def run_engine_arm(args) -> None:
         "metric": "decode-step tokens/s", "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": args.dtype,
+        "vs_baseline": None, "dtype": args.dtype + ("; K/V e4m3" if args.kv_fp8 else ""),
         "data": "synthetic (seeded trace, K/V/q ~ N(0,1))",
         "config": {
             "workload": f"{args.workload}: {w['desc']}", "hq": HQ, "hkv": hkv, "gqa_group": HQ // hkv,
@@ -448,8 +463,11 @@ def run_engine_arm(args) -> None:
                      "frac": achieved / peak, "traffic": traffic,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                      "kernel": "pkv_decode_kernel (fused merge), 1 launch per step"},
-        "e2e": {"value": tokens / (e2e_ms / 1000.0), "unit": "tokens/s",
-                "h2d_bytes_per_step": bi // args.steps, "d2h_bytes_per_step": bo // args.steps},
+        "e2e": ({"value": tokens / (e2e_ms / 1000.0), "unit": "tokens/s",
+                 "h2d_bytes_per_step": bi // args.steps, "d2h_bytes_per_step": bo // args.steps}
+                if not args.kv_fp8 else
+                {"value": None, "unit": "tokens/s",
+                 "note": "the native host step serves 16-bit caches only"}),
         "gpu_launches": launches,
         "correctness_max_abs_err": max_err,
     }
@@ -633,6 +651,8 @@ def main() -> None:
     ap.add_argument("--hkv", type=int, choices=[32, 8, 4], default=0,
                     help="KV heads (G = 32 / hkv); default: the workload's (8)")
     ap.add_argument("--dtype", choices=sorted(DTYPES), default="f16")
+    ap.add_argument("--kv-fp8", action="store_true",
+                    help="e4m3 K/V cache with per-tensor scales (q / output fp16)")
     ap.add_argument("--no-fused", action="store_true", help="separate PDL merge kernel")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seq-shard", action="store_true",
@@ -642,6 +662,8 @@ def main() -> None:
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.kv_fp8 and args.dtype != "f16":
+        ap.error("--kv-fp8 computes with fp16 q / output (--dtype f16)")
     global TRACE_FILE
     TRACE_FILE = args.trace_file
     if args.impl == "reference":

@@ -208,6 +208,21 @@ pkv_status pkv_paged_attention_sharded(
     int physical_pages, int page_size, int max_pages,
     pkv_dtype dtype, void* stream);
 
+/* ---- e4m3 (FP8) K/V cache ----
+ * pkv_paged_attention_auto over pools of e4m3 values (one byte per element,
+ * [P][Hkv][page][128]) with per-tensor scales: K = k_scale * e4m3 value,
+ * V = v_scale * e4m3 value.  q and output are fp16.  Half the bytes per
+ * token of the fp16 cache; the tensor-core math runs in fp16 (every e4m3
+ * value is exact in fp16) with fp32 accumulation.  No counterpart in the
+ * reference, which is fp16-only. */
+pkv_status pkv_paged_attention_auto_fp8(
+    const void* q_source, const void* k_pages, const void* v_pages, float k_scale,
+    float v_scale, const int32_t* block_table, const int32_t* seq_lens,
+    const int32_t* q_indices, const int32_t* out_indices, void* output,
+    void* workspace, size_t workspace_bytes, int32_t* merge_counters,
+    int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim,
+    int physical_pages, int page_size, int max_pages, void* stream);
+
 /* ---- KV append (the write side of a decode step) ----
  * Writes one new token per row into the paged pools: row b's k_new[b] /
  * v_new[b] ([B][Hkv][128], same 16-bit dtype as the pools) land at token

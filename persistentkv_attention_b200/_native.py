@@ -8,7 +8,7 @@ is no fallback path (build it with ``python -m persistentkv_attention_b200.build
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, c_char_p, c_double, c_int, c_int32, c_size_t, c_uint32, c_void_p
+from ctypes import POINTER, c_char_p, c_double, c_float, c_int, c_int32, c_size_t, c_uint32, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "lib" / "libpkv_b200.so"
@@ -107,6 +107,11 @@ SIGNATURES = {
         c_int,
         [_P, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, c_int, c_int, c_int, c_int, c_int,
          c_int, c_int, c_int, c_int, _P],
+    ),
+    "pkv_paged_attention_auto_fp8": (
+        c_int,
+        [_P, _P, _P, c_float, c_float, _P, _P, _P, _P, _P, _P, c_size_t, _P, c_int, c_int,
+         c_int, c_int, c_int, c_int, c_int, c_int, c_int, _P],
     ),
     "pkv_kv_append": (
         c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int,

@@ -245,6 +245,7 @@ struct LaunchSpec {
     DecodeParams dp;
     bool merge;       // run the separate merge kernel after decode
     bool pdl = false; // decode may launch early behind the previous kernel (it waits on it)
+    bool kv8 = false; // e4m3 K/V pools (cp.async producer; no tensor maps)
     int G;
     int box_rows;
     pkv_dtype dtype;
@@ -253,10 +254,10 @@ struct LaunchSpec {
     long long rows;
 };
 
-template <int G, typename T, int BR>
+template <int G, typename T, int BR, bool KV8 = false>
 pkv_status launch_typed(const LaunchSpec& ls, const CUtensorMap& tk, const CUtensorMap& tv,
                         cudaStream_t stream, DeviceState* ds) {
-    auto kern = pkv_decode_kernel<G, T, BR, kSlots, kLoadMode>;
+    auto kern = pkv_decode_kernel<G, T, BR, kSlots, KV8 ? kLoadCpAsync : kLoadMode, KV8>;
     const size_t smem = decode_smem_bytes<G, kSlots>();
     // the device schedule's grid (2 CTAs per SM) must be resident in one wave
     static_assert(decode_fits_two_per_sm<G, kSlots>(), "decode CTA too large for 2 per SM");
@@ -356,14 +357,14 @@ pkv_status launch_typed(const LaunchSpec& ls, const CUtensorMap& tk, const CUten
     return ok_status();
 }
 
-template <typename T, int BR>
+template <typename T, int BR, bool KV8 = false>
 pkv_status launch_g(const LaunchSpec& ls, const CUtensorMap& tk, const CUtensorMap& tv,
                     cudaStream_t s, DeviceState* ds) {
     switch (ls.G) {
-        case 1: return launch_typed<1, T, BR>(ls, tk, tv, s, ds);
-        case 2: return launch_typed<2, T, BR>(ls, tk, tv, s, ds);
-        case 4: return launch_typed<4, T, BR>(ls, tk, tv, s, ds);
-        case 8: return launch_typed<8, T, BR>(ls, tk, tv, s, ds);
+        case 1: return launch_typed<1, T, BR, KV8>(ls, tk, tv, s, ds);
+        case 2: return launch_typed<2, T, BR, KV8>(ls, tk, tv, s, ds);
+        case 4: return launch_typed<4, T, BR, KV8>(ls, tk, tv, s, ds);
+        case 8: return launch_typed<8, T, BR, KV8>(ls, tk, tv, s, ds);
         default: return fail(PKV_ERR_UNSUPPORTED, "unsupported G=%d", ls.G);
     }
 }
@@ -375,11 +376,17 @@ pkv_status launch(LaunchSpec& ls, void* stream_ptr) {
     if (st != PKV_OK) return st;
     ls.dp.error = ds->error_word;
     CUtensorMap tk, tv;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    if (ls.kv8) {  // the cp.async producer needs no tensor maps
+        std::memset(&tk, 0, sizeof(tk));
+        std::memset(&tv, 0, sizeof(tv));
+        return ls.box_rows == 16 ? launch_g<__half, 16, true>(ls, tk, tv, stream, ds)
+                                 : launch_g<__half, 8, true>(ls, tk, tv, stream, ds);
+    }
     st = kv_tensor_map(ls.k, ls.rows, ls.dtype, ls.box_rows, &tk);
     if (st != PKV_OK) return st;
     st = kv_tensor_map(ls.v, ls.rows, ls.dtype, ls.box_rows, &tv);
     if (st != PKV_OK) return st;
-    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     if (ls.dtype == PKV_DTYPE_F16) {
         return ls.box_rows == 16 ? launch_g<__half, 16>(ls, tk, tv, stream, ds)
                                  : launch_g<__half, 8>(ls, tk, tv, stream, ds);
@@ -399,6 +406,7 @@ void fill_common(LaunchSpec& ls, const Common& c) {
     ls.dp.page_size = c.page_size;
     ls.dp.max_pages = c.max_pages;
     ls.dp.scale_log2 = (1.0f / sqrtf((float)kHeadDim)) * kLog2e;
+    ls.dp.v_scale = 1.0f;
     ls.dp.k_pages = static_cast<const uint8_t*>(c.k);
     ls.dp.v_pages = static_cast<const uint8_t*>(c.v);
     ls.G = c.Hq / c.Hkv;
@@ -712,7 +720,8 @@ pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* 
                        const int32_t* out_indices, void* output, float* state_out,
                        void* workspace, size_t workspace_bytes, int32_t* merge_counters,
                        int q_rows, int out_rows, void* stream,
-                       const pkv_exchange* xg = nullptr, bool pdl = false);
+                       const pkv_exchange* xg = nullptr, bool pdl = false,
+                       const float* kv8_scales = nullptr);
 
 }  // namespace
 
@@ -754,7 +763,7 @@ pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* 
                        const int32_t* out_indices, void* output, float* state_out,
                        void* workspace, size_t workspace_bytes, int32_t* merge_counters,
                        int q_rows, int out_rows, void* stream, const pkv_exchange* xg,
-                       bool pdl) {
+                       bool pdl, const float* kv8_scales) {
     const int B = c.B, Hq = c.Hq, Hkv = c.Hkv;
     const int max_pages = c.max_pages, page_size = c.page_size;
     pkv_status st = check_common(c);
@@ -797,6 +806,11 @@ pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* 
     ls.merge = merge_counters == nullptr;
     if (xg != nullptr) xg_fill(ls.dp, *xg);
     ls.pdl = pdl;
+    if (kv8_scales != nullptr) {
+        ls.kv8 = true;
+        ls.dp.scale_log2 *= kv8_scales[0];
+        ls.dp.v_scale = kv8_scales[1];
+    }
     return launch(ls, stream);
 }
 
@@ -943,6 +957,25 @@ pkv_status auto_after_stage(const void* q_source, const void* k_pages, const voi
 }  // namespace pkv_internal
 
 extern "C" {
+
+// ------------------------------------------------------------ e4m3 K/V
+pkv_status pkv_paged_attention_auto_fp8(
+    const void* q_source, const void* k_pages, const void* v_pages, float k_scale,
+    float v_scale, const int32_t* block_table, const int32_t* seq_lens,
+    const int32_t* q_indices, const int32_t* out_indices, void* output, void* workspace,
+    size_t workspace_bytes, int32_t* merge_counters, int B, int q_rows, int out_rows, int Hq,
+    int Hkv, int head_dim, int physical_pages, int page_size, int max_pages, void* stream) {
+    if (output == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "output must be a CUDA tensor");
+    if (!(k_scale > 0.f) || !(v_scale > 0.f) || !isfinite(k_scale) || !isfinite(v_scale))
+        return fail(PKV_ERR_INVALID_ARGUMENT, "k_scale and v_scale must be positive and finite");
+    // q / output are fp16; the pools are e4m3 rows of 128 bytes
+    Common c{q_source, k_pages, v_pages, block_table, B, Hq, Hkv, head_dim,
+             physical_pages, page_size, max_pages, PKV_DTYPE_F16};
+    const float scales[2] = {k_scale, v_scale};
+    return auto_common(c, seq_lens, q_indices, out_indices, output, nullptr, workspace,
+                       workspace_bytes, merge_counters, q_rows, out_rows, stream, nullptr, false,
+                       scales);
+}
 
 // ------------------------------------------------------------ KV append
 pkv_status pkv_kv_append(const void* k_new, const void* v_new, void* k_pages, void* v_pages,

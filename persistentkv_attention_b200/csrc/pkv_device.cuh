@@ -6,6 +6,7 @@
 #include <cuda.h>  // CUtensorMap (type only; the driver is reached at run time)
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 

@@ -47,7 +47,8 @@ struct DecodeParams {
     int num_pages, page_size, max_pages;
     int context, num_splits, num_items, total_slots;
     int auto_groups;   // > 0: device-side schedule over auto_groups x Hkv CTAs
-    float scale_log2;  // softmax scale * log2(e)
+    float scale_log2;  // softmax scale * log2(e) (times the K scale for e4m3 pools)
+    float v_scale;     // e4m3 pools: V scale, applied to each item's state
     // Sequence-sharded decode with the state exchange fused in (xg_world > 0):
     // rank r's gather buffer of LL words [2 parities][world][xg_bcap][Hq][130],
     // mapped into this process for every rank, and this rank's
@@ -762,13 +763,42 @@ __device__ __forceinline__ void xg_collect(const DecodeParams& p, int row, int k
     consumer_bar_sync();  // the own-state buffer is reused by the next row
 }
 
-template <int G, typename T, int BOX_ROWS, int NSLOTS, int LOAD>
+// 16 e4m3 values (elements [16c, 16c + 16) of token t, chunk q = 8t + c of a
+// row-major e4m3 stage) to fp16, stored as two 16-byte chunks of the stage's
+// swizzled 16-bit layout (lo / hi half of 64 elements, 128-byte rows).
+__device__ __forceinline__ void expand_e4m3_chunk(uint8_t* half_base, int q, uint4 raw) {
+    const int t = q >> 3;
+    const int c = q & 7;
+    uint32_t w[8];
+    const uint32_t in[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half2_raw lo =
+            __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(in[i] & 0xffffu), __NV_E4M3);
+        const __half2_raw hi =
+            __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(in[i] >> 16), __NV_E4M3);
+        w[2 * i] = (uint32_t)lo.x | ((uint32_t)lo.y << 16);
+        w[2 * i + 1] = (uint32_t)hi.x | ((uint32_t)hi.y << 16);
+    }
+    uint8_t* row = half_base + (c >> 2) * (kStageTokens * kHalfRowBytes) + t * kHalfRowBytes;
+    const int cc = 2 * (c & 3);
+    *reinterpret_cast<uint4*>(row + ((cc ^ (t & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(row + (((cc + 1) ^ (t & 7)) << 4)) =
+        make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+// KV8: the K/V pools hold e4m3 (one byte per element) with per-tensor scales;
+// each consumer warp expands its stage to the 16-bit layout in place and the
+// math below is unchanged (the K scale is folded into scale_log2, the V scale
+// is applied to each item's state).  q and output stay 16-bit.
+template <int G, typename T, int BOX_ROWS, int NSLOTS, int LOAD, bool KV8 = false>
 __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     pkv_decode_kernel(const __grid_constant__ DecodeParams p,
                       const __grid_constant__ CUtensorMap tmap_k,
                       const __grid_constant__ CUtensorMap tmap_v) {
     static_assert(G == 1 || G == 2 || G == 4 || G == 8, "G must be 1, 2, 4 or 8");
     static_assert(BOX_ROWS == 8 || BOX_ROWS == 16, "box rows must be 8 or 16");
+    static_assert(!KV8 || (LOAD == kLoadCpAsync && sizeof(T) == 2), "e4m3 K/V: cp.async only");
     constexpr int kBoxesPerStage = kStageTokens / BOX_ROWS;
     constexpr int kStagesPerBatch = 32 / kBoxesPerStage;
     constexpr int kBoxBytes = BOX_ROWS * kHalfRowBytes;
@@ -976,6 +1006,28 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                         const int yb = __shfl_sync(0xffffffffu, y, st * kBoxesPerStage + kBoxesPerStage - 1);
                         const bool okb = __shfl_sync(0xffffffffu, ok, st * kBoxesPerStage + kBoxesPerStage - 1);
                         const int t0 = it.tok_begin + (base / kBoxesPerStage + st) * kStageTokens;
+                        if constexpr (KV8) {
+                            // e4m3 rows are 128 B: K into bytes [4096, 6144) of the slot, V
+                            // into [6144, 8192), row-major; lane copies chunk (lane & 7) of
+                            // tokens (lane >> 3) + 4k
+                            const uint32_t sd8 = ring_base + slot * kSlotBytes + kSlotBytes / 2;
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const int t = (lane >> 3) + 4 * k;
+                                const int c = lane & 7;
+                                const bool second = BOX_ROWS == 8 && t >= 8;
+                                const bool valid = (second ? okb : oka) && t0 + t < it.tok_end;
+                                const size_t row = valid ? (size_t)((second ? yb : ya) + (t & (BOX_ROWS - 1))) : 0;
+                                const size_t off = row * kHeadDim + c * 16;
+                                const uint32_t dst = sd8 + t * kHeadDim + c * 16;
+                                const uint32_t nbytes = valid ? 16u : 0u;
+                                cp_async_16(dst, p.k_pages + off, nbytes, policy);
+                                cp_async_16(dst + kStageTokens * kHeadDim, p.v_pages + off, nbytes, policy);
+                            }
+                            cp_async_mbar_arrive_noinc(&full_bar[slot]);
+                            ++gstage;
+                            continue;
+                        }
                         const uint32_t sdst = ring_base + slot * kSlotBytes + ph * (kStageTokens * kHalfRowBytes);
 #pragma unroll
                         for (int k = 0; k < 8; ++k) {
@@ -1112,6 +1164,28 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
             const int valid = min(kStageTokens, it.tok_end - t0);
             uint8_t* sbase = ring + (size_t)slot * kSlotBytes;
             const uint32_t sbase_u32 = ring_u32 + slot * kSlotBytes;
+            if constexpr (KV8) {
+                // Expand the stage from e4m3 rows (bytes [4096, 8192) of the slot)
+                // to the 16-bit swizzled layout the fragments below read: K first
+                // (its 16-bit rows, bytes [0, 4096), do not overlap the e4m3 rows),
+                // then V from registers once every lane has read its bytes.
+                const uint8_t* k8 = sbase + kSlotBytes / 2;
+                const uint8_t* v8 = k8 + kStageTokens * kHeadDim;
+                uint4 vr[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    vr[k] = *reinterpret_cast<const uint4*>(v8 + (lane + 32 * k) * 16);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int q = lane + 32 * k;
+                    expand_e4m3_chunk(sbase, q, *reinterpret_cast<const uint4*>(k8 + q * 16));
+                }
+                __syncwarp();
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    expand_e4m3_chunk(sbase + 2 * kStageTokens * kHalfRowBytes, lane + 32 * k, vr[k]);
+                __syncwarp();
+            }
             if (LOAD == kLoadTma && valid < kStageTokens) {
                 // Rows past the row's last token may hold anything (stale
                 // slot contents, unwritten pool memory): zero V there so that
@@ -1258,6 +1332,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                 osum = fmaf(wt, mbuf[(w * G + g) * DecodeSmem<G>::kMergeStride + d], osum);
             }
             const float mnat = mx == -INFINITY ? kNegFltMax : mx * kLn2;
+            if constexpr (KV8) osum *= p.v_scale;
             if (direct) {
                 if (xg_direct) {
                     emit_merged<T, true>(g, d, osum, mnat, lsum, nullptr, nullptr, xs);

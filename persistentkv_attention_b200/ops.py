@@ -444,6 +444,53 @@ def paged_attention_sharded(q_source, k_pages, v_pages, block_table, seq_lens, o
         _stream()))
 
 
+def paged_attention_auto_fp8(q_source, k_pages, v_pages, k_scale: float, v_scale: float,
+                             block_table, seq_lens, output, workspace, q_indices=None,
+                             out_indices=None, merge_counters=None) -> None:
+    """``paged_attention_auto`` over an e4m3 (``torch.float8_e4m3fn``) K/V cache
+    with per-tensor scales (K = k_scale * k_pages, V = v_scale * v_pages); q and
+    output are fp16.  No counterpart in the reference."""
+    _check_tensor(q_source, "q_source", torch.float16, 3)
+    _check_tensor(k_pages, "k_pages", torch.float8_e4m3fn, 4)
+    _check_tensor(v_pages, "v_pages", torch.float8_e4m3fn, 4)
+    _check_tensor(block_table, "block_table", torch.int32, 2)
+    _check_tensor(seq_lens, "seq_lens", torch.int32, 1)
+    _check_tensor(output, "output", torch.float16, 3)
+    if tuple(v_pages.shape) != tuple(k_pages.shape) or k_pages.size(3) != HEAD_DIM:
+        raise RuntimeError("k_pages / v_pages shape mismatch")
+    hkv, physical_pages, page_size = k_pages.size(1), k_pages.size(0), k_pages.size(2)
+    b = block_table.size(0)
+    hq, d = q_source.size(1), q_source.size(2)
+    if d != HEAD_DIM:
+        raise RuntimeError("PersistentKV extension currently requires d=128")
+    if seq_lens.size(0) != b:
+        raise RuntimeError("seq_lens batch mismatch")
+    if not (output.size(1) == hq and output.size(2) == d):
+        raise RuntimeError("output shape must match q head dimensions")
+    ptrs = []
+    for name, t in (("q_indices", q_indices), ("out_indices", out_indices)):
+        if t is None:
+            ptrs.append(None)
+        else:
+            _check_tensor(t, name, torch.int32, 1)
+            if t.size(0) != b:
+                raise RuntimeError(f"{name} batch mismatch")
+            ptrs.append(t.data_ptr())
+    ctr = None
+    if merge_counters is not None:
+        _check_tensor(merge_counters, "merge_counters", torch.int32, 2)
+        if not (merge_counters.size(0) == b and merge_counters.size(1) == hkv):
+            raise RuntimeError("merge_counters shape mismatch")
+        ctr = merge_counters.data_ptr()
+    _check_supported_gqa(hq, hkv)
+    ws_ptr, ws_bytes = _workspace(workspace)
+    _native.check(_native.load().pkv_paged_attention_auto_fp8(
+        q_source.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), float(k_scale),
+        float(v_scale), block_table.data_ptr(), seq_lens.data_ptr(), ptrs[0], ptrs[1],
+        output.data_ptr(), ws_ptr, ws_bytes, ctr, b, q_source.size(0), output.size(0), hq, hkv,
+        d, physical_pages, page_size, block_table.size(1), _stream()))
+
+
 def kv_append(k_new, v_new, k_pages, v_pages, block_table, positions, free_pages=None,
               free_count=None, counters=None) -> None:
     """Writes one new token per row into the paged pools (``pkv_kv_append``).

@@ -88,13 +88,19 @@ class DecodeEngine:
 
     def __init__(self, k_pages: torch.Tensor, v_pages: torch.Tensor, hq: int,
                  router: Router | None = None, policy: str = "device", fused: bool = True,
-                 requested_splits: int = 0):
+                 requested_splits: int = 0, kv_scales: tuple[float, float] | None = None):
+        """``kv_scales`` = (k_scale, v_scale) for ``torch.float8_e4m3fn`` pools
+        (q and output are then fp16; device schedule only)."""
         self.k_pages = k_pages
         self.v_pages = v_pages
         self.hq = hq
         self.hkv = k_pages.shape[1]
         self.page_size = k_pages.shape[2]
-        self.dtype = k_pages.dtype
+        self.kv8 = k_pages.dtype == torch.float8_e4m3fn
+        self.dtype = torch.float16 if self.kv8 else k_pages.dtype
+        if self.kv8 and (kv_scales is None or policy != "device"):
+            raise RuntimeError("an e4m3 K/V cache needs kv_scales and the device schedule")
+        self.kv_scales = kv_scales
         self.device = k_pages.device
         if router is None:
             sms = torch.cuda.get_device_properties(self.device).multi_processor_count
@@ -181,6 +187,12 @@ class DecodeEngine:
     def run(self, plan: StepPlan, q_source: torch.Tensor, out: torch.Tensor) -> None:
         f = plan.fields
         counters = self._counters[: plan.batch * self.hkv].view(plan.batch, self.hkv)
+        if self.kv8:
+            ops.paged_attention_auto_fp8(
+                q_source, self.k_pages, self.v_pages, self.kv_scales[0], self.kv_scales[1],
+                f["block_table"], f["seq_lens"], out, self._workspace, f["q_indices"],
+                f["out_indices"], counters if self.fused else None)
+            return
         if self.policy == "device":
             ops.paged_attention_auto(
                 q_source, self.k_pages, self.v_pages, f["block_table"], f["seq_lens"], out,
@@ -269,6 +281,8 @@ class DecodeEngine:
         (``pkv_engine_step_host``); a host-built work queue takes the Python
         path below.
         """
+        if self.kv8:
+            raise RuntimeError("the native host step serves 16-bit K/V caches")
         if self.policy == "device":
             return self._step_host_native(seq_lens, block_rows, q_host, out_host, scratch)
         plan = self.plan_step(seq_lens, block_rows, out=scratch.get("stage"))

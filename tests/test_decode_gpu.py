@@ -574,3 +574,32 @@ def test_kv_append_errors_are_flagged():
     assert code & 0x80 and code & 0x2 and code & 0x1
     assert float(dk.abs().sum()) == 0.0
     assert int(fc.item()) == 0 and int(ctr.item()) == 0
+
+
+@pytest.mark.parametrize("fused", [False, True])
+@pytest.mark.parametrize("g,page", [(4, 16), (1, 16), (8, 16), (4, 8)])
+def test_auto_route_fp8_kv(fused, g, page):
+    """e4m3 K/V cache with per-tensor scales against the oracle on the
+    dequantized values (every e4m3 value is exact in fp16 and fp64)."""
+    lens = [0] + EDGE_LENS + [9000, 4096, 20000]
+    c = make_case(lens, hq=32, hkv=32 // g, page_size=page, seed=120 + g + page, indexed=True)
+    kf, vf = c.k_pages.float(), c.v_pages.float()
+    k_scale = float(kf.abs().max()) / 448.0
+    v_scale = float(vf.abs().max()) / 448.0
+    k8 = (kf / k_scale).to(torch.float8_e4m3fn)
+    v8 = (vf / v_scale).to(torch.float8_e4m3fn)
+    kd = k8.float().numpy() * k_scale
+    vd = v8.float().numpy() * v_scale
+    want = po.paged_decode(c.q_source.float().numpy(), kd, vd, c.block_table,
+                           seq_lens=c.seq_lens, q_indices=c.q_indices,
+                           out_indices=c.out_indices, out_rows=c.out_rows)
+    d = c.cuda()
+    b = len(lens)
+    out = torch.full((c.out_rows, 32, 128), float("nan"), device="cuda", dtype=torch.float16)
+    ws = torch.empty(ops.auto_workspace_bytes(b, 32, c.hkv) // 4, device="cuda")
+    counters = torch.zeros(b, c.hkv, device="cuda", dtype=torch.int32)
+    ops.paged_attention_auto_fp8(d["q_source"], k8.cuda(), v8.cuda(), k_scale, v_scale,
+                                 d["block_table"], d["seq_lens"], out, ws, d["q_indices"],
+                                 d["out_indices"], counters if fused else None)
+    torch.cuda.synchronize()
+    assert_close(out, want, "f16", f"fp8 kv G{g} page{page} fused={fused}")
