@@ -7,7 +7,10 @@
 // reading host memory from every decode CTA costs far more); the
 // device-scheduled decode (fused merge) follows with programmatic dependent
 // launch, so its launch overlaps the stage-in, and writes the output rows
-// straight into the caller's pinned buffer.
+// straight into the caller's pinned buffer.  The two launches of a step are
+// captured once per (batch, staging buffer, output buffer) and replayed as a
+// CUDA graph afterwards, one launch call per step; a new q buffer only
+// updates the stage-in node's source pointer.
 //
 // The reference harness does the same per step from Python
 // (tests/benchmark_serving_trace.py:838-946, run_persistentkv_step: tensors
@@ -18,6 +21,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <vector>
 
 #include "pkv_b200.h"
 
@@ -39,6 +43,16 @@ namespace {
 
 constexpr int kHeadDim = 128;
 constexpr int kStaging = 2;  // pinned metadata buffers in rotation
+constexpr size_t kMaxGraphs = 16;
+
+struct StepGraph {
+    int B, staging;
+    const void* q;           // q source the stage-in node currently reads
+    void* out;
+    cudaGraph_t graph;       // kept: its stage-in node addresses updates of q
+    cudaGraphNode_t stage;   // the stage-in kernel node (the graph's root)
+    cudaGraphExec_t exec;
+};
 
 pkv_status efail(pkv_status st, const char* fmt, ...) {
     char buf[512];
@@ -66,14 +80,18 @@ struct pkv_engine {
     void* d_ws;
     size_t ws_bytes;
     int32_t* d_counters;
-    // pinned staging [block table B * row_pages | seq_lens B] int32, read by
-    // the stage-in kernel
+    // pinned staging [seq_lens (max_batch, 16-byte padded) | block table
+    // max_batch rows of max_pages] int32, read by the stage-in kernel; the same
+    // layout on the device, so a captured step serves every row width
+    size_t sl_words;
     int32_t* h_meta[kStaging];
     int32_t* dh_meta[kStaging];    // the same buffers as the device addresses them
     cudaEvent_t staged[kStaging];  // the launch that read staging buffer i has finished
     int next;
     const void* checked[2];        // last q / out host pointers found page-locked
     void* mapped[2];               // and their device addresses
+    std::vector<StepGraph> graphs;
+    bool no_graphs;                // capture failed or is impossible here: launch directly
 };
 
 extern "C" {
@@ -93,7 +111,6 @@ pkv_status pkv_engine_create(const void* k_pages, const void* v_pages, int physi
         max_pages <= 0)
         return efail(PKV_ERR_INVALID_ARGUMENT, "engine dimensions must be positive");
     pkv_engine* e = new pkv_engine();
-    std::memset(e, 0, sizeof(*e));
     e->k_pages = k_pages;
     e->v_pages = v_pages;
     e->physical_pages = physical_pages;
@@ -105,9 +122,9 @@ pkv_status pkv_engine_create(const void* k_pages, const void* v_pages, int physi
     e->dtype = dtype;
     e->elem = 2;
     cudaGetDevice(&e->device);
-    // staging rounded up to whole 16-byte chunks for the stage-in copy
+    e->sl_words = align_up((size_t)max_batch, 4);
     const size_t meta_bytes =
-        align_up((size_t)max_batch * (max_pages + 1) * sizeof(int32_t), 16);
+        align_up((e->sl_words + (size_t)max_batch * max_pages) * sizeof(int32_t), 16);
     const size_t q_bytes = (size_t)max_batch * Hq * kHeadDim * e->elem;
     e->ws_bytes = pkv_auto_workspace_bytes(max_batch, Hq, Hkv, 0);
     const size_t ctr_bytes = (size_t)max_batch * Hkv * sizeof(int32_t);
@@ -173,32 +190,111 @@ pkv_status pkv_engine_step_host(pkv_engine* e, const int32_t* seq_lens,
         e->checked[k] = host_ptrs[k];
         e->mapped[k] = attr.devicePointer;
     }
+    // every row must fit the block-table columns it brings
+    for (int r = 0; r < B; ++r) {
+        if (seq_lens[r] > row_pages * e->page_size)
+            return efail(PKV_ERR_INVALID_ARGUMENT,
+                         "seq_lens[%d] = %d exceeds row_pages * page_size = %d", r, seq_lens[r],
+                         row_pages * e->page_size);
+    }
     // staging buffer: wait until the launch that last read it has finished
     const int i = e->next;
     e->next = (e->next + 1) % kStaging;
-    cudaError_t err = cudaEventSynchronize(e->staged[i]);
+    cudaError_t err = cudaEventQuery(e->staged[i]);
+    if (err == cudaErrorNotReady) err = cudaEventSynchronize(e->staged[i]);
     if (err != cudaSuccess) {
         cudaGetLastError();
         return efail(PKV_ERR_CUDA, "waiting for the staging buffer failed: %s",
                      cudaGetErrorString(err));
     }
     int32_t* h = e->h_meta[i];
-    const size_t bt_words = (size_t)B * row_pages;
-    std::memcpy(h, block_table, bt_words * sizeof(int32_t));
-    std::memcpy(h + bt_words, seq_lens, (size_t)B * sizeof(int32_t));
-    const size_t meta_bytes = (bt_words + B) * sizeof(int32_t);
+    std::memcpy(h, seq_lens, (size_t)B * sizeof(int32_t));
+    int32_t* rows = h + e->sl_words;
+    for (int r = 0; r < B; ++r)
+        std::memcpy(rows + (size_t)r * e->max_pages, block_table + (size_t)r * row_pages,
+                    (size_t)row_pages * sizeof(int32_t));
+    const size_t meta_bytes = (e->sl_words + (size_t)B * e->max_pages) * sizeof(int32_t);
     const size_t q_bytes = (size_t)B * e->hq * kHeadDim * e->elem;
-    pkv_status st = pkv_internal::stage_in(e->dh_meta[i], e->d_meta, align_up(meta_bytes, 16),
-                                           e->mapped[0], e->d_q, q_bytes, stream);
-    if (st != PKV_OK) return st;
-    // nothing between the two launches: the decode starts behind the stage-in
-    st = pkv_internal::auto_after_stage(
-        e->d_q, e->k_pages, e->v_pages, e->d_meta, e->d_meta + bt_words, e->mapped[1],
-        e->d_ws,
-        e->ws_bytes, e->d_counters, B, B, B, e->hq, e->hkv, kHeadDim, e->physical_pages,
-        e->page_size, row_pages, e->dtype, stream);
-    if (st != PKV_OK) return st;  // message already recorded
-    err = cudaEventRecord(e->staged[i], static_cast<cudaStream_t>(stream));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+    auto enqueue = [&]() -> pkv_status {
+        pkv_status st = pkv_internal::stage_in(e->dh_meta[i], e->d_meta,
+                                               align_up(meta_bytes, 16), e->mapped[0], e->d_q,
+                                               q_bytes, stream);
+        if (st != PKV_OK) return st;
+        // nothing between the two launches: the decode starts behind the stage-in
+        return pkv_internal::auto_after_stage(
+            e->d_q, e->k_pages, e->v_pages, e->d_meta + e->sl_words, e->d_meta, e->mapped[1],
+            e->d_ws, e->ws_bytes, e->d_counters, B, B, B, e->hq, e->hkv, kHeadDim,
+            e->physical_pages, e->page_size, e->max_pages, e->dtype, stream);
+    };
+    StepGraph* g = nullptr;
+    for (auto& x : e->graphs) {
+        if (x.B == B && x.staging == i && x.out == e->mapped[1]) {
+            g = &x;
+            break;
+        }
+    }
+    if (g != nullptr && g->q != e->mapped[0]) {
+        // same step shape, another q buffer: point the stage-in node at it
+        cudaKernelNodeParams kp;
+        err = cudaGraphKernelNodeGetParams(g->stage, &kp);
+        if (err == cudaSuccess) {
+            const void* src0 = e->dh_meta[i];
+            void* dst0 = e->d_meta;
+            long long n0 = (long long)(align_up(meta_bytes, 16) / 16);
+            const void* src1 = e->mapped[0];
+            void* dst1 = e->d_q;
+            long long n1 = (long long)(q_bytes / 16);
+            void* args[6] = {&src0, &dst0, &n0, &src1, &dst1, &n1};
+            kp.kernelParams = args;
+            kp.extra = nullptr;
+            err = cudaGraphExecKernelNodeSetParams(g->exec, g->stage, &kp);
+        }
+        if (err == cudaSuccess) {
+            g->q = e->mapped[0];
+        } else {
+            cudaGetLastError();
+            g = nullptr;  // run directly this time
+        }
+    }
+    pkv_status st = PKV_OK;
+    if (g != nullptr) {
+        err = cudaGraphLaunch(g->exec, s);
+        if (err != cudaSuccess) {
+            cudaGetLastError();
+            return efail(PKV_ERR_CUDA, "step graph launch failed: %s", cudaGetErrorString(err));
+        }
+    } else {
+        st = enqueue();  // this step runs directly (and sets kernel attributes once)
+        if (st != PKV_OK) return st;
+        if (!e->no_graphs && s != nullptr) {
+            // capture the same two launches for the next steps with this key
+            cudaGraph_t graph = nullptr;
+            cudaGraphExec_t exec = nullptr;
+            err = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+            pkv_status cst = err == cudaSuccess ? enqueue() : PKV_ERR_CUDA;
+            cudaError_t end = err == cudaSuccess ? cudaStreamEndCapture(s, &graph) : err;
+            cudaGraphNode_t root = nullptr;
+            size_t n_roots = 1;
+            if (cst == PKV_OK && end == cudaSuccess &&
+                cudaGraphGetRootNodes(graph, &root, &n_roots) == cudaSuccess && n_roots == 1 &&
+                cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess) {
+                if (e->graphs.size() >= kMaxGraphs) {
+                    cudaGraphExecDestroy(e->graphs.front().exec);
+                    cudaGraphDestroy(e->graphs.front().graph);
+                    e->graphs.erase(e->graphs.begin());
+                }
+                e->graphs.push_back(StepGraph{B, i, e->mapped[0], e->mapped[1], graph, root, exec});
+                graph = nullptr;
+            } else {
+                e->no_graphs = true;  // keep launching directly
+            }
+            if (graph != nullptr) cudaGraphDestroy(graph);
+            cudaGetLastError();
+        }
+    }
+    err = cudaEventRecord(e->staged[i], s);
     if (err != cudaSuccess) {
         cudaGetLastError();
         return efail(PKV_ERR_CUDA, "event record failed: %s", cudaGetErrorString(err));
@@ -215,6 +311,11 @@ pkv_status pkv_engine_destroy(pkv_engine* e) {
     cudaGetDevice(&prev);
     if (prev != e->device) cudaSetDevice(e->device);
     cudaDeviceSynchronize();
+    for (auto& g : e->graphs) {
+        cudaGraphExecDestroy(g.exec);
+        cudaGraphDestroy(g.graph);
+    }
+    e->graphs.clear();
     for (int i = 0; i < kStaging; ++i) {
         if (e->staged[i] != nullptr) cudaEventDestroy(e->staged[i]);
         if (e->h_meta[i] != nullptr) cudaFreeHost(e->h_meta[i]);

@@ -473,9 +473,24 @@ def test_native_host_step():
         out_host.fill_(float("nan"))
         h2d, d2h = engine.step_host(c.seq_lens[:b], c.block_table[:b], q_host, out_host, scratch)
         torch.cuda.current_stream().synchronize()
-        assert h2d == b * c.block_table.shape[1] * 4 + b * 4 + b * 32 * 128 * 2
+        nat = scratch["native"]
+        # staged metadata: lengths (padded to 16 bytes), then b rows of the engine's width
+        meta = (-(-nat.max_batch // 4) * 4 + b * nat.max_pages) * 4
+        assert h2d == meta + b * 32 * 128 * 2
         assert d2h == b * 32 * 128 * 2
         assert_close(out_host[:b], want[:b], "f16", f"native step B{b}")
+    # a side stream: the engine captures its two launches and replays them;
+    # alternating q buffers re-point the captured stage-in
+    s = torch.cuda.Stream()
+    q_other = c.q_source.clone().pin_memory()
+    with torch.cuda.stream(s):
+        for rep in range(4):
+            for b in (6, 3):
+                out_host.fill_(float("nan"))
+                qh = q_host if rep % 2 == 0 else q_other
+                engine.step_host(c.seq_lens[:b], c.block_table[:b], qh, out_host, scratch)
+                s.synchronize()
+                assert_close(out_host[:b], want[:b], "f16", f"graph-replayed native step B{b}")
     scratch["native"].close()
 
 
