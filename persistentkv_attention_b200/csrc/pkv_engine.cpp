@@ -268,7 +268,13 @@ pkv_status pkv_engine_step_host(pkv_engine* e, const int32_t* seq_lens,
     } else {
         st = enqueue();  // this step runs directly (and sets kernel attributes once)
         if (st != PKV_OK) return st;
-        if (!e->no_graphs && s != nullptr) {
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(s, &cap) != cudaSuccess) {
+            cudaGetLastError();
+            cap = cudaStreamCaptureStatusActive;
+        }
+        // not on the legacy default stream, and not inside the caller's own capture
+        if (!e->no_graphs && s != nullptr && cap == cudaStreamCaptureStatusNone) {
             // capture the same two launches for the next steps with this key
             cudaGraph_t graph = nullptr;
             cudaGraphExec_t exec = nullptr;
