@@ -125,3 +125,45 @@ def test_no_cpu_fallback_in_product_path():
     for path in (REPO / "persistentkv_attention_b200").rglob("*.py"):
         text = path.read_text()
         assert "import oracle" not in text and "from oracle" not in text, path
+
+
+def test_newer_entry_points_validate_before_touching_a_device(lib):
+    """The entry points beyond the reference's surface reject bad arguments
+    with a status and a message, before any device call."""
+    P = ctypes.c_void_p
+    # e4m3 cache: scales must be positive and finite
+    st = lib.pkv_paged_attention_auto_fp8(FAKE, FAKE, FAKE, 0.0, 1.0, FAKE, FAKE, None, None,
+                                          FAKE, FAKE, 1 << 20, None, 1, 1, 1, 32, 8, 128, 64,
+                                          16, 4, None)
+    assert st == 1 and b"k_scale and v_scale" in lib.pkv_last_error_message()
+    st = lib.pkv_paged_attention_auto_fp8(FAKE, FAKE, FAKE, 1.0, float("inf"), FAKE, FAKE, None,
+                                          None, FAKE, FAKE, 1 << 20, None, 1, 1, 1, 32, 8, 128,
+                                          64, 16, 4, None)
+    assert st == 1
+    # KV append: missing buffers, a free list without its counters, bad head_dim
+    st = lib.pkv_kv_append(None, FAKE, FAKE, FAKE, FAKE, FAKE, None, None, None, 4, 8, 128, 64,
+                           16, 8, 0, None)
+    assert st == 1 and b"k_new and v_new" in lib.pkv_last_error_message()
+    st = lib.pkv_kv_append(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, None, None, 4, 8, 128, 64,
+                           16, 8, 0, None)
+    assert st == 1 and b"free_count" in lib.pkv_last_error_message()
+    st = lib.pkv_kv_append(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, None, None, None, 4, 8, 64, 64,
+                           16, 8, 0, None)
+    assert st == 2 and b"d=128" in lib.pkv_last_error_message()
+    # exchange: world beyond PKV_MAX_WORLD, rank outside the world
+    out = P()
+    handle = ctypes.create_string_buffer(64)
+    assert lib.pkv_exchange_create(9, 0, 4, 32, 8, ctypes.byref(out), handle) == 2
+    assert lib.pkv_exchange_create(2, 2, 4, 32, 8, ctypes.byref(out), handle) == 1
+    assert lib.pkv_exchange_bytes(0, 4, 32, 8) == 0
+    assert lib.pkv_exchange_bytes(2, 4, 32, 8) == 256 + 2 * 2 * 4 * 32 * 130 * 8
+    # sharded step without an exchange
+    st = lib.pkv_paged_attention_sharded(FAKE, FAKE, FAKE, FAKE, FAKE, None, None, FAKE, FAKE,
+                                         1 << 20, FAKE, None, 1, 1, 1, 32, 8, 128, 64, 16, 4, 0,
+                                         None)
+    assert st == 1 and b"exchange" in lib.pkv_last_error_message()
+    # native engine: head_dim and dtype are checked first
+    eng = P()
+    assert lib.pkv_engine_create(FAKE, FAKE, 64, 32, 8, 64, 16, 0, 8, 32, ctypes.byref(eng)) == 2
+    assert lib.pkv_engine_create(FAKE, FAKE, 64, 32, 8, 128, 16, 7, 8, 32, ctypes.byref(eng)) == 2
+    assert lib.pkv_engine_destroy(None) == 0
