@@ -3,6 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
                     [--impl engine|reference] [--trace-file FILE]
+                    [--hkv 32|8|4] [--dtype f16|bf16] [--kv-fp8]
                     [--seq-shard [--exchange fused|nccl]]
 
 A step is one continuous-batching decode step of a seeded synthetic trace
