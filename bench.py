@@ -4,6 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
                     [--impl engine|reference] [--trace-file FILE]
                     [--hkv 32|8|4] [--dtype f16|bf16] [--kv-fp8]
+                    [--gather cpasync|tma] [--no-per-config] [--phase-stamps]
                     [--seq-shard [--exchange fused|nccl]]
 
 A step is one continuous-batching decode step of a seeded synthetic trace
@@ -21,23 +22,32 @@ Reported (one JSON line on rank 0):
               (DecodeEngine.step_host -> pkv_engine_step_host): per step,
               staging of lengths + block rows, a stage-in kernel copying
               metadata and pinned q rows to the device, the decode (launched
-              behind it), output rows written into pinned host memory;
+              behind it), output rows written into pinned host memory; with
+              the split of one step into host call, interval and decode;
   roofline    algorithmic K/V bytes per step / step interval vs the measured
               HBM copy bandwidth;
-  cpu_baseline the reference's own fp32 CPU decode (cpu_gqa_attention built
-              from its sources) on the host cores, bounded sample.
+  per_config  configs 1 and 3-5 (and the default config with the other
+              gather) measured in the same run, same timing method, each
+              with its correctness gate on every row of one step;
+  cpu_baseline the reference's torch CPU repack + SDPA path
+              (tests/benchmark_torch_paged_sdpa.py:90-109) on the host cores,
+              bounded sample, with the reference's own cpu_gqa_attention
+              (built from its sources) beside it;
+  seq_shard   (N > 1) config 4 sequence-sharded across the N GPUs, states
+              exchanged over NVLink inside the decode kernel (strong scaling).
 
-``--impl reference`` times that reference CPU implementation alone on the
-same workload (rank 0 only).
+``--impl reference`` times the reference CPU implementation alone on the
+same workload (rank 0 only).  ``--phase-stamps`` loads the diagnostic build
+and prints per-phase timings of the decode CTAs instead of the bench line.
 """
 
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
-import subprocess
 import sys
 import time
 from concurrent.futures import ThreadPoolExecutor
@@ -52,6 +62,9 @@ sys.path.insert(0, str(REPO))
 from persistentkv_attention_b200 import trace as tr  # noqa: E402
 
 WORKLOADS = {
+    "single_b1": dict(trace=None, requests=1, max_active=1, hole=0.0, hkv=8,
+                      desc="config 1: B1, 4096 tokens, 256 pages drawn as a seeded permutation "
+                           "of a 1024-page pool"),
     "uniform_8k": dict(trace="uniform_8k", requests=24, max_active=8, hole=0.0, hkv=8,
                        desc="config 2: B8 uniform context [512, 8192], 24 requests, 8 active"),
     "bimodal_32k": dict(trace="bimodal_32k", requests=24, max_active=8, hole=0.0, hkv=8,
@@ -61,12 +74,16 @@ WORKLOADS = {
     "zipf_b64": dict(trace="zipf_b64", requests=128, max_active=64, hole=0.1, hkv=8,
                      desc="config 5: B64 Zipf(1.1) context [256, 32768], 10% holes"),
 }
+PER_CONFIG = ["single_b1", "uniform_8k", "bimodal_32k", "long_b1", "zipf_b64"]
 HQ = 32
 PAGE = 16
 DTYPES = {"f16": torch.float16, "bf16": torch.bfloat16}
 D = 128
 SEED = 20260622
 FLUSH_BYTES = 256 << 20
+# tolerance of the reference (benchmark_serving_trace.py:37-38); bf16 outputs
+# add one bf16 rounding of the value (2^-8 relative), since they are stored in bf16
+MAX_ERR = 2e-3
 
 
 def measured_peak_gbs() -> tuple[float, str]:
@@ -79,11 +96,11 @@ def measured_peak_gbs() -> tuple[float, str]:
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """SM clock and clock-event reasons sampled during the timed region.
+    """SM clock and clock-event reasons sampled during the timed regions.
 
-    Polls NVML from a background thread (the timed region lasts milliseconds,
+    Polls NVML from a background thread (a timed region lasts milliseconds,
     far shorter than nvidia-smi's sampling period); only samples taken
-    between ``__enter__`` and ``__exit__`` count."""
+    between ``__enter__`` and ``__exit__`` count, over every region."""
 
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
@@ -146,7 +163,7 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(m for m, _ in self.samples),
                 "sm_max_mhz": self.max_mhz, "samples": len(self.samples),
                 "reasons": [name for bit, name in self.REASONS.items() if mask & bit],
-                "source": "NVML, polled during the timed region"}
+                "source": "NVML, polled during the timed regions"}
 
 
 class L2Flush:
@@ -172,7 +189,15 @@ TRACE_FILE = None  # --trace-file: request specs of an external trace replace th
 
 
 def build_workload(name: str, rank: int, steps_needed: int):
+    """(workload dict, requests, physical pages, steps) of a named config."""
     w = dict(WORKLOADS[name])
+    if name == "single_b1":
+        # config 1: one request of 4096 tokens whose 256 pages are a seeded
+        # permutation drawn from a 1024-page pool; the step repeats
+        gen = torch.Generator().manual_seed(SEED + 4096 + rank)
+        pages = torch.randperm(1024, generator=gen)[:256].tolist()
+        req = tr.Request(0, 0, 4096, 1, tuple(pages))
+        return w, [req], 1024, [tr.StepState(0, (0,), (4096,))]
     specs = None
     if TRACE_FILE is not None:
         specs = tr.load_trace_specs(TRACE_FILE, w["requests"], PAGE)
@@ -186,11 +211,21 @@ def build_workload(name: str, rank: int, steps_needed: int):
     return w, reqs, physical, steps
 
 
+def make_inputs(w, physical: int, hkv: int, dtype, dev, rank: int):
+    """Seeded N(0,1) K/V pools [physical, hkv, 16, 128] and q pool [requests, 32, 128],
+    generated on the device directly in the compute dtype."""
+    gen = torch.Generator(device=dev).manual_seed(SEED + 7 + rank)
+    k_pages = torch.randn(physical, hkv, PAGE, D, generator=gen, device=dev, dtype=dtype)
+    v_pages = torch.randn(physical, hkv, PAGE, D, generator=gen, device=dev, dtype=dtype)
+    q_pool = torch.randn(w["requests"], HQ, D, generator=gen, device=dev, dtype=dtype)
+    return k_pages, v_pages, q_pool
+
+
 def kv_bytes(state, hkv: int, elem: int = 2) -> int:
     return int(sum(state.lengths)) * hkv * D * 2 * elem
 
 
-# ------------------------------------------------------------------ CPU reference
+# ------------------------------------------------------------------ CPU baselines
 def cpu_reference_steps(reqs, steps, k_host, v_host, q_host, budget_s: float, hkv: int):
     """Reference cpu_gqa_attention (oracle/_ref) over trace steps, rows in parallel.
 
@@ -238,6 +273,31 @@ def cpu_reference_steps(reqs, steps, k_host, v_host, q_host, budget_s: float, hk
     return tokens / secs, done, threads, "reference" if use_ref else "port", secs
 
 
+def cpu_sdpa_steps(reqs, steps, k_host, v_host, q_host, budget_s: float):
+    """The reference's torch CPU repack + SDPA path (benchmark_torch_paged_sdpa.py:90-109,
+    restated in oracle.pkv_oracle.sdpa_repack_row) on fp32 host tensors, row
+    by row, torch's intra-op threads over the host cores.
+
+    Returns (tokens/s, steps run, torch threads, affinity cores, seconds)."""
+    from oracle import pkv_oracle as po
+
+    by_id = {r.request_id: r for r in reqs}
+    tokens = done = 0
+    t0 = time.perf_counter()
+    with torch.inference_mode():
+        for state in steps:
+            for rid, n in zip(state.active_ids, state.lengths):
+                pages = torch.tensor(by_id[rid].physical_pages[: (n + PAGE - 1) // PAGE],
+                                     dtype=torch.int64)
+                po.sdpa_repack_row(q_host[rid], k_host, v_host, pages, n)
+            tokens += len(state.active_ids)
+            done += 1
+            if time.perf_counter() - t0 > budget_s:
+                break
+    secs = time.perf_counter() - t0
+    return tokens / secs, done, torch.get_num_threads(), len(os.sched_getaffinity(0)), secs
+
+
 def run_reference_arm(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -271,9 +331,174 @@ def run_reference_arm(args) -> None:
 
 
 # ------------------------------------------------------------------ engine arm
+class Config:
+    """One workload on this GPU: pools, plans, one captured graph per
+    distinct step, and its timed run."""
+
+    def __init__(self, name, args, dev, stream, rank, hkv=None, dtype="f16", kv_fp8=False,
+                 steps=None):
+        from persistentkv_attention_b200.serving import DecodeEngine
+
+        self.name = name
+        self.steps_timed = steps if steps is not None else args.steps
+        self.warmup = args.warmup
+        w, reqs, physical, trace_steps = build_workload(name, rank,
+                                                        self.steps_timed + self.warmup)
+        self.w, self.reqs, self.trace_steps = w, reqs, trace_steps
+        self.hkv = hkv or w["hkv"]
+        self.dtype = dtype
+        self.kv_fp8 = kv_fp8
+        tdt = DTYPES[dtype]
+        k_pages, v_pages, q_pool = make_inputs(w, physical, self.hkv, tdt, dev, rank)
+        self.kv_elem = 2
+        if kv_fp8:
+            # e4m3 cache with per-tensor scales; the pools kept here hold the
+            # dequantised values for the correctness gate and the CPU baseline
+            scales = (float(k_pages.abs().max()) / 448.0, float(v_pages.abs().max()) / 448.0)
+            k8 = (k_pages.float() / scales[0]).to(torch.float8_e4m3fn)
+            v8 = (v_pages.float() / scales[1]).to(torch.float8_e4m3fn)
+            k_pages = (k8.float() * scales[0]).to(tdt)
+            v_pages = (v8.float() * scales[1]).to(tdt)
+            self.kv_elem = 1
+            self.engine = DecodeEngine(k8, v8, HQ, fused=not args.no_fused, kv_scales=scales)
+        else:
+            self.engine = DecodeEngine(k_pages, v_pages, HQ, fused=not args.no_fused)
+        self.k_pages, self.v_pages, self.q_pool = k_pages, v_pages, q_pool
+        self.stream = stream
+        self.plans, self.graphs, self.outs = [], [], []
+        n_distinct = min(len(trace_steps), self.steps_timed + self.warmup)
+        for state in trace_steps[:n_distinct]:
+            self.plans.append(self.engine.upload(self.engine.plan_from_trace(reqs, state)))
+        for p in self.plans:
+            o = torch.empty(p.batch, HQ, D, dtype=tdt, device=dev)
+            self.outs.append(o)
+            self.graphs.append(self.engine.capture(p, q_pool, o, stream))
+        torch.cuda.synchronize()
+        self.sched = [i % n_distinct for i in range(self.warmup + self.steps_timed)]
+
+    def timed(self, flush, barrier, clocks):
+        """Warm-up, then one CUDA-event interval per step (L2 flushed before
+        each, outside the interval).  Returns the per-step milliseconds."""
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(self.steps_timed)]
+        with torch.cuda.stream(self.stream):
+            for j in self.sched[: self.warmup]:
+                flush(j)
+                self.graphs[j].replay()
+        barrier()
+        with clocks:
+            with torch.cuda.stream(self.stream):
+                torch.cuda._sleep(20_000_000)         # lets the host queue run ahead (~10 ms)
+                for i, j in enumerate(self.sched[self.warmup:]):
+                    flush(i)
+                    ev[i][0].record(self.stream)
+                    self.graphs[j].replay()
+                    ev[i][1].record(self.stream)
+            barrier()
+        self.times_ms = [a.elapsed_time(b) for a, b in ev]
+        self.tokens = sum(self.plans[j].batch for j in self.sched[self.warmup:])
+        self.bytes_alg = sum(kv_bytes(self.trace_steps[j], self.hkv, self.kv_elem)
+                             for j in self.sched[self.warmup:])
+        return self.times_ms
+
+    def gate(self):
+        """Every row of one mid-trace step against the float64 checker (after
+        timing).  Returns the max abs error; raises past the tolerance."""
+        from oracle import pkv_oracle as po  # checker only
+
+        j = len(self.plans) // 2
+        with torch.cuda.stream(self.stream):
+            self.graphs[j].replay()
+        torch.cuda.synchronize()
+        st = self.trace_steps[j]
+        f = self.plans[j].fields
+        want = po.torch_paged_decode(self.q_pool, self.k_pages, self.v_pages, f["block_table"],
+                                     st.lengths, q_indices=st.active_ids)
+        got = self.outs[j].double()
+        excess = (got - want).abs() - (MAX_ERR + (2.0 ** -8 * want.abs()
+                                                  if self.dtype == "bf16" else 0.0))
+        err = float((got - want).abs().max())
+        if bool((excess >= 0).any()):
+            raise SystemExit(f"correctness gate failed on {self.name}: max abs error {err:.3e}")
+        return err
+
+    def summary(self, peak):
+        total_ms = sum(self.times_ms)
+        per_step_bytes = self.bytes_alg / self.steps_timed
+        achieved = per_step_bytes / (total_ms / self.steps_timed / 1000.0) / 1e9
+        return {"workload": f"{self.name}: {self.w['desc']}", "hkv": self.hkv,
+                "dtype": self.dtype + ("; K/V e4m3" if self.kv_fp8 else ""),
+                "steps": self.steps_timed, "value": self.tokens / (total_ms / 1000.0),
+                "unit": "tokens/s", "ms_per_step": total_ms / self.steps_timed,
+                "us_per_step_median": 1000.0 * statistics.median(self.times_ms),
+                "kv_bytes_per_step": per_step_bytes, "hbm_gbs": achieved,
+                "frac_of_measured_peak": achieved / peak, "frac_of_8tbs": achieved / 8000.0}
+
+    def release(self):
+        self.graphs.clear()
+        self.plans.clear()
+        self.outs.clear()
+        self.engine = None
+        self.k_pages = self.v_pages = self.q_pool = None
+
+
+def e2e_measure(cfg, flush, barrier, args):
+    """Each step through the public API from pinned host buffers.  Returns
+    (total ms, h2d bytes, d2h bytes, split dict)."""
+    engine, stream = cfg.engine, cfg.stream
+    q_host = cfg.q_pool.cpu().pin_memory()
+    out_host = torch.empty(max(p.batch for p in cfg.plans), HQ, D,
+                           dtype=cfg.q_pool.dtype).pin_memory()
+    scratch: dict = {}
+    host_rows = []
+    for p, state in zip(cfg.plans, cfg.trace_steps):
+        v = p.host.views(p.host.buf)
+        host_rows.append((list(state.lengths), v["block_table"].numpy().copy(),
+                          torch.stack([q_host[r] for r in state.active_ids]).pin_memory()))
+    engine.reserve_host(scratch, max(len(r[0]) for r in host_rows),
+                        max(r[1].shape[1] for r in host_rows))
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(cfg.steps_timed)]
+    host_us = []
+    bi = bo = 0
+    with torch.cuda.stream(stream):
+        for j in cfg.sched[: cfg.warmup]:
+            lens, rows, qh = host_rows[j]
+            engine.step_host(lens, rows, qh, out_host, scratch)
+            stream.synchronize()
+        barrier()
+        for i, j in enumerate(cfg.sched[cfg.warmup:]):
+            lens, rows, qh = host_rows[j]
+            flush(i)
+            stream.synchronize()
+            ev[i][0].record(stream)
+            t0 = time.perf_counter()
+            h, d = engine.step_host(lens, rows, qh, out_host, scratch)
+            host_us.append(1e6 * (time.perf_counter() - t0))
+            ev[i][1].record(stream)
+            stream.synchronize()
+            bi += h
+            bo += d
+        barrier()
+    # the last step's output rows, read from host memory, against the device run
+    lens, rows, qh = host_rows[cfg.sched[-1]]
+    ref = cfg.outs[cfg.sched[-1]].cpu()
+    err = float((out_host[: len(lens)].float() - ref.float()).abs().max())
+    if err > MAX_ERR:
+        raise SystemExit(f"e2e output differs from the device-resident run: {err:.3e}")
+    scratch["native"].close()
+    times = [a.elapsed_time(b) for a, b in ev]
+    split = {"host_call_us_median": statistics.median(host_us),
+             "interval_us_median": 1000.0 * statistics.median(times),
+             "decode_device_us_median": 1000.0 * statistics.median(cfg.times_ms),
+             "note": "interval = host call (staging, graph launch) + launch latency + stage-in "
+                     "kernel (metadata and q rows read from pinned host memory) + decode + "
+                     "output rows written to pinned host memory"}
+    return sum(times), bi, bo, split
+
+
 def run_engine_arm(args) -> None:
     from persistentkv_attention_b200 import _native
-    from persistentkv_attention_b200.serving import DecodeEngine
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -287,134 +512,35 @@ def run_engine_arm(args) -> None:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
-
-    w, reqs, physical, steps = build_workload(args.workload, rank, args.steps + args.warmup)
-    hkv = args.hkv or w["hkv"]
-    tdt = DTYPES[args.dtype]
-    gen = torch.Generator(device=dev).manual_seed(SEED + 7 + rank)
-    k_pages = torch.randn(physical, hkv, PAGE, D, generator=gen, device=dev).to(tdt)
-    v_pages = torch.randn(physical, hkv, PAGE, D, generator=gen, device=dev).to(tdt)
-    q_pool = torch.randn(w["requests"], HQ, D, generator=gen, device=dev).to(tdt)
-    kv_elem = 2
-    kv_scales = None
-    if args.kv_fp8:
-        # e4m3 cache with per-tensor scales; the pools below hold the
-        # dequantised values for the correctness gate and the CPU baseline
-        kv_scales = (float(k_pages.abs().max()) / 448.0, float(v_pages.abs().max()) / 448.0)
-        k8 = (k_pages.float() / kv_scales[0]).to(torch.float8_e4m3fn)
-        v8 = (v_pages.float() / kv_scales[1]).to(torch.float8_e4m3fn)
-        k_pages = (k8.float() * kv_scales[0]).to(tdt)
-        v_pages = (v8.float() * kv_scales[1]).to(tdt)
-        kv_elem = 1
-        engine = DecodeEngine(k8, v8, HQ, fused=not args.no_fused, kv_scales=kv_scales)
-    else:
-        engine = DecodeEngine(k_pages, v_pages, HQ, fused=not args.no_fused)
+    _native.set_gather_mode(args.gather)
     flush = L2Flush(dev)
     stream = torch.cuda.Stream(dev)
-
-    # device-resident plans + one CUDA graph per distinct step
-    plans, graphs, outs = [], [], []
-    n_distinct = min(len(steps), args.steps + args.warmup)
-    for state in steps[:n_distinct]:
-        p = engine.upload(engine.plan_from_trace(reqs, state))
-        plans.append(p)
-    for p in plans:
-        o = torch.empty(p.batch, HQ, D, dtype=tdt, device=dev)
-        outs.append(o)
-        graphs.append(engine.capture(p, q_pool, o, stream))
-    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    peak, peak_kind = measured_peak_gbs()
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
-    sched = [i % n_distinct for i in range(args.warmup + args.steps)]
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
-    with torch.cuda.stream(stream):
-        for j in sched[: args.warmup]:
-            flush(j)
-            graphs[j].replay()
-    barrier()
-    with ClockSampler(local) as clocks:
-        with torch.cuda.stream(stream):
-            torch.cuda._sleep(20_000_000)         # lets the host queue run ahead (~10 ms)
-            for i, j in enumerate(sched[args.warmup:]):
-                flush(i)
-                ev[i][0].record(stream)
-                graphs[j].replay()
-                ev[i][1].record(stream)
-        barrier()
-    times_ms = [a.elapsed_time(b) for a, b in ev]
-    tokens = sum(plans[j].batch for j in sched[args.warmup:])
-    bytes_alg = sum(kv_bytes(steps[j], hkv, kv_elem) for j in sched[args.warmup:])
-    total_ms = sum(times_ms)
-    launches = args.steps * (1 if not args.no_fused else 2)
+    main = Config(args.workload, args, dev, stream, rank, hkv=args.hkv or None, dtype=args.dtype,
+                  kv_fp8=args.kv_fp8)
+    main.timed(flush, barrier, clocks)
     code = _native.device_error(clear=True)
     if code:
         raise RuntimeError(f"device error: {_native.describe_device_error(code)}")
-    # correctness gate on one step (reference: one mid-trace check, :1082-1088)
-    check_step = len(plans) // 2
-    graphs[check_step].replay()
-    torch.cuda.synchronize()
-    from oracle import pkv_oracle as po  # checker only
-
-    st = steps[check_step]
-    row = 0
-    rid = st.active_ids[row]
-    k_row = k_pages[torch.tensor(reqs[rid].physical_pages[: (st.lengths[row] + PAGE - 1) // PAGE],
-                                 device=dev)]
-    v_row = v_pages[torch.tensor(reqs[rid].physical_pages[: (st.lengths[row] + PAGE - 1) // PAGE],
-                                 device=dev)]
-    kk = k_row.permute(1, 0, 2, 3).reshape(hkv, -1, D)[:, : st.lengths[row]].double().cpu().numpy()
-    vv = v_row.permute(1, 0, 2, 3).reshape(hkv, -1, D)[:, : st.lengths[row]].double().cpu().numpy()
-    want = po.attend_row(q_pool[rid].double().cpu().numpy(), kk, vv)
-    got = outs[check_step][row].double().cpu().numpy()
-    max_err = float(np.abs(got - want).max())
-    # fp16 tolerance of the reference; bf16 output adds one bf16 rounding (2^-8 relative)
-    excess = np.abs(got - want) - (2e-3 + (2.0 ** -8 * np.abs(want) if args.dtype == "bf16" else 0))
-    if (excess >= 0).any():
-        raise SystemExit(f"correctness gate failed: max abs error {max_err:.3e}")
+    max_err = main.gate()
+    total_ms = sum(main.times_ms)
+    launches = args.steps * (1 if not args.no_fused else 2)
 
     # ---- end to end through the public API from pinned host buffers
-    q_host = q_pool.cpu().pin_memory()
-    out_host = torch.empty(max(p.batch for p in plans), HQ, D, dtype=tdt).pin_memory()
-    scratch: dict = {}
-    bi = bo = 0
-    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(args.steps)]
-    host_rows = []
-    for state in steps[:n_distinct]:
-        plan = engine.plan_from_trace(reqs, state)
-        v = plan.views(plan.buf)
-        host_rows.append((list(state.lengths), v["block_table"].numpy().copy(),
-                          torch.stack([q_host[r] for r in state.active_ids]).pin_memory()))
-    if not engine.kv8:
-        engine.reserve_host(scratch, max(len(r[0]) for r in host_rows),
-                            max(r[1].shape[1] for r in host_rows))
-    with torch.cuda.stream(stream):
-        for j in (sched[: args.warmup] if not engine.kv8 else []):
-            lens, rows, qh = host_rows[j]
-            engine.step_host(lens, rows, qh, out_host, scratch)
-            stream.synchronize()
-        barrier()
-        for i, j in enumerate(sched[args.warmup:] if not engine.kv8 else []):
-            lens, rows, qh = host_rows[j]
-            flush(i)
-            stream.synchronize()
-            e2e_ev[i][0].record(stream)
-            h, d = engine.step_host(lens, rows, qh, out_host, scratch)
-            e2e_ev[i][1].record(stream)
-            stream.synchronize()
-            bi += h
-            bo += d
-        barrier()
-    e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev) if not engine.kv8 else 0.0
+    e2e_ms, bi, bo, e2e_split = (0.0, 0, 0, None)
+    if not main.kv_fp8:
+        e2e_ms, bi, bo, e2e_split = e2e_measure(main, flush, barrier, args)
 
     # ---- aggregate over ranks (max time, summed tokens)
-    stats = torch.tensor([total_ms, e2e_ms, float(tokens), float(bytes_alg)], dtype=torch.float64,
-                         device=dev)
+    stats = torch.tensor([total_ms, e2e_ms, float(main.tokens), float(main.bytes_alg)],
+                         dtype=torch.float64, device=dev)
     if world > 1:
         import torch.distributed as dist
 
@@ -424,12 +550,50 @@ def run_engine_arm(args) -> None:
         dist.all_reduce(sm, op=dist.ReduceOp.SUM)
         total_ms, e2e_ms = float(mx[0]), float(mx[1])
         tokens, bytes_alg = float(sm[2]), float(sm[3])
+    else:
+        tokens, bytes_alg = float(main.tokens), float(main.bytes_alg)
+
+    # ---- the other configs, same run, same timing method (one GPU)
+    per_config = {}
+    if world == 1 and not args.no_per_config and TRACE_FILE is None:
+        main_summary = main.summary(peak)
+        for name in PER_CONFIG:
+            if name == args.workload:
+                continue
+            cfg = Config(name, args, dev, stream, rank, dtype=args.dtype,
+                         steps=min(args.steps, 20))
+            cfg.timed(flush, barrier, clocks)
+            err = cfg.gate()
+            per_config[name] = dict(cfg.summary(peak), correctness_max_abs_err=err,
+                                    gate="every row of one mid-trace step vs float64 checker")
+            cfg.release()
+            torch.cuda.empty_cache()
+        # the default config under the other gather, for the gather comparison
+        other = "tma" if args.gather == "cpasync" else "cpasync"
+        _native.set_gather_mode(other)
+        cfg = Config(args.workload, args, dev, stream, rank, hkv=args.hkv or None,
+                     dtype=args.dtype, steps=args.steps)
+        cfg.timed(flush, barrier, clocks)
+        err = cfg.gate()
+        per_config[f"{args.workload}@gather={other}"] = dict(cfg.summary(peak),
+                                                              correctness_max_abs_err=err)
+        cfg.release()
+        _native.set_gather_mode(args.gather)
+        per_config[f"{args.workload}@gather={args.gather}"] = main_summary
+        code = _native.device_error(clear=True)
+        if code:
+            raise RuntimeError(f"device error: {_native.describe_device_error(code)}")
+
+    # ---- config 4 sequence-sharded across the ranks (strong scaling)
+    seq_shard = None
+    if world > 1 and not args.no_per_config:
+        seq_shard = measure_seq_shard(args, "fused", dev, stream, flush, clocks, world, rank)
+
     if rank != 0:
         if world > 1:
             torch.distributed.destroy_process_group()
         return
 
-    peak, peak_kind = measured_peak_gbs()
     value = tokens / (total_ms / 1000.0)
     per_step_bytes = bytes_alg / args.steps / world
     achieved = per_step_bytes / (total_ms / args.steps / 1000.0) / 1e9
@@ -437,7 +601,7 @@ def run_engine_arm(args) -> None:
     # committed ncu capture of this workload, applied to this run's launches.
     traffic = None
     tpath = REPO / "profiles" / f"traffic_{args.workload}.json"
-    if (tpath.exists() and hkv == 8 and args.dtype == "f16" and TRACE_FILE is None
+    if (tpath.exists() and main.hkv == 8 and args.dtype == "f16" and TRACE_FILE is None
             and not args.kv_fp8):
         ratio = json.loads(tpath.read_text()).get("traffic_over_algorithmic")
         if ratio:
@@ -450,14 +614,15 @@ def run_engine_arm(args) -> None:
         "vs_baseline": None, "dtype": args.dtype + ("; K/V e4m3" if args.kv_fp8 else ""),
         "data": "synthetic (seeded trace, K/V/q ~ N(0,1))",
         "config": {
-            "workload": f"{args.workload}: {w['desc']}", "hq": HQ, "hkv": hkv, "gqa_group": HQ // hkv,
-            "head_dim": D,
-            "page_size": PAGE, "active_per_gpu": w["max_active"],
+            "workload": f"{args.workload}: {main.w['desc']}", "hq": HQ, "hkv": main.hkv,
+            "gqa_group": HQ // main.hkv, "head_dim": D,
+            "page_size": PAGE, "active_per_gpu": main.w["max_active"],
             "parallelism": f"batch-partitioned x{world} (independent batch per GPU)",
             "l2": "flushed before every step outside the timed intervals: 256 MiB write, "
                   "then 256 MiB read (no dirty lines left for the timed step)",
             "merge": "fused last-task merge" if not args.no_fused else "PDL merge kernel",
             "schedule": "device-side equal-token groups (no host work queue)",
+            "gather": args.gather,
         },
         "hbm_gbs": achieved, "hbm_frac_of_8tbs": achieved / 8000.0,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -465,69 +630,79 @@ def run_engine_arm(args) -> None:
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                      "kernel": "pkv_decode_kernel (fused merge), 1 launch per step"},
         "e2e": ({"value": tokens / (e2e_ms / 1000.0), "unit": "tokens/s",
-                 "h2d_bytes_per_step": bi // args.steps, "d2h_bytes_per_step": bo // args.steps}
+                 "h2d_bytes_per_step": bi // args.steps, "d2h_bytes_per_step": bo // args.steps,
+                 "split": e2e_split}
                 if not args.kv_fp8 else
                 {"value": None, "unit": "tokens/s",
                  "note": "the native host step serves 16-bit caches only"}),
         "gpu_launches": launches,
         "correctness_max_abs_err": max_err,
+        "correctness_gate": "every row of one mid-trace step vs a float64 checker, "
+                            "max 2e-3 (bf16: + 2^-8 |ref|)",
     }
-    c = clocks.summary()
-    line["clocks"] = c
+    if per_config:
+        line["per_config"] = per_config
+    if seq_shard is not None:
+        line["seq_shard"] = seq_shard
+    line["clocks"] = clocks.summary()
     if world == 1 and not args.no_cpu_baseline:
-        k_host = k_pages.float().cpu().numpy()
-        v_host = v_pages.float().cpu().numpy()
-        qn = q_pool.float().cpu().numpy()
-        # the trace's steps, cycled, for a bounded ~12 s sample of CPU work
-        cycle = [steps[i % len(steps)] for i in range(50 * max(1, args.steps))]
-        val, done, threads, kind, secs = cpu_reference_steps(reqs, cycle, k_host, v_host, qn,
-                                                             12.0, hkv)
-        line["cpu_baseline"] = {"value": val, "unit": "tokens/s", "cores": threads, "kind": kind,
-                                "sample": f"{done} decode steps of the trace, cycled "
-                                          f"({secs:.1f} s), (row, KV head) groups in parallel"}
+        line["cpu_baseline"] = cpu_baselines(main, args)
     if world > 1:
         torch.distributed.destroy_process_group()
     print(json.dumps(line), flush=True)
 
 
-def run_seq_shard_arm(args) -> None:
+def cpu_baselines(cfg, args):
+    """The torch CPU repack + SDPA path (the north star's CPU baseline) and,
+    beside it, the reference's own cpu_gqa_attention, each a bounded sample
+    of the same workload's steps on this host's cores."""
+    k_t = cfg.k_pages.float().cpu()
+    v_t = cfg.v_pages.float().cpu()
+    q_t = cfg.q_pool.float().cpu()
+    cycle = [cfg.trace_steps[i % len(cfg.trace_steps)] for i in range(50 * max(1, args.steps))]
+    val, done, threads, cores, secs = cpu_sdpa_steps(cfg.reqs, cycle, k_t, v_t, q_t, 10.0)
+    out = {"value": val, "unit": "tokens/s", "cores": threads, "kind": "port",
+           "affinity_cores": cores, "torch_num_threads": threads,
+           "path": "torch CPU repack + scaled_dot_product_attention(enable_gqa=True) in fp32, "
+                   "tests/benchmark_torch_paged_sdpa.py:90-109",
+           "sample": f"{done} decode steps of the trace, cycled ({secs:.1f} s), rows in turn, "
+                     f"torch intra-op threads"}
+    rval, rdone, rthreads, rkind, rsecs = cpu_reference_steps(
+        cfg.reqs, cycle, k_t.numpy(), v_t.numpy(), q_t.numpy(), 10.0, cfg.hkv)
+    out["reference_cpu_gqa_attention"] = {
+        "value": rval, "unit": "tokens/s", "cores": rthreads, "kind": rkind,
+        "sample": f"{rdone} decode steps ({rsecs:.1f} s), (row, KV head) groups in parallel"}
+    return out
+
+
+# ------------------------------------------------------------------ sequence sharding
+def measure_seq_shard(args, exchange, dev, stream, flush, clocks, world, rank,
+                      workload="long_b1", steps=None):
     """Config 4 across GPUs: every rank decodes its contiguous page range of the
     active request, and the per-rank (m, l, acc) states are merged exactly on
-    every rank (strong scaling).  ``--exchange fused`` (default): one kernel
-    per step pushes the states to the peers over NVLink and merges them;
-    ``--exchange nccl``: state kernel, NCCL all-gather, combine kernel."""
-    import datetime
-
+    every rank (strong scaling).  ``exchange="fused"``: one kernel per step
+    pushes the states to the peers over NVLink and merges them; ``"nccl"``:
+    state kernel, NCCL all-gather, combine kernel.  Returns a summary dict."""
     import torch.distributed as dist
 
     from persistentkv_attention_b200 import _native, ops
     from persistentkv_attention_b200 import dist as pdist
     from persistentkv_attention_b200.serving import DecodeEngine
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    w, reqs, physical, steps = build_workload(args.workload, 0, args.steps + args.warmup)
+    steps_timed = steps or args.steps
+    w, reqs, physical, trace_steps = build_workload(workload, 0, steps_timed + args.warmup)
     hkv = w["hkv"]
-    gen = torch.Generator(device=dev).manual_seed(SEED + 7)   # same pool on every rank
-    k_pages = torch.randn(physical, hkv, PAGE, D, generator=gen, device=dev).half()
-    v_pages = torch.randn(physical, hkv, PAGE, D, generator=gen, device=dev).half()
-    q_pool = torch.randn(w["requests"], HQ, D, generator=gen, device=dev).half()
+    k_pages, v_pages, q_pool = make_inputs(w, physical, hkv, torch.float16, dev, 0)
     engine = DecodeEngine(k_pages, v_pages, HQ, fused=True)
-    flush = L2Flush(dev)
-    stream = torch.cuda.Stream(dev)
-    n = min(len(steps), args.steps + args.warmup)
-    fused = args.exchange == "fused"
+    n = min(len(trace_steps), steps_timed + args.warmup)
+    fused = exchange == "fused"
     plans, states, outs, graphs = [], [], [], []
-    for state in steps[:n]:
+    for state in trace_steps[:n]:
         full = engine.plan_from_trace(reqs, state)
         rows = full.views(full.buf)["block_table"].numpy()
         bt, sl = pdist.shard_rows(rows, state.lengths, PAGE, world, rank)
-        plans.append(engine.upload(engine.plan_step(sl, bt, q_indices=np.asarray(state.active_ids))))
+        plans.append(engine.upload(engine.plan_step(sl, bt,
+                                                    q_indices=np.asarray(state.active_ids))))
     xg = pdist.make_exchange(HQ, hkv, max(p.batch for p in plans)) if fused else None
     for p in plans:
         st = torch.empty(p.batch, HQ, 130, dtype=torch.float32, device=dev)
@@ -561,15 +736,15 @@ def run_seq_shard_arm(args) -> None:
             dist.barrier()
         torch.cuda.synchronize()
 
-    sched = [i % n for i in range(args.warmup + args.steps)]
+    sched = [i % n for i in range(args.warmup + steps_timed)]
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
+          for _ in range(steps_timed)]
     with torch.cuda.stream(stream):
         for j in sched[: args.warmup]:
             flush(j)
             step(j)
     barrier()
-    with ClockSampler(local) as clocks:
+    with clocks:
         with torch.cuda.stream(stream):
             torch.cuda._sleep(20_000_000)     # host runs ahead: a host hiccup on one rank
                                               # must not stall the coupled peer kernels
@@ -583,53 +758,38 @@ def run_seq_shard_arm(args) -> None:
     code = _native.device_error(clear=True)
     if code:
         raise RuntimeError(f"device error: {_native.describe_device_error(code)}")
-    # correctness: the merged output of one step against the oracle
+    # correctness: the merged output of one step against the float64 checker
     from oracle import pkv_oracle as po  # checker only
 
     j = n // 2
     with torch.cuda.stream(stream):
         step(j)
     torch.cuda.synchronize()
-    st = steps[j]
-    rid, length = st.active_ids[0], st.lengths[0]
-    pages = torch.tensor(reqs[rid].physical_pages[: (length + PAGE - 1) // PAGE], device=dev)
-    kk = k_pages[pages].permute(1, 0, 2, 3).reshape(hkv, -1, D)[:, :length].double().cpu().numpy()
-    vv = v_pages[pages].permute(1, 0, 2, 3).reshape(hkv, -1, D)[:, :length].double().cpu().numpy()
-    want = po.attend_row(q_pool[rid].double().cpu().numpy(), kk, vv)
-    max_err = float(np.abs(outs[j][0].double().cpu().numpy() - want).max())
-    if max_err >= 2e-3:
+    st = trace_steps[j]
+    full = engine.plan_from_trace(reqs, st)
+    table = full.views(full.buf)["block_table"].numpy()
+    want = po.torch_paged_decode(q_pool, k_pages, v_pages, table, st.lengths,
+                                 q_indices=st.active_ids)
+    max_err = float((outs[j].double() - want).abs().max())
+    if max_err >= MAX_ERR:
         raise SystemExit(f"correctness gate failed: max abs error {max_err:.3e}")
     tokens = float(sum(plans[j].batch for j in sched[args.warmup:]))
-    full_bytes = float(sum(kv_bytes(steps[j], hkv) for j in sched[args.warmup:]))
+    full_bytes = float(sum(kv_bytes(trace_steps[j], hkv) for j in sched[args.warmup:]))
     t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_ms = float(t[0])
-    if rank == 0:
-        peak, peak_kind = measured_peak_gbs()
-        achieved = full_bytes / args.steps / world / (total_ms / args.steps / 1000.0) / 1e9
-        line = {
-            "metric": "decode-step tokens/s", "value": tokens / (total_ms / 1000.0),
-            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded trace, K/V/q ~ N(0,1))",
-            "config": {"workload": f"{args.workload}: {w['desc']}", "hq": HQ, "hkv": hkv,
-                       "head_dim": D, "page_size": PAGE,
-                       "parallelism": f"sequence-sharded x{world}: page ranges per GPU, "
-                                      + ("(m, l, acc) pushed to peers over NVLink and merged "
-                                         "inside the decode kernel" if fused else
-                                         "(m, l, acc) all-gather over NCCL, LSE combine"),
-                       "l2": "flushed before every step outside the timed intervals"},
-            "hbm_gbs_per_gpu": achieved,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
-                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                         "kernel": "pkv_decode_kernel (fused exchange)" if fused else
-                                   "pkv_decode_kernel (state) + all-gather + combine"},
-            "gpu_launches": args.steps * (1 if fused else 2), "correctness_max_abs_err": max_err,
-            "clocks": clocks.summary(),
-        }
-        print(json.dumps(line), flush=True)
+    peak, _ = measured_peak_gbs()
+    achieved = full_bytes / steps_timed / world / (total_ms / steps_timed / 1000.0) / 1e9
+    summary = {
+        "workload": f"{workload}: {w['desc']}", "scaling": "strong", "n_gpus": world,
+        "steps": steps_timed, "value": tokens / (total_ms / 1000.0), "unit": "tokens/s",
+        "ms_per_step": total_ms / steps_timed, "hbm_gbs_per_gpu": achieved,
+        "frac_of_measured_peak": achieved / peak,
+        "exchange": ("(m, l, acc) pushed to peers over NVLink and merged inside the decode "
+                     "kernel" if fused else "(m, l, acc) all-gather over NCCL, LSE combine"),
+        "gpu_launches_per_step": 1 if fused else 2, "correctness_max_abs_err": max_err,
+    }
     graphs.clear()
     torch.cuda.synchronize()
     if world > 1:
@@ -638,7 +798,140 @@ def run_seq_shard_arm(args) -> None:
         xg.close()
     if world > 1:
         dist.barrier()
+    return summary
+
+
+def run_seq_shard_arm(args) -> None:
+    import datetime
+
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    flush = L2Flush(dev)
+    stream = torch.cuda.Stream(dev)
+    clocks = ClockSampler(local)
+    s = measure_seq_shard(args, args.exchange, dev, stream, flush, clocks, world, rank,
+                          workload=args.workload)
+    if rank == 0:
+        peak, peak_kind = measured_peak_gbs()
+        line = {
+            "metric": "decode-step tokens/s", "value": s["value"], "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": s["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded trace, K/V/q ~ N(0,1))",
+            "config": {"workload": s["workload"], "hq": HQ, "hkv": 8, "head_dim": D,
+                       "page_size": PAGE,
+                       "parallelism": f"sequence-sharded x{world}: page ranges per GPU, "
+                                      + s["exchange"],
+                       "l2": "flushed before every step outside the timed intervals"},
+            "hbm_gbs_per_gpu": s["hbm_gbs_per_gpu"],
+            "roofline": {"bound": "hbm", "achieved": s["hbm_gbs_per_gpu"], "peak": peak,
+                         "unit": "GB/s", "frac": s["frac_of_measured_peak"], "traffic": None,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                         "kernel": "pkv_decode_kernel (fused exchange)"
+                                   if args.exchange == "fused" else
+                                   "pkv_decode_kernel (state) + all-gather + combine"},
+            "gpu_launches": args.steps * s["gpu_launches_per_step"],
+            "correctness_max_abs_err": s["correctness_max_abs_err"],
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
         dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ phase stamps
+PHASES = [("launch_spread", 0, None), ("schedule", 0, 1), ("first_pages", 1, 2),
+          ("first_issue", 2, 3), ("first_data", 3, 4), ("stream", 4, 5),
+          ("merge", 6, 7)]
+
+
+def stamp_summary(stamps, event_us):
+    """Phases of one launch from the per-CTA stamps (nanoseconds)."""
+    s = np.asarray([x for x in stamps if x[0] > 0 and x[7] > 0], dtype=np.float64)
+    t0 = s[:, 0].min()
+    out = {"ctas": int(s.shape[0]), "event_interval_us": event_us,
+           "kernel_span_us": (s[:, 7].max() - t0) / 1e3}
+    for name, a, b in PHASES:
+        if b is None:
+            d = (s[:, a] - t0) / 1e3
+        else:
+            m = (s[:, a] > 0) & (s[:, b] > 0)
+            d = (s[m, b] - s[m, a]) / 1e3
+        if d.size:
+            out[name + "_us"] = {"median": float(np.median(d)), "max": float(d.max()),
+                                 "n": int(d.size)}
+    first_data = (s[:, 4][s[:, 4] > 0] - t0) / 1e3
+    last_stage = (s[:, 5][s[:, 5] > 0] - t0) / 1e3
+    out["first_data_at_us"] = {"min": float(first_data.min()), "median": float(np.median(first_data)),
+                               "max": float(first_data.max())}
+    out["last_stage_at_us"] = {"min": float(last_stage.min()), "median": float(np.median(last_stage)),
+                               "max": float(last_stage.max())}
+    out["exit_at_us"] = {"median": float(np.median((s[:, 7] - t0) / 1e3)),
+                         "max": float((s[:, 7].max() - t0) / 1e3)}
+    return out
+
+
+def run_phase_stamps(args) -> None:
+    """Per-phase timings of the decode CTAs (diagnostic build), per workload:
+    each step flushed and replayed like the timed bench, then its stamps read."""
+    from persistentkv_attention_b200 import _native
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    _native.load()
+    _native.set_gather_mode(args.gather)
+    flush = L2Flush(dev)
+    stream = torch.cuda.Stream(dev)
+    names = [args.workload] if args.no_per_config else ["uniform_8k", "long_b1", "bimodal_32k"]
+    report = {"build": "libpkv_b200_stamps.so (PKV_PHASE_STAMPS)", "gather": args.gather,
+              "workloads": {}}
+    for name in names:
+        cfg = Config(name, args, dev, stream, 0, steps=args.steps)
+        runs = []
+        with torch.cuda.stream(stream):
+            for j in cfg.sched[: cfg.warmup]:
+                flush(j)
+                cfg.graphs[j].replay()
+            torch.cuda.synchronize()
+            _native.phase_stamps()
+            for i, j in enumerate(cfg.sched[cfg.warmup:]):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                flush(i)
+                a.record(stream)
+                cfg.graphs[j].replay()
+                b.record(stream)
+                torch.cuda.synchronize()
+                runs.append(stamp_summary(_native.phase_stamps(), 1000.0 * a.elapsed_time(b)))
+
+        def med(path):
+            vals = []
+            for r in runs:
+                v = r
+                for k in path:
+                    v = v.get(k) if isinstance(v, dict) else None
+                if v is not None:
+                    vals.append(v)
+            return float(np.median(vals)) if vals else None
+
+        keys = [("event_interval_us",), ("kernel_span_us",)] + \
+               [(n + "_us", "median") for n, _, _ in PHASES] + \
+               [(n + "_us", "max") for n, _, _ in PHASES] + \
+               [("first_data_at_us", "min"), ("first_data_at_us", "median"),
+                ("first_data_at_us", "max"), ("last_stage_at_us", "median"),
+                ("last_stage_at_us", "max"), ("exit_at_us", "median"), ("exit_at_us", "max")]
+        report["workloads"][name] = {
+            "steps": len(runs), "ctas": runs[0]["ctas"] if runs else 0,
+            "median_over_steps": {".".join(k): med(k) for k in keys}}
+        cfg.release()
+        torch.cuda.empty_cache()
+    print(json.dumps(report, indent=1), flush=True)
 
 
 def main() -> None:
@@ -656,8 +949,14 @@ def main() -> None:
     ap.add_argument("--dtype", choices=sorted(DTYPES), default="f16")
     ap.add_argument("--kv-fp8", action="store_true",
                     help="e4m3 K/V cache with per-tensor scales (q / output fp16)")
+    ap.add_argument("--gather", choices=["cpasync", "tma"], default="cpasync",
+                    help="decode gather of 16-bit pools (pkv_set_gather_mode)")
     ap.add_argument("--no-fused", action="store_true", help="separate PDL merge kernel")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-per-config", action="store_true",
+                    help="time only --workload (no per_config / seq_shard sub-objects)")
+    ap.add_argument("--phase-stamps", action="store_true",
+                    help="diagnostic build: print per-phase CTA timings instead of the bench line")
     ap.add_argument("--seq-shard", action="store_true",
                     help="shard each request's pages across the GPUs (config 4 strong scaling)")
     ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused",
@@ -669,7 +968,10 @@ def main() -> None:
         ap.error("--kv-fp8 computes with fp16 q / output (--dtype f16)")
     global TRACE_FILE
     TRACE_FILE = args.trace_file
-    if args.impl == "reference":
+    if args.phase_stamps:
+        os.environ["PKV_LIB_VARIANT"] = "stamps"
+        run_phase_stamps(args)
+    elif args.impl == "reference":
         run_reference_arm(args)
     elif args.seq_shard:
         run_seq_shard_arm(args)

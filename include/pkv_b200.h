@@ -71,6 +71,35 @@ int pkv_abi_version(void);
  * calling thread (mirrors the TORCH_CHECK messages of the reference). */
 const char* pkv_last_error_message(void);
 
+/* How the decode kernel's producer warp moves K/V pages of 16-bit pools into
+ * its shared-memory ring.  Both produce the same bits; the choice only
+ * changes speed.  The reference has one gather, 16-byte cp.async
+ * (kernels/persistentkv_attention.cuh:87-103, :221-267). */
+typedef enum pkv_gather {
+    /* cp.async.bulk.tensor.2d boxes (TMA) of 64 elements x 16 (or 8) token
+     * rows from a tensor map over this GPU's own pool (no multicast), one
+     * issuing lane, completion as mbarrier transaction bytes. */
+    PKV_GATHER_TMA = 0,
+    /* 16-byte cp.async from all 32 lanes, completion through
+     * cp.async.mbarrier.arrive (the default). */
+    PKV_GATHER_CP_ASYNC = 1
+} pkv_gather;
+
+/* Selects the gather of every later 16-bit decode launch in this process
+ * (e4m3 pools always use cp.async).  Launches already captured in a CUDA
+ * graph keep the gather they were captured with. */
+pkv_status pkv_set_gather_mode(pkv_gather mode);
+pkv_gather pkv_get_gather_mode(void);
+
+/* Diagnostic build only (libpkv_b200_stamps.so, compiled with
+ * PKV_PHASE_STAMPS): copies the per-CTA %globaltimer stamps of the last
+ * decode launch on this thread -- PKV_STAMPS_PER_CTA values per CTA, see
+ * the kernel's stamp list -- into out (max_ctas * PKV_STAMPS_PER_CTA
+ * uint64), sets *n_ctas, clears the device copy and synchronises the device.
+ * The regular library returns PKV_ERR_UNSUPPORTED. */
+#define PKV_STAMPS_PER_CTA 8
+pkv_status pkv_phase_stamps(uint64_t* out, int max_ctas, int* n_ctas);
+
 /* ---------------------------------------------------------------------------
  * Paged decode attention, the four reference operator entry points.
  * ------------------------------------------------------------------------- */
@@ -247,15 +276,18 @@ pkv_status pkv_kv_append(const void* k_new, const void* v_new, void* k_pages, vo
 
 /* ---- Native host step ----
  * A decode engine over one paged K/V pool that takes a step from host
- * buffers to host buffers in one call: it stages the block-table rows and
- * lengths in its own pinned memory and runs pkv_paged_attention_auto with
- * the fused merge on `stream`, the kernel reading metadata and query rows
- * from pinned host memory and writing the output rows into out_host over
- * the host link (no separate copies).  Synchronise `stream` before reading
- * out_host.  q_host and out_host must be page-locked and mapped
- * (cudaHostAlloc, or a framework's pinned allocator), else
- * PKV_ERR_INVALID_ARGUMENT.  The native counterpart of the reference
- * harness's per-step Python (tests/benchmark_serving_trace.py:838-946). */
+ * buffers to host buffers in one call: it copies the block-table rows and
+ * lengths into its own mapped pinned staging memory; a short stage-in kernel
+ * copies them and the caller's q rows (read from pinned host memory) into
+ * device buffers, and pkv_paged_attention_auto (fused merge) follows it with
+ * programmatic dependent launch, writing the output rows straight into
+ * out_host over the host link.  The two launches are captured once per
+ * (batch, staging buffer, output buffer) and replayed as a CUDA graph.
+ * Synchronise `stream` before reading out_host.  q_host and out_host must be
+ * page-locked and mapped (cudaHostAlloc, or a framework's pinned allocator),
+ * else PKV_ERR_INVALID_ARGUMENT; this is checked on every call.  The native
+ * counterpart of the reference harness's per-step Python
+ * (tests/benchmark_serving_trace.py:838-946). */
 typedef struct pkv_engine pkv_engine;
 
 /* k_pages / v_pages: device pools [physical_pages][Hkv][page_size][128].

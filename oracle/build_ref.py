@@ -5,7 +5,9 @@ baseline), never part of the engine.  Nothing is copied from the reference
 into this repository; only the compiled outputs land in ``oracle/_ref/``,
 which git ignores but which travels with the tree to the GPU box.
 
-Artefacts (all built from the reference checkout, ``PKV_REFERENCE_DIR``):
+Artefacts (all built from the reference checkout: the directory named by
+``PKV_REFERENCE_DIR``, else the ``reference_path`` that ``BASELINE.json``
+records; nothing is built when neither names an existing checkout):
 
 * ``libref_smoke.so`` -- ``tests/smoke_test.cu`` (with ``kernels/
   persistentkv_attention.cuh``) compiled as a shared library with its ``main``
@@ -22,6 +24,7 @@ Artefacts (all built from the reference checkout, ``PKV_REFERENCE_DIR``):
 from __future__ import annotations
 
 import argparse
+import json
 import os
 import subprocess
 import sys
@@ -29,13 +32,28 @@ from pathlib import Path
 
 ORACLE_DIR = Path(__file__).resolve().parent
 REF_OUT = ORACLE_DIR / "_ref"
-REFERENCE_DIR = Path(os.environ.get("PKV_REFERENCE_DIR", "/root/reference"))
+
+
+def _reference_dir() -> Path | None:
+    env = os.environ.get("PKV_REFERENCE_DIR")
+    if env:
+        return Path(env)
+    baseline = ORACLE_DIR.parent / "BASELINE.json"
+    try:
+        recorded = json.loads(baseline.read_text()).get("reference_path")
+    except (OSError, ValueError):
+        recorded = None
+    return Path(recorded) if recorded else None
+
+
+REFERENCE_DIR = _reference_dir()
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc")
 
 
 def reference_present() -> bool:
-    return (REFERENCE_DIR / "kernels" / "persistentkv_attention.cuh").exists()
+    return REFERENCE_DIR is not None and (
+        REFERENCE_DIR / "kernels" / "persistentkv_attention.cuh").exists()
 
 
 def _newer(target: Path, *sources: Path) -> bool:

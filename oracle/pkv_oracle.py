@@ -17,6 +17,13 @@ It restates, in numpy, the reference's CPU algorithm for the path:
   reference's four extension entry points
   (``tests/persistentkv_torch_extension.cu:35-317``) and of its repack + SDPA
   oracle (``tests/benchmark_torch_paged_sdpa.py:90-109``);
+* ``sdpa_repack_row`` / ``torch_paged_decode`` -- the reference's repack +
+  SDPA oracle in torch (``tests/benchmark_torch_paged_sdpa.py:90-109``:
+  index_select of the row's pages, permute to [Hkv, tokens, D], slice to the
+  row's length, ``scaled_dot_product_attention(enable_gqa=True)``): the
+  first in fp32 through torch's own SDPA (the timed CPU baseline of
+  ``bench.py``), the second in float64 on any device (the checker of
+  full-size steps whose K/V are too large to copy to the host);
 * ``GlibcRand`` -- glibc's ``rand()`` (the TYPE_3 additive-feedback generator
   with its LCG seeding, as published), so the smoke test's ``srand(42)`` input
   stream (``tests/smoke_test.cu:77-81, :438``) can be replayed here and on a
@@ -254,3 +261,58 @@ def kv_append(k_new, v_new, k_pages, v_pages, block_table, positions, free_pages
     new_count = avail - min(taken, avail) if free_pages is not None else free_count
     return new_count, errors
 
+
+
+def sdpa_repack_row(q_row, k_pages, v_pages, pages, n):
+    """One row through the reference's torch repack + SDPA path
+    (tests/benchmark_torch_paged_sdpa.py:90-109) in fp32 on torch tensors:
+    q_row [Hq, D], pools [P, Hkv, page, D], pages = the row's physical page
+    ids (int64 tensor) -> [Hq, D]."""
+    import torch
+    import torch.nn.functional as F
+
+    hkv, page = k_pages.shape[1], k_pages.shape[2]
+    n_pages = pages.numel()
+    k = (torch.index_select(k_pages, 0, pages).permute(1, 0, 2, 3).contiguous()
+         .view(1, hkv, n_pages * page, HEAD_DIM))[:, :, :n]
+    v = (torch.index_select(v_pages, 0, pages).permute(1, 0, 2, 3).contiguous()
+         .view(1, hkv, n_pages * page, HEAD_DIM))[:, :, :n]
+    out = F.scaled_dot_product_attention(q_row[None, :, None, :], k, v, is_causal=False,
+                                         enable_gqa=True)
+    return out[0, :, 0, :]
+
+
+def torch_paged_decode(q_source, k_pages, v_pages, block_table, seq_lens, q_indices=None,
+                       out_indices=None, out_rows=None):
+    """``paged_decode`` in float64 with torch on the tensors' own device: per
+    row, the repack of benchmark_torch_paged_sdpa.py:90-103 and exact
+    softmax(q k^T / sqrt(128)) v.  Rows never written stay NaN."""
+    import torch
+
+    dev = k_pages.device
+    bt = torch.as_tensor(block_table, device=dev).long()
+    sl = [int(x) for x in (seq_lens.tolist() if hasattr(seq_lens, "tolist") else seq_lens)]
+    b = bt.shape[0]
+    hq = q_source.shape[1]
+    hkv, page = k_pages.shape[1], k_pages.shape[2]
+    g = hq // hkv
+    qi = list(range(b)) if q_indices is None else [int(x) for x in q_indices]
+    oi = list(range(b)) if out_indices is None else [int(x) for x in out_indices]
+    rows = out_rows if out_rows is not None else b
+    out = torch.full((rows, hq, HEAD_DIM), float("nan"), dtype=torch.float64, device=dev)
+    # the fp32 scale 1.0f / sqrtf(128) of the reference (smoke_test.cu:35-74)
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(HEAD_DIM)))
+    for r in range(b):
+        n = sl[r]
+        if n <= 0:
+            out[oi[r]] = 0.0
+            continue
+        pages = bt[r, : (n + page - 1) // page]
+        k = k_pages.index_select(0, pages).permute(1, 0, 2, 3).reshape(hkv, -1, HEAD_DIM)[:, :n]
+        v = v_pages.index_select(0, pages).permute(1, 0, 2, 3).reshape(hkv, -1, HEAD_DIM)[:, :n]
+        q = q_source[qi[r]].double().view(hkv, g, HEAD_DIM)
+        s = torch.einsum("hgd,hnd->hgn", q, k.double()) * scale
+        w = torch.exp(s - s.amax(dim=2, keepdim=True))
+        o = torch.einsum("hgn,hnd->hgd", w, v.double()) / w.sum(dim=2, keepdim=True)
+        out[oi[r]] = o.reshape(hq, HEAD_DIM)
+    return out

@@ -3,15 +3,21 @@
 No torch types cross this boundary: tensors are passed as device pointers plus
 sizes, streams as raw ``cudaStream_t`` handles.  The library must exist; there
 is no fallback path (build it with ``python -m persistentkv_attention_b200.build``).
+
+``PKV_LIB_VARIANT=stamps`` in the environment loads the diagnostic build
+``libpkv_b200_stamps.so`` instead (same ABI; decode CTAs record phase stamps).
 """
 
 from __future__ import annotations
 
 import ctypes
 from ctypes import POINTER, c_char_p, c_double, c_float, c_int, c_int32, c_size_t, c_uint32, c_void_p
+import os
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "lib" / "libpkv_b200.so"
+LIB_DIR = Path(__file__).resolve().parent / "lib"
+LIB_NAMES = {"default": "libpkv_b200.so", "stamps": "libpkv_b200_stamps.so"}
+LIB_PATH = LIB_DIR / LIB_NAMES["default"]
 
 PKV_OK = 0
 PKV_ERR_INVALID_ARGUMENT = 1
@@ -28,6 +34,11 @@ PKV_DTYPE_BF16 = 1
 PKV_SPLITS_REFERENCE = 0
 PKV_SPLITS_BALANCED = 1
 PKV_SPLITS_FIXED = 2
+
+PKV_GATHER_TMA = 0
+PKV_GATHER_CP_ASYNC = 1
+GATHER_MODES = {"tma": PKV_GATHER_TMA, "cpasync": PKV_GATHER_CP_ASYNC}
+STAMPS_PER_CTA = 8
 
 PKV_ROUTE_SINGLE_PASS = 0
 PKV_ROUTE_BUCKET = 1
@@ -77,6 +88,9 @@ SIGNATURES = {
     "pkv_status_string": (c_char_p, [c_int]),
     "pkv_abi_version": (c_int, []),
     "pkv_last_error_message": (c_char_p, []),
+    "pkv_set_gather_mode": (c_int, [c_int]),
+    "pkv_get_gather_mode": (c_int, []),
+    "pkv_phase_stamps": (c_int, [POINTER(ctypes.c_uint64), c_int, POINTER(c_int)]),
     "pkv_paged_attention": (
         c_int,
         [_P, _P, _P, _P, _P, _P, c_size_t, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
@@ -171,11 +185,15 @@ def load() -> ctypes.CDLL:
     global _lib
     if _lib is not None:
         return _lib
-    if not LIB_PATH.exists():
+    variant = os.environ.get("PKV_LIB_VARIANT", "default") or "default"
+    if variant not in LIB_NAMES:
+        raise ImportError(f"PKV_LIB_VARIANT={variant!r}: expected one of {sorted(LIB_NAMES)}")
+    path = LIB_DIR / LIB_NAMES[variant]
+    if not path.exists():
         raise ImportError(
-            f"{LIB_PATH} is missing: build it with `python -m persistentkv_attention_b200.build`"
+            f"{path} is missing: build it with `python -m persistentkv_attention_b200.build`"
         )
-    lib = ctypes.CDLL(str(LIB_PATH))
+    lib = ctypes.CDLL(str(path))
     for name, (restype, argtypes) in SIGNATURES.items():
         fn = getattr(lib, name)
         fn.restype = restype
@@ -211,3 +229,23 @@ def device_error(clear: bool = True) -> int:
 
 def describe_device_error(code: int) -> str:
     return ", ".join(text for bit, text in DEVERR_BITS.items() if code & bit) or "none"
+
+
+def set_gather_mode(mode: str) -> None:
+    """Selects the decode gather of later 16-bit launches: "tma" or "cpasync"."""
+    check(load().pkv_set_gather_mode(GATHER_MODES[mode]))
+
+
+def gather_mode() -> str:
+    value = load().pkv_get_gather_mode()
+    return {v: k for k, v in GATHER_MODES.items()}[value]
+
+
+def phase_stamps(max_ctas: int = 4096):
+    """Per-CTA phase stamps of the last decode launch (diagnostic build only):
+    a list of ``STAMPS_PER_CTA``-tuples of %globaltimer nanoseconds."""
+    lib = load()
+    buf = (ctypes.c_uint64 * (max_ctas * STAMPS_PER_CTA))()
+    n = c_int(0)
+    check(lib.pkv_phase_stamps(buf, max_ctas, ctypes.byref(n)))
+    return [tuple(buf[i * STAMPS_PER_CTA:(i + 1) * STAMPS_PER_CTA]) for i in range(n.value)]

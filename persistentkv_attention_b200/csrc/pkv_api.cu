@@ -1,5 +1,6 @@
 // pkv_api.cu -- C ABI of the B200 paged decode engine (declared in
-// include/pkv_b200.h): argument validation, TMA tensor maps, kernel dispatch.
+// include/pkv_b200.h): argument validation, gather-mode and kernel dispatch,
+// the merge / combine / stage-in / append launches.
 //
 // Validation mirrors the reference's operator checks
 // (tests/persistentkv_torch_extension.cu:9-31 and the per-entry TORCH_CHECKs)
@@ -13,9 +14,13 @@
 #include <mutex>
 
 #include "../../include/pkv_b200.h"
-#include "pkv_kernels.cuh"
+#include "pkv_aux_kernels.cuh"
+#include "pkv_launch.cuh"
 
 using namespace pkv;
+using pkv_internal::kCtasPerSm;
+using pkv_internal::kMaxDevices;
+using pkv_internal::LaunchSpec;
 
 // Device-side error word (one per device that loads the library).
 __device__ unsigned int g_pkv_error_word = 0u;
@@ -28,18 +33,14 @@ __device__ unsigned int g_pkv_error_word = 0u;
 // a stand-in: kernels get its device address from cudaGetSymbolAddress.
 static __device__ __align__(256) unsigned char g_pkv_noalloc_scratch[PKV_NOALLOC_SCRATCH_BYTES];
 
-namespace {
+#ifdef PKV_PHASE_STAMPS
+// Per-CTA %globaltimer phase stamps of the last decode launches (diagnostic
+// build only): [CTA][kStampsPerCta].
+constexpr int kStampCtasMax = 4096;
+__device__ unsigned long long g_pkv_stamps[kStampCtasMax * kStampsPerCta];
+#endif
 
-#ifndef PKV_RING_SLOTS
-#define PKV_RING_SLOTS 8
-#endif
-#ifndef PKV_LOAD_MODE
-#define PKV_LOAD_MODE 1
-#endif
-constexpr int kSlots = PKV_RING_SLOTS;          // ring depth (8 KB per slot)
-constexpr int kLoadMode = PKV_LOAD_MODE;        // kLoadCpAsync or kLoadTma
-constexpr int kCtasPerSm = PKV_MIN_CTAS_PER_SM;  // resident decode CTAs per SM
-constexpr int kMaxDevices = 64;
+namespace {
 
 thread_local char t_last_error[512] = "";
 
@@ -56,12 +57,29 @@ pkv_status ok_status() {
     return PKV_OK;
 }
 
+// Gather used by the 16-bit decode launches (PKV_GATHER_*; process-wide).
+#ifndef PKV_GATHER_DEFAULT
+#define PKV_GATHER_DEFAULT PKV_GATHER_CP_ASYNC
+#endif
+static_assert((int)PKV_GATHER_TMA == kLoadTma && (int)PKV_GATHER_CP_ASYNC == kLoadCpAsync,
+              "gather enum values are the kernel's LOAD template values");
+std::atomic<int> g_gather_mode{PKV_GATHER_DEFAULT};
+
 }  // namespace
 
 namespace pkv_internal {
 // Error reporting shared with the other translation units of the library.
 pkv_status set_error(pkv_status st, const char* msg) { return fail(st, "%s", msg); }
 void clear_error() { t_last_error[0] = '\0'; }
+pkv_status fail_fmt(pkv_status st, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+    va_end(ap);
+    return st;
+}
+pkv_status ok() { return ok_status(); }
+thread_local int t_last_grid = 0;
 }  // namespace pkv_internal
 
 namespace {
@@ -72,6 +90,7 @@ struct DeviceState {
     int sm_count = 0;
     int cc_major = 0;
     unsigned* error_word = nullptr;
+    unsigned long long* stamps = nullptr;  // phase-stamp array (diagnostic build), else null
 };
 DeviceState g_devices[kMaxDevices];
 std::mutex g_device_mutex;
@@ -107,6 +126,16 @@ pkv_status current_device(DeviceState** out) {
                 return fail(PKV_ERR_CUDA, "cudaGetSymbolAddress(error word) failed: %s",
                             cudaGetErrorString(e));
             }
+#ifdef PKV_PHASE_STAMPS
+            void* sptr = nullptr;
+            e = cudaGetSymbolAddress(&sptr, g_pkv_stamps);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                return fail(PKV_ERR_CUDA, "cudaGetSymbolAddress(phase stamps) failed: %s",
+                            cudaGetErrorString(e));
+            }
+            ds.stamps = static_cast<unsigned long long*>(sptr);
+#endif
             ds.sm_count = sms;
             ds.cc_major = major;
             ds.error_word = static_cast<unsigned*>(ptr);
@@ -241,132 +270,74 @@ pkv_status check_common(const Common& c) {
 int box_rows_for(int page_size) { return page_size % 16 == 0 ? 16 : 8; }
 
 // ------------------------------------------------------------ launch
-struct LaunchSpec {
-    DecodeParams dp;
-    bool merge;       // run the separate merge kernel after decode
-    bool pdl = false; // decode may launch early behind the previous kernel (it waits on it)
-    bool kv8 = false; // e4m3 K/V pools (cp.async producer; no tensor maps)
-    int G;
-    int box_rows;
-    pkv_dtype dtype;
-    const void* k;
-    const void* v;
-    long long rows;
-};
-
-template <int G, typename T, int BR, bool KV8 = false>
-pkv_status launch_typed(const LaunchSpec& ls, const CUtensorMap& tk, const CUtensorMap& tv,
-                        cudaStream_t stream, DeviceState* ds) {
-    auto kern = pkv_decode_kernel<G, T, BR, kSlots, KV8 ? kLoadCpAsync : kLoadMode, KV8>;
-    const size_t smem = decode_smem_bytes<G, kSlots>();
-    // the device schedule's grid (2 CTAs per SM) must be resident in one wave
-    static_assert(decode_fits_two_per_sm<G, kSlots>(), "decode CTA too large for 2 per SM");
-    static std::atomic<unsigned long long> attr_done{0ull};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const unsigned long long bit = 1ull << (dev & 63);
-    if (!(attr_done.load(std::memory_order_acquire) & bit)) {
-        cudaError_t e =
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) {
-            cudaGetLastError();
-            return fail(PKV_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
-        }
-        attr_done.fetch_or(bit, std::memory_order_acq_rel);
-    }
-    const int resident = kCtasPerSm * ds->sm_count;
-    const int grid = ls.dp.auto_groups > 0
-                         ? ls.dp.auto_groups * ls.dp.Hkv
-                         : (ls.dp.num_items < resident ? ls.dp.num_items : resident);
-    if (ls.dp.xg_world > 0) {
-        // the sharded step waits on peers inside the kernel: every CTA of the
-        // launch must be able to be resident at once
-        static std::atomic<int> occupancy[kMaxDevices];
-        int occ = occupancy[dev & (kMaxDevices - 1)].load(std::memory_order_acquire);
-        if (occ == 0) {
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem) !=
-                cudaSuccess) {
-                cudaGetLastError();
-                occ = 0;
-            }
-            occupancy[dev & (kMaxDevices - 1)].store(occ, std::memory_order_release);
-        }
-        if (grid > occ * ds->sm_count) {
-            return fail(PKV_ERR_UNSUPPORTED,
-                        "sharded decode needs %d resident CTAs but the device holds %d", grid,
-                        occ * ds->sm_count);
-        }
-    }
+template <typename T>
+pkv_status launch_merge_t(const LaunchSpec& ls, cudaStream_t stream) {
+    MergeParams mp;
+    mp.part_m = ls.dp.part_m;
+    mp.part_l = ls.dp.part_l;
+    mp.part_acc = ls.dp.part_acc;
+    mp.split_offsets = ls.dp.work_items != nullptr ? ls.dp.split_offsets : nullptr;
+    mp.seq_lens = ls.dp.seq_lens;
+    mp.auto_groups = ls.dp.auto_groups;
+    mp.max_pages = ls.dp.max_pages;
+    mp.page_size = ls.dp.page_size;
+    mp.out_indices = ls.dp.out_indices;
+    mp.out = ls.dp.out;
+    mp.state_out = ls.dp.state_out;
+    mp.error = ls.dp.error;
+    mp.B = ls.dp.B;
+    mp.Hq = ls.dp.Hq;
+    mp.Hkv = ls.dp.Hkv;
+    mp.out_rows = ls.dp.out_rows;
+    mp.num_splits = ls.dp.num_splits;
+    mp.total_slots = ls.dp.total_slots;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ls.dp.Hkv, ls.dp.B);
+    cfg.blockDim = dim3(kHeadDim);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     cudaError_t e;
-    if (ls.pdl) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(grid);
-        cfg.blockDim = dim3(kThreads);
-        cfg.dynamicSmemBytes = smem;
-        cfg.stream = stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, kern, ls.dp, tk, tv);
-    } else {
-        kern<<<grid, kThreads, smem, stream>>>(ls.dp, tk, tv);
-        e = cudaGetLastError();
+    switch (ls.G) {
+        case 1: e = cudaLaunchKernelEx(&cfg, pkv_merge_kernel<1, T>, mp); break;
+        case 2: e = cudaLaunchKernelEx(&cfg, pkv_merge_kernel<2, T>, mp); break;
+        case 4: e = cudaLaunchKernelEx(&cfg, pkv_merge_kernel<4, T>, mp); break;
+        case 8: e = cudaLaunchKernelEx(&cfg, pkv_merge_kernel<8, T>, mp); break;
+        default: return fail(PKV_ERR_UNSUPPORTED, "unsupported G=%d", ls.G);
     }
     if (e != cudaSuccess) {
         cudaGetLastError();
-        return fail(PKV_ERR_CUDA, "decode launch failed: %s", cudaGetErrorString(e));
-    }
-    if (ls.merge) {
-        MergeParams mp;
-        mp.part_m = ls.dp.part_m;
-        mp.part_l = ls.dp.part_l;
-        mp.part_acc = ls.dp.part_acc;
-        mp.split_offsets = ls.dp.work_items != nullptr ? ls.dp.split_offsets : nullptr;
-        mp.seq_lens = ls.dp.seq_lens;
-        mp.auto_groups = ls.dp.auto_groups;
-        mp.max_pages = ls.dp.max_pages;
-        mp.page_size = ls.dp.page_size;
-        mp.out_indices = ls.dp.out_indices;
-        mp.out = ls.dp.out;
-        mp.state_out = ls.dp.state_out;
-        mp.error = ls.dp.error;
-        mp.B = ls.dp.B;
-        mp.Hq = ls.dp.Hq;
-        mp.Hkv = ls.dp.Hkv;
-        mp.out_rows = ls.dp.out_rows;
-        mp.num_splits = ls.dp.num_splits;
-        mp.total_slots = ls.dp.total_slots;
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(ls.dp.Hkv, ls.dp.B);
-        cfg.blockDim = dim3(kHeadDim);
-        cfg.dynamicSmemBytes = 0;
-        cfg.stream = stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, pkv_merge_kernel<G, T>, mp);
-        if (e != cudaSuccess) {
-            cudaGetLastError();
-            return fail(PKV_ERR_CUDA, "merge launch failed: %s", cudaGetErrorString(e));
-        }
+        return fail(PKV_ERR_CUDA, "merge launch failed: %s", cudaGetErrorString(e));
     }
     return ok_status();
 }
 
-template <typename T, int BR, bool KV8 = false>
-pkv_status launch_g(const LaunchSpec& ls, const CUtensorMap& tk, const CUtensorMap& tv,
-                    cudaStream_t s, DeviceState* ds) {
-    switch (ls.G) {
-        case 1: return launch_typed<1, T, BR, KV8>(ls, tk, tv, s, ds);
-        case 2: return launch_typed<2, T, BR, KV8>(ls, tk, tv, s, ds);
-        case 4: return launch_typed<4, T, BR, KV8>(ls, tk, tv, s, ds);
-        case 8: return launch_typed<8, T, BR, KV8>(ls, tk, tv, s, ds);
-        default: return fail(PKV_ERR_UNSUPPORTED, "unsupported G=%d", ls.G);
+// The decode kernel of the spec's configuration, then the separate merge.
+pkv_status launch_decode(const LaunchSpec& ls, const CUtensorMap& tk, const CUtensorMap& tv,
+                         cudaStream_t stream) {
+    using namespace pkv_internal;
+    const bool f16 = ls.kv8 || ls.dtype == PKV_DTYPE_F16;
+    const bool b16 = ls.box_rows == 16;
+    if (ls.kv8) {
+        return b16 ? launch_g<__half, 16, kLoadCpAsync, true>(ls, tk, tv, stream)
+                   : launch_g<__half, 8, kLoadCpAsync, true>(ls, tk, tv, stream);
     }
+    if (ls.load == kLoadTma) {
+        if (f16)
+            return b16 ? launch_g<__half, 16, kLoadTma, false>(ls, tk, tv, stream)
+                       : launch_g<__half, 8, kLoadTma, false>(ls, tk, tv, stream);
+        return b16 ? launch_g<__nv_bfloat16, 16, kLoadTma, false>(ls, tk, tv, stream)
+                   : launch_g<__nv_bfloat16, 8, kLoadTma, false>(ls, tk, tv, stream);
+    }
+    if (f16)
+        return b16 ? launch_g<__half, 16, kLoadCpAsync, false>(ls, tk, tv, stream)
+                   : launch_g<__half, 8, kLoadCpAsync, false>(ls, tk, tv, stream);
+    return b16 ? launch_g<__nv_bfloat16, 16, kLoadCpAsync, false>(ls, tk, tv, stream)
+               : launch_g<__nv_bfloat16, 8, kLoadCpAsync, false>(ls, tk, tv, stream);
 }
 
 pkv_status launch(LaunchSpec& ls, void* stream_ptr) {
@@ -375,24 +346,23 @@ pkv_status launch(LaunchSpec& ls, void* stream_ptr) {
     pkv_status st = current_device(&ds);
     if (st != PKV_OK) return st;
     ls.dp.error = ds->error_word;
+    ls.dp.stamps = ds->stamps;
+    ls.sm_count = ds->sm_count;
+    ls.load = ls.kv8 ? kLoadCpAsync : g_gather_mode.load(std::memory_order_relaxed);
     CUtensorMap tk, tv;
+    std::memset(&tk, 0, sizeof(tk));
+    std::memset(&tv, 0, sizeof(tv));
+    if (ls.load == kLoadTma) {  // the cp.async producer reads no tensor map
+        st = kv_tensor_map(ls.k, ls.rows, ls.dtype, ls.box_rows, &tk);
+        if (st != PKV_OK) return st;
+        st = kv_tensor_map(ls.v, ls.rows, ls.dtype, ls.box_rows, &tv);
+        if (st != PKV_OK) return st;
+    }
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-    if (ls.kv8) {  // the cp.async producer needs no tensor maps
-        std::memset(&tk, 0, sizeof(tk));
-        std::memset(&tv, 0, sizeof(tv));
-        return ls.box_rows == 16 ? launch_g<__half, 16, true>(ls, tk, tv, stream, ds)
-                                 : launch_g<__half, 8, true>(ls, tk, tv, stream, ds);
-    }
-    st = kv_tensor_map(ls.k, ls.rows, ls.dtype, ls.box_rows, &tk);
-    if (st != PKV_OK) return st;
-    st = kv_tensor_map(ls.v, ls.rows, ls.dtype, ls.box_rows, &tv);
-    if (st != PKV_OK) return st;
-    if (ls.dtype == PKV_DTYPE_F16) {
-        return ls.box_rows == 16 ? launch_g<__half, 16>(ls, tk, tv, stream, ds)
-                                 : launch_g<__half, 8>(ls, tk, tv, stream, ds);
-    }
-    return ls.box_rows == 16 ? launch_g<__nv_bfloat16, 16>(ls, tk, tv, stream, ds)
-                             : launch_g<__nv_bfloat16, 8>(ls, tk, tv, stream, ds);
+    st = launch_decode(ls, tk, tv, stream);
+    if (st != PKV_OK || !ls.merge) return st;
+    return (ls.kv8 || ls.dtype == PKV_DTYPE_F16) ? launch_merge_t<__half>(ls, stream)
+                                                 : launch_merge_t<__nv_bfloat16>(ls, stream);
 }
 
 void fill_common(LaunchSpec& ls, const Common& c) {
@@ -601,6 +571,48 @@ const char* pkv_status_string(pkv_status status) {
 int pkv_abi_version(void) { return PKV_ABI_VERSION; }
 
 const char* pkv_last_error_message(void) { return t_last_error; }
+
+pkv_status pkv_set_gather_mode(pkv_gather mode) {
+    if (mode != PKV_GATHER_TMA && mode != PKV_GATHER_CP_ASYNC)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "unknown gather mode %d", (int)mode);
+    g_gather_mode.store((int)mode, std::memory_order_relaxed);
+    return ok_status();
+}
+
+pkv_gather pkv_get_gather_mode(void) {
+    return (pkv_gather)g_gather_mode.load(std::memory_order_relaxed);
+}
+
+pkv_status pkv_phase_stamps(uint64_t* out, int max_ctas, int* n_ctas) {
+#ifdef PKV_PHASE_STAMPS
+    if (out == nullptr || n_ctas == nullptr || max_ctas <= 0)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "out, n_ctas and max_ctas must be valid");
+    DeviceState* ds = nullptr;
+    pkv_status st = current_device(&ds);
+    if (st != PKV_OK) return st;
+    int n = pkv_internal::t_last_grid;
+    if (n > kStampCtasMax) n = kStampCtasMax;
+    if (n > max_ctas) n = max_ctas;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess)
+        e = cudaMemcpy(out, ds->stamps, (size_t)n * kStampsPerCta * sizeof(uint64_t),
+                       cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess)
+        e = cudaMemset(ds->stamps, 0, (size_t)kStampCtasMax * kStampsPerCta * sizeof(uint64_t));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(PKV_ERR_CUDA, "reading the phase stamps failed: %s", cudaGetErrorString(e));
+    }
+    *n_ctas = n;
+    return ok_status();
+#else
+    (void)out;
+    (void)max_ctas;
+    if (n_ctas != nullptr) *n_ctas = 0;
+    return fail(PKV_ERR_UNSUPPORTED,
+                "phase stamps need the diagnostic build (PKV_PHASE_STAMPS, libpkv_b200_stamps.so)");
+#endif
+}
 
 size_t pkv_workspace_bytes(int B, int Hq, int num_splits) {
     if (num_splits <= 1 || B <= 0 || Hq <= 0) return 0;

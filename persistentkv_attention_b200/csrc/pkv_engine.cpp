@@ -88,8 +88,7 @@ struct pkv_engine {
     int32_t* dh_meta[kStaging];    // the same buffers as the device addresses them
     cudaEvent_t staged[kStaging];  // the launch that read staging buffer i has finished
     int next;
-    const void* checked[2];        // last q / out host pointers found page-locked
-    void* mapped[2];               // and their device addresses
+    void* mapped[2];               // device addresses of this call's q / out host buffers
     std::vector<StepGraph> graphs;
     bool no_graphs;                // capture failed or is impossible here: launch directly
 };
@@ -173,10 +172,11 @@ pkv_status pkv_engine_step_host(pkv_engine* e, const int32_t* seq_lens,
     if (h2d_bytes) *h2d_bytes = 0;
     if (d2h_bytes) *d2h_bytes = 0;
     if (B == 0) return PKV_OK;
-    // the kernel dereferences q_host / out_host: they must be page-locked
+    // the kernels dereference q_host / out_host: they must be page-locked and
+    // mapped.  Checked on every call (a pointer value seen before may now
+    // belong to another allocation).
     const void* host_ptrs[2] = {q_host, out_host};
     for (int k = 0; k < 2; ++k) {
-        if (host_ptrs[k] == e->checked[k]) continue;
         cudaPointerAttributes attr;
         cudaError_t aerr = cudaPointerGetAttributes(&attr, host_ptrs[k]);
         if (aerr != cudaSuccess || attr.type != cudaMemoryTypeHost ||
@@ -187,7 +187,6 @@ pkv_status pkv_engine_step_host(pkv_engine* e, const int32_t* seq_lens,
                          "(cudaHostAlloc / pinned)",
                          k == 0 ? "q_host" : "out_host");
         }
-        e->checked[k] = host_ptrs[k];
         e->mapped[k] = attr.devicePointer;
     }
     // every row must fit the block-table columns it brings

@@ -1,4 +1,5 @@
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -13,6 +14,22 @@ if str(REPO) not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU")
+
+
+@pytest.fixture(autouse=True)
+def _gather_mode():
+    """PKV_GATHER=tma|cpasync runs every test with that decode gather (the
+    library default otherwise), so the whole GPU suite can run on both."""
+    mode = os.environ.get("PKV_GATHER")
+    if not mode:
+        yield
+        return
+    from persistentkv_attention_b200 import _native
+
+    prev = _native.gather_mode()
+    _native.set_gather_mode(mode)
+    yield
+    _native.set_gather_mode(prev)
 
 
 @pytest.fixture(scope="session")

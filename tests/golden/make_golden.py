@@ -23,12 +23,23 @@ Fixtures written (all small):
   outputs for each reference trace.
 * ``trace_files.json`` -- ``load_trace_specs`` and the requests / steps built
   from the committed ``trace_specs.csv`` / ``trace_specs.json``.
+* ``harness_calls.json.gz`` -- the operator calls the reference's serving-trace
+  harness makes per decode step: ``compile_persistentkv_metadata`` +
+  ``run_persistentkv_step_compiled`` (tests/benchmark_serving_trace.py:655-781,
+  :949-1001) run here with a recording module in place of the extension,
+  for four of its routes (work queue with auto splits and fused merge, work
+  queue with 20 requested splits, length buckets through the indexed entry
+  point, one bucket with auto splits).  Each call keeps the entry-point name
+  and every argument (metadata tensors as int lists, the q / K / V /
+  workspace / output operands by role), so a GPU test can replay the
+  harness's exact call sequence through this engine's ``ops`` and through the
+  reference's extension.
 """
 
 from __future__ import annotations
 
+import gzip
 import json
-import os
 import random
 import sys
 from pathlib import Path
@@ -43,7 +54,7 @@ sys.path.insert(0, str(REPO))
 from oracle import pkv_oracle as po  # noqa: E402
 from oracle import ref  # noqa: E402
 
-REFERENCE_DIR = Path(os.environ.get("PKV_REFERENCE_DIR", "/root/reference"))
+from oracle.build_ref import REFERENCE_DIR  # noqa: E402  (PKV_REFERENCE_DIR or BASELINE.json)
 
 # (kind, B, Hq, Hkv, N, splits, page_size) in smoke_test.cu order (:486-493)
 SMOKE_CASES = [
@@ -100,6 +111,8 @@ class _CpuTorch:
 
 
 def load_harness():
+    if REFERENCE_DIR is None or not (REFERENCE_DIR / "tests").is_dir():
+        raise SystemExit("set PKV_REFERENCE_DIR to the reference checkout")
     sys.path.insert(0, str(REFERENCE_DIR / "tests"))
     import benchmark_serving_trace as harness  # noqa: PLC0415
 
@@ -199,6 +212,79 @@ def make_trace_files(h) -> None:
     (HERE / "trace_files.json").write_text(json.dumps(out))
 
 
+class _Role:
+    """Stands for a large operand the replay supplies itself."""
+
+    def __init__(self, role):
+        self.role = role
+
+    def __getitem__(self, index):          # q_pool[state_index] -> q source of that step
+        return _Role(f"{self.role}[{int(index)}]")
+
+
+class _Recorder:
+    """Records the harness's calls of the extension's four entry points."""
+
+    def __init__(self, outputs):
+        self.calls = []
+        self.outputs = outputs
+
+    def __getattr__(self, name):
+        if not name.startswith("paged_attention"):
+            raise AttributeError(name)
+
+        def record(*args):
+            enc = []
+            for a in args:
+                if isinstance(a, _Role):
+                    enc.append({"role": a.role})
+                elif isinstance(a, torch.Tensor):
+                    if id(a) in self.outputs:
+                        enc.append({"role": "output", "shape": list(a.shape)})
+                    else:
+                        enc.append({"dtype": str(a.dtype).replace("torch.", ""),
+                                    "shape": list(a.shape), "values": a.reshape(-1).tolist()})
+                else:
+                    enc.append(a)
+            self.calls.append({"fn": name, "args": enc})
+
+        return record
+
+
+def make_harness_calls(h) -> None:
+    h.HKV = 8
+    out = []
+    routes = [
+        # (trace, requested splits, bucket tokens, single bucket, auto, workqueue, fused)
+        ("uniform", 16, 0, False, True, True, True),
+        ("bimodal", 20, 0, False, False, True, False),
+        ("bimodal", 16, 2048, False, False, False, False),
+        ("uniform", 16, 0, True, True, False, False),
+    ]
+    for trace, splits, bucket, single, auto, wq, fused in routes:
+        reqs, physical = h.build_requests(trace, 24, 8, 20260622, 0.0, 0, None)
+        steps = h.build_steps(reqs, 8)
+        metas = h.compile_persistentkv_metadata(reqs, steps, splits, bucket, single, auto, False,
+                                                wq)
+        for idx in (0, len(steps) // 2, len(steps) - 1):
+            meta = metas[idx]
+            rec = _Recorder({id(meta.output)})
+            h.run_persistentkv_step_compiled(rec, _Role("q_pool"), _Role("k_pages"),
+                                             _Role("v_pages"), idx, _Role("workspace"), metas,
+                                             fused)
+            state = steps[idx]
+            out.append({
+                "route": {"trace": trace, "splits": splits, "bucket_tokens": bucket,
+                          "single_bucket": single, "auto_splits": auto, "workqueue": wq,
+                          "fused_merge": fused},
+                "step": idx, "requests": 24, "physical_pages": physical,
+                "active_ids": list(state.active_ids), "lengths": list(state.lengths),
+                "output_shape": list(meta.output.shape), "calls": rec.calls,
+            })
+    with gzip.open(HERE / "harness_calls.json.gz", "wt") as f:
+        f.write(json.dumps(out))
+
+
 def main() -> None:
     if not ref.ref_cpu_available():
         raise SystemExit("build oracle/_ref first: python -m oracle.build_ref --skip-torch-ext")
@@ -207,6 +293,7 @@ def main() -> None:
     make_scheduler(h)
     make_traces(h)
     make_trace_files(h)
+    make_harness_calls(h)
     for p in sorted(HERE.glob("*.*")):
         print(p.name, p.stat().st_size)
 

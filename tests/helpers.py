@@ -106,3 +106,18 @@ def assert_close(got: torch.Tensor, ref: np.ndarray, dtype: str, what=""):
         assert diff.max() < MAX_ERR, f"{what}: max err {diff.max():.3e}"
         assert diff.mean() < MEAN_ERR, f"{what}: mean err {diff.mean():.3e}"
     return float(diff.max()), float(diff.mean())
+
+
+def config1_case(seed: int = 20260615 + 4096) -> Case:
+    """BASELINE config 1 exactly: B=1, 4096 tokens, Hq 32 / Hkv 8, head_dim 128,
+    page 16, so 256 logical pages, drawn as a seeded random permutation from a
+    pool of 1024 pages; q / K / V fp16 N(0,1) (every pool page filled).  The
+    seed follows the reference's per-context seeding of its single-request
+    baselines (20260615 + context, benchmark_native_paged_baselines.py:49-51)."""
+    gen = torch.Generator().manual_seed(seed)
+    q = torch.randn(1, 32, 128, generator=gen).half()
+    k = torch.randn(1024, 8, 16, 128, generator=gen).half()
+    v = torch.randn(1024, 8, 16, 128, generator=gen).half()
+    table = torch.randperm(1024, generator=gen)[:256].numpy().astype(np.int32)[None]
+    zero = np.zeros(1, np.int32)
+    return Case(q, k, v, table, np.array([4096], np.int32), zero, zero, 1, 16, "f16")

@@ -120,6 +120,41 @@ def test_torch_mirror_errors_match_reference_messages():
                                       64, 16, 1, False)
 
 
+def test_noalloc_capacity_checked_before_any_device_call(lib):
+    """The no-alloc entry point refuses a queue whose partial states exceed its
+    static scratch (PKV_NOALLOC_SCRATCH_BYTES) before it touches a device."""
+    limit_slots = (8 << 20) // (32 * 130 * 4)
+    st = lib.pkv_paged_attention_workqueue_noalloc(
+        FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 4, 4, 4, 32, 8, 128, 64, 16,
+        8, 128, 16, limit_slots + 1, 0, None)
+    assert st == _native.PKV_ERR_CAPACITY
+    assert b"holds at most" in lib.pkv_last_error_message()
+
+
+def test_gather_mode_switch(lib):
+    """Both gathers are selectable at run time; unknown modes are refused."""
+    prev = _native.gather_mode()
+    try:
+        for mode in ("tma", "cpasync"):
+            _native.set_gather_mode(mode)
+            assert _native.gather_mode() == mode
+        assert lib.pkv_set_gather_mode(7) == _native.PKV_ERR_INVALID_ARGUMENT
+    finally:
+        _native.set_gather_mode(prev)
+
+
+def test_phase_stamps_only_in_the_diagnostic_build(lib):
+    import os
+
+    n = ctypes.c_int(5)
+    buf = (ctypes.c_uint64 * 8)()
+    st = lib.pkv_phase_stamps(buf, 1, ctypes.byref(n))
+    if os.environ.get("PKV_LIB_VARIANT") == "stamps":
+        assert st in (_native.PKV_OK, _native.PKV_ERR_NO_DEVICE)
+    else:
+        assert st == _native.PKV_ERR_UNSUPPORTED and n.value == 0
+
+
 def test_no_cpu_fallback_in_product_path():
     """The engine never imports the oracle."""
     for path in (REPO / "persistentkv_attention_b200").rglob("*.py"):

@@ -96,3 +96,28 @@ def test_bf16_quantize_round_to_nearest_even():
     assert q[0] == 1.0 and q[1] == 1.0 and q[2] == np.float32(1.0078125)
     assert np.abs(q[3] - x[3]) / abs(x[3]) < 2 ** -8
     assert len(SMOKE_CASES) == 8
+
+
+def test_torch_repack_forms_match_numpy_oracle():
+    """The repack + SDPA forms (benchmark_torch_paged_sdpa.py:90-109) agree
+    with the numpy oracle: torch's fp32 SDPA (the CPU baseline) to fp32
+    rounding, the float64 checker to 1e-12."""
+    import torch
+
+    rng = np.random.default_rng(11)
+    hq, hkv, page, pool = 32, 8, 16, 40
+    kp = po.quantize(rng.standard_normal((pool, hkv, page, 128)))
+    vp = po.quantize(rng.standard_normal((pool, hkv, page, 128)))
+    table = rng.permutation(pool)[:24].reshape(3, 8).astype(np.int32)
+    seq = np.array([100, 0, 128], np.int32)
+    q = po.quantize(rng.standard_normal((3, hq, 128)))
+    want = po.paged_decode(q, kp, vp, table, seq_lens=seq)
+    got64 = po.torch_paged_decode(torch.from_numpy(q), torch.from_numpy(kp),
+                                  torch.from_numpy(vp), table, seq)
+    assert np.abs(got64.numpy() - want).max() < 1e-12
+    kt, vt = torch.from_numpy(kp), torch.from_numpy(vp)
+    for r in (0, 2):
+        n = int(seq[r])
+        pages = torch.from_numpy(table[r, : (n + page - 1) // page]).long()
+        got = po.sdpa_repack_row(torch.from_numpy(q[r]), kt, vt, pages, n).numpy()
+        assert np.abs(got - want[r]).max() < 1e-5

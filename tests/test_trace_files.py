@@ -1,4 +1,4 @@
-"""External trace files (SURVEY next-row 3): the loader and the requests /
+"""External trace files: the loader and the requests /
 steps built from it match the reference's own ``load_trace_specs`` /
 ``build_requests(trace_file=...)`` / ``build_steps`` on the committed files
 (golden outputs from ``tests/golden/make_golden.py``)."""

@@ -5,9 +5,12 @@ Some callers cannot allocate device memory on the decode path: an FFI host
 owning every allocation through its own pool, or code that must not call
 cudaMalloc there.  They cannot supply the workspace the other entry points
 need, so this variant keeps its split partial states in a static device
-array inside the library.  This test calls it through the C ABI, twice in a
-row on different inputs (the array keeps the first call's contents), and
-checks each result against the ordinary work-queue entry point.  It lives in
+array inside the library.  This test calls it through the C ABI several
+times in a row (the array keeps the previous call's contents): twice with the
+same row lengths, hence the same slot layout, on different data -- so a call
+whose partial writes went missing would merge the previous call's partials
+and fail -- then once with another shape.  Each result is checked against
+the ordinary work-queue entry point and against the CPU oracle.  It lives in
 its own file so pytest collects it last.
 """
 
@@ -19,7 +22,7 @@ import torch
 
 from persistentkv_attention_b200 import _native, ops
 from persistentkv_attention_b200.scheduler import Router
-from tests.helpers import MAX_ERR, make_case
+from tests.helpers import MAX_ERR, assert_close, make_case
 
 pytestmark = pytest.mark.gpu
 
@@ -53,9 +56,11 @@ def _with_workspace(c, d, queue):
 
 def test_noalloc_matches_workspace_entry_twice_in_a_row():
     lib = _native.load()
-    cases = [make_case([4096, 700, 9000, 33, 2048], seed=101, indexed=True),
-             make_case([12000, 1, 517, 6000], seed=202, indexed=True)]
-    for c in cases:  # two calls in a row: the second sees the first call's scratch contents
+    same = [4096, 700, 9000, 33, 2048]
+    cases = [make_case(same, seed=101, indexed=True),
+             make_case(same, seed=202, indexed=True),      # same slots, other data
+             make_case([12000, 1, 517, 6000], seed=303, indexed=True)]
+    for c in cases:  # calls in a row: each sees the previous call's scratch contents
         d = c.cuda()
         queue = Router.b200(32, c.hkv).build_workqueue(c.seq_lens)
         assert queue.total_slots > len(c.seq_lens)  # real splits: the scratch is used
@@ -67,6 +72,8 @@ def test_noalloc_matches_workspace_entry_twice_in_a_row():
         diff = (got[rows].float() - want[rows].float()).abs().max().item()
         assert diff < MAX_ERR, diff
         assert torch.isfinite(got[rows].float()).all()
+        want_cpu = c.oracle()
+        assert_close(got[rows], want_cpu[c.out_indices], "f16", "no-alloc vs oracle")
     assert _native.device_error(clear=True) == 0
 
 
