@@ -93,11 +93,15 @@ pkv_gather pkv_get_gather_mode(void);
 
 /* Diagnostic build only (libpkv_b200_stamps.so, compiled with
  * PKV_PHASE_STAMPS): copies the per-CTA %globaltimer stamps of the last
- * decode launch on this thread -- PKV_STAMPS_PER_CTA values per CTA, see
- * the kernel's stamp list -- into out (max_ctas * PKV_STAMPS_PER_CTA
+ * decode launch on this thread -- PKV_STAMPS_PER_CTA values per CTA:
+ * %globaltimer at entry, schedule resolved, first page ids, first copy
+ * issued, first data, last stage, last merge start and exit, then the SM id,
+ * work items, tokens streamed and pieces of the last merge, then SM clock
+ * cycles of the prologue's and the last merge's steps -- into out
+ * (max_ctas * PKV_STAMPS_PER_CTA
  * uint64), sets *n_ctas, clears the device copy and synchronises the device.
  * The regular library returns PKV_ERR_UNSUPPORTED. */
-#define PKV_STAMPS_PER_CTA 8
+#define PKV_STAMPS_PER_CTA 32
 pkv_status pkv_phase_stamps(uint64_t* out, int max_ctas, int* n_ctas);
 
 /* ---------------------------------------------------------------------------

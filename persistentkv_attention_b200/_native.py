@@ -38,7 +38,7 @@ PKV_SPLITS_FIXED = 2
 PKV_GATHER_TMA = 0
 PKV_GATHER_CP_ASYNC = 1
 GATHER_MODES = {"tma": PKV_GATHER_TMA, "cpasync": PKV_GATHER_CP_ASYNC}
-STAMPS_PER_CTA = 8
+STAMPS_PER_CTA = 32
 
 PKV_ROUTE_SINGLE_PASS = 0
 PKV_ROUTE_BUCKET = 1

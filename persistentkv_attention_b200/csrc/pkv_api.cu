@@ -388,8 +388,11 @@ void fill_common(LaunchSpec& ls, const Common& c) {
     ls.merge = false;
 }
 
-// Workspace layout (internal): acc[slots*Hq*128] | m[slots*Hq] | l[slots*Hq],
-// acc first so its rows stay 16-byte aligned for vector loads.
+// Workspace layout (internal): acc[Hkv][slots][G][128] | m[Hkv][slots][G] |
+// l[Hkv][slots][G]: acc first so its rows stay 16-byte aligned, and the slots
+// of one (row, KV head) one contiguous block, which the end-of-CTA merge
+// moves into shared memory with bulk copies.  Same size as the reference's
+// slots * Hq * (128 + 2) floats.
 void partition_workspace(DecodeParams& dp, void* ws, long long slots) {
     float* base = static_cast<float*>(ws);
     dp.part_acc = base;

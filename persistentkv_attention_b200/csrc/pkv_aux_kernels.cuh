@@ -37,6 +37,8 @@ __device__ __forceinline__ void auto_slot_range(const MergeParams& p, int row, i
     long long mine = 0;
     for (int b = t; b < p.B; b += 128) mine += tiles_of(b);
     const long long T = block_sum(mine, s_red);
+    SchedDiv sd;
+    sd.init(T, p.auto_groups);
     // tile prefix of every row below `row`, then their piece counts
     long long pre = 0;
     for (int b = t; b < row; b += 128) pre += tiles_of(b);
@@ -62,13 +64,13 @@ __device__ __forceinline__ void auto_slot_range(const MergeParams& p, int row, i
         __syncthreads();
         const long long pfx = base + warp_off + x - n;
         int gf = 0, gl = -1;
-        if (b < row) auto_row_groups(pfx, n, T, p.auto_groups, gf, gl);
+        if (b < row) auto_row_groups(pfx, n, sd, gf, gl);
         pieces_before += (b < row) ? (gl - gf + 1) : 0;
         base += chunk_total;
     }
     const long long O_row = block_sum(pieces_before, s_red);
     int gf, gl;
-    auto_row_groups(P_row, tiles_of(row), T, p.auto_groups, gf, gl);
+    auto_row_groups(P_row, tiles_of(row), sd, gf, gl);
     s0 = (int)O_row;
     s1 = (int)O_row + (gl - gf + 1);
 }
@@ -111,8 +113,10 @@ __global__ void __launch_bounds__(kHeadDim)
     }
     MergeSmem ms{s_w, s_w + kMergeChunk * 8, s_red};
     const XgSink unused{};
-    merge_slots<G, T, 4, false, false>(p.part_m, p.part_l, p.part_acc, s0, s1 - s0, p.Hq, qh0, ms,
-                                       o, st, unused);
+    // the row's slots of this KV head: one contiguous block of the workspace
+    const size_t sb = ((size_t)kvh * p.total_slots + s0) * G;
+    merge_slots<G, T, 4, false, false>(p.part_m + sb, p.part_l + sb, p.part_acc + sb * kHeadDim, 0,
+                                       s1 - s0, G, 0, ms, o, st, unused);
 }
 
 // Merges n_parts blocks of combined states [n_parts][B][Hq][130] into the

@@ -177,6 +177,37 @@ __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
+// One bulk copy (TMA, untiled, no multicast) of `bytes` contiguous bytes of
+// global memory into shared memory, completing as transaction bytes on `bar`.
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_copy_g2s(uint32_t smem_dst, const void* src, uint32_t bytes,
+                                              uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_dst), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Orders this thread's generic-proxy global accesses (and those it has
+// acquired) before its later async-proxy (bulk copy) accesses of global memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Atomic add at GPU scope with acquire-release semantics: the release half
+// publishes every write that happens-before it (those of the CTA's other
+// threads included, through a preceding barrier); the acquire half makes the
+// writes released by earlier adds visible.  The issuing thread only waits for
+// the result when it reads it.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int32_t* addr, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;"
+                 : "=r"(old)
+                 : "l"(addr), "r"(v)
+                 : "memory");
+    return old;
+}
+
 // ---------------------------------------------------------------- PDL
 __device__ __forceinline__ void griddep_wait() {
     asm volatile("griddepcontrol.wait;" ::: "memory");

@@ -40,9 +40,11 @@ struct DecodeParams {
     const int32_t* work_items;     // [T, 5] or null (rectangular grid)
     const int32_t* split_offsets;  // [B + 1] (work queue)
     int32_t* merge_counters;       // [B, Hkv] for the fused merge, or null
-    float* part_m;                 // [slots * Hq]
-    float* part_l;                 // [slots * Hq]
-    float* part_acc;               // [slots * Hq * 128]
+    // partial states, [Hkv][total_slots][G] (m, l) and [Hkv][total_slots][G][128]
+    // (acc): the slots of one (row, KV head) are one contiguous block
+    float* part_m;
+    float* part_l;
+    float* part_acc;
     const uint8_t* k_pages;        // pool bases (cp.async load path)
     const uint8_t* v_pages;
     unsigned* error;               // device error word
@@ -62,22 +64,49 @@ struct DecodeParams {
     int xg_world, xg_rank, xg_bcap;
 };
 
-// Phase stamps (diagnostic build, PKV_PHASE_STAMPS): %globaltimer values per
-// CTA, written by one thread each --
+// Phase stamps (diagnostic build, PKV_PHASE_STAMPS): per CTA, written by one
+// thread each -- %globaltimer values
 //   0 entry, 1 schedule resolved, 2 first page ids in hand,
 //   3 first K/V stage issued, 4 first stage arrived (consumer warp 0),
 //   5 last stage of the CTA's last item consumed (all consumer warps),
-//   6 start of the CTA's last fused merge (0 if it merges nothing), 7 exit.
-constexpr int kStampsPerCta = 8;
+//   6 start of the CTA's last fused merge (0 if it merges nothing), 7 exit;
+// and counts -- 8 SM id, 9 work items, 10 tokens streamed, 11 pieces of the
+// last fused merge; then SM clock cycles (clock64) since the CTA's entry --
+// producer lane 0: 12 past griddepcontrol.wait, 13 schedule, 14 first item,
+// 15 CTA barrier passed,
+// 16 first descriptor published, 17 first page ids in hand, 18 first stage
+// issued; consumer thread 0: 24 CTA barrier passed, 25 first descriptor
+// read, 26 first stage arrived, 27 first stage computed -- and cycles since
+// the start of the last end-of-CTA merge: 20 weights formed, 21 first bulk
+// copy landed, 22 sums formed, 23 stored; and raw clock64 values of producer
+// lane 0 past griddepcontrol.wait (28) and once the row lengths are summed,
+// the schedule's first metadata read (29).
+constexpr int kStampsPerCta = 32;
 #ifdef PKV_PHASE_STAMPS
 #define PKV_STAMP(p, k)                                                                   \
     do {                                                                                  \
         if ((p).stamps != nullptr)                                                        \
             (p).stamps[(size_t)blockIdx.x * kStampsPerCta + (k)] = global_timer_ns();     \
     } while (0)
+#define PKV_STAMP_VALUE(p, k, v)                                                          \
+    do {                                                                                  \
+        if ((p).stamps != nullptr)                                                        \
+            (p).stamps[(size_t)blockIdx.x * kStampsPerCta + (k)] = (unsigned long long)(v); \
+    } while (0)
+#define PKV_CLOCK_BASE(var) const long long var = clock64()
+#define PKV_CLOCK_STAMP(p, k, base) PKV_STAMP_VALUE(p, k, clock64() - (base))
 #else
 #define PKV_STAMP(p, k) \
     do {                \
+    } while (0)
+#define PKV_STAMP_VALUE(p, k, v) \
+    do {                         \
+    } while (0)
+#define PKV_CLOCK_BASE(var) \
+    do {                    \
+    } while (0)
+#define PKV_CLOCK_STAMP(p, k, base) \
+    do {                            \
     } while (0)
 #endif
 
@@ -495,22 +524,70 @@ __device__ __forceinline__ int auto_row_tiles(const DecodeParams& p, int b) {
     return (seq + kTileTokens - 1) / kTileTokens;
 }
 
-__device__ __forceinline__ long long auto_group_start(int g, long long T, int NG) {
-    return (long long)g * T / NG;
+// Division of 32-bit numerators by a divisor fixed for the launch, through a
+// precomputed reciprocal m = floor((2^32 - 1) / d): umulhi(a, m) is floor(a / d)
+// or one below it (a * m / 2^32 > a / d - 1 for every a < 2^32), and one
+// correction step makes it exact.  The schedule divides by the tile total T
+// and the group count NG several times per CTA on its critical path, where a
+// 64-bit division is a long dependent instruction sequence.
+struct FastDiv {
+    uint32_t d, m;
+    __device__ __forceinline__ void init(uint32_t divisor) {
+        d = divisor;
+        m = 0xffffffffu / divisor;
+    }
+    __device__ __forceinline__ uint32_t div(uint32_t a) const {
+        uint32_t q = __umulhi(a, m);
+        if (a - q * d >= d) ++q;
+        return q;
+    }
+};
+
+// The schedule's divisors: 32-bit arithmetic whenever T * NG < 2^32 (every
+// numerator below is at most T * NG), 64-bit otherwise.
+struct SchedDiv {
+    long long T;
+    int NG;
+    bool fast;
+    FastDiv byT, byNG;
+    __device__ __forceinline__ void init(long long total, int groups) {
+        T = total;
+        NG = groups;
+        fast = total > 0 && (unsigned long long)total * (unsigned)groups < (1ull << 32);
+        if (fast) {
+            byT.init((uint32_t)total);
+            byNG.init((uint32_t)groups);
+        }
+    }
+    // first tile of group g: floor(g * T / NG)
+    __device__ __forceinline__ long long group_start(int g) const {
+        if (fast) return byNG.div((uint32_t)g * (uint32_t)T);
+        return (long long)g * T / NG;
+    }
+    // group of tile x: floor(((x + 1) * NG - 1) / T)
+    __device__ __forceinline__ int group_of(long long x) const {
+        if (fast) return (int)byT.div((uint32_t)(x + 1) * (uint32_t)NG - 1u);
+        return (int)(((x + 1) * NG - 1) / T);
+    }
+};
+
+__device__ __forceinline__ long long auto_group_start(int g, const SchedDiv& sd) {
+    return sd.group_start(g);
 }
 
 // Groups holding the first and last tile of a row (tile prefix P, n tiles);
 // an empty row is placed in the group of its position in the stream.
-__device__ __forceinline__ void auto_row_groups(long long P, int n, long long T, int NG, int& gf,
+__device__ __forceinline__ void auto_row_groups(long long P, int n, const SchedDiv& sd, int& gf,
                                                 int& gl) {
+    const long long T = sd.T;
     if (T == 0) {
         gf = gl = 0;
         return;
     }
     const long long first = n > 0 ? P : (P < T ? P : T - 1);
     const long long last = n > 0 ? P + n - 1 : first;
-    gf = (int)(((first + 1) * NG - 1) / T);
-    gl = (int)(((last + 1) * NG - 1) / T);
+    gf = sd.group_of(first);
+    gl = sd.group_of(last);
 }
 
 __device__ __forceinline__ int warp_exclusive_scan(int v, int lane) {
@@ -532,6 +609,7 @@ __device__ __forceinline__ int warp_sum_int(int v) {
 struct AutoCursor {
     int g, kvh, NG;
     long long T;
+    SchedDiv sd;
     int b, b_end;      // next row to emit, one past the last row of the group
     long long P;       // tile prefix of row b
     int O;             // slot prefix of row b
@@ -549,6 +627,8 @@ __device__ __forceinline__ AutoCursor auto_init(const DecodeParams& p, int lane)
         T += warp_sum_int(b < p.B ? auto_row_tiles(p, b) : 0);
     }
     c.T = T;
+    if (lane == 0) PKV_STAMP_VALUE(p, 29, clock64());  // absolute; entry clock in slot 28
+    c.sd.init(T, c.NG);
     int b_lo = -1, b_hi = -1;
     long long P_lo = 0, P = 0;
     int O_lo = 0, O = 0;
@@ -558,7 +638,7 @@ __device__ __forceinline__ AutoCursor auto_init(const DecodeParams& p, int lane)
         const int n = valid ? auto_row_tiles(p, b) : 0;
         const long long pfx = P + warp_exclusive_scan(n, lane);
         int gf = 0, gl = -1;
-        if (valid) auto_row_groups(pfx, n, T, c.NG, gf, gl);
+        if (valid) auto_row_groups(pfx, n, c.sd, gf, gl);
         const int pieces = valid ? gl - gf + 1 : 0;
         const int ofx = O + warp_exclusive_scan(pieces, lane);
         const unsigned lo = __ballot_sync(0xffffffffu, valid && gl >= c.g);
@@ -595,11 +675,11 @@ __device__ __forceinline__ Item auto_item(const DecodeParams& p, AutoCursor& c, 
     const int seq = seq_raw < 0 ? 0 : ((long long)seq_raw > limit ? (int)limit : seq_raw);
     const int n = (seq + kTileTokens - 1) / kTileTokens;
     int gf, gl;
-    auto_row_groups(c.P, n, c.T, c.NG, gf, gl);
+    auto_row_groups(c.P, n, c.sd, gf, gl);
     long long tb = 0, te = 0;
     if (n > 0) {
-        const long long s0 = auto_group_start(c.g, c.T, c.NG);
-        const long long s1 = auto_group_start(c.g + 1, c.T, c.NG);
+        const long long s0 = auto_group_start(c.g, c.sd);
+        const long long s1 = auto_group_start(c.g + 1, c.sd);
         tb = (s0 > c.P ? s0 : c.P) - c.P;
         te = ((c.P + n) < s1 ? (c.P + n) : s1) - c.P;
     }
@@ -650,14 +730,40 @@ struct ItemDesc {
     int pad[6];
 };
 
+// A fused merge whose "last task" was decided during the CTA's work and that
+// runs after the CTA's last item.
+struct PendingMerge {
+    int row, kvh, s0, n, out_row, old;
+    int pad[2];
+};
+constexpr int kMaxPending = 8;
+// Merge weights of the end-of-CTA merge: n * G floats (+ per-head max / sum).
+constexpr int kMergeWeights = 1024;
+
+template <int G>
+__host__ __device__ constexpr int mw_floats() {
+    return (merge_scratch_floats<kConsumerWarps>() > kMergeWeights
+                ? merge_scratch_floats<kConsumerWarps>()
+                : kMergeWeights) + 16;
+}
+
+// Shared memory, in order: the K/V ring, the Q slots and the combine buffers
+// (one contiguous region, idle after the CTA's last item, that receives the
+// partial states of the end-of-CTA merges), then descriptors, barriers,
+// flags, statistics, merge weights and the pending-merge list.
+template <int G, int NSLOTS>
+__host__ __device__ constexpr size_t merge_region_bytes() {
+    return (size_t)NSLOTS * kSlotBytes + (size_t)kDescSlots * kQSlotBytes +
+           2 * DecodeSmem<G>::kMergeFloats * sizeof(float);
+}
+
 template <int G, int NSLOTS>
 constexpr size_t decode_smem_bytes() {
-    return 1024 /* alignment slack */ + (size_t)NSLOTS * kSlotBytes +
-           (size_t)kDescSlots * kQSlotBytes + kDescSlots * sizeof(ItemDesc) +
-           (2 * NSLOTS + 2 * kDescSlots) * sizeof(uint64_t) + 64 +
-           2 * 2 * kConsumerWarps * 8 * sizeof(float) +
-           2 * DecodeSmem<G>::kMergeFloats * sizeof(float) +
-           merge_scratch_floats<kConsumerWarps>() * sizeof(float);
+    return 1024 /* alignment slack */ + merge_region_bytes<G, NSLOTS>() +
+           kDescSlots * sizeof(ItemDesc) +
+           (2 * NSLOTS + 2 * kDescSlots + 2) * sizeof(uint64_t) + 64 +
+           2 * 2 * kConsumerWarps * 8 * sizeof(float) + mw_floats<G>() * sizeof(float) +
+           kMaxPending * sizeof(PendingMerge);
 }
 
 // Two decode CTAs share an SM (228 KB of shared memory, 1 KB reserved per CTA).
@@ -786,6 +892,178 @@ __device__ __forceinline__ void xg_collect(const DecodeParams& p, int row, int k
     consumer_bar_sync();  // the own-state buffer is reused by the next row
 }
 
+// ------------------------------------------------------------ end-of-CTA merge
+// Log-sum-exp merge of slots [s0, s0 + n) of (row, kvh), run by the consumer
+// warps after the CTA's last item, when the K/V ring, the Q slots and the
+// combine buffers -- one contiguous shared-memory region of `region_bytes` --
+// are idle.  The slots' acc rows are one contiguous block of the workspace
+// ([n][G][128] fp32); bulk copies (cp.async.bulk, untiled, no multicast)
+// move it into the region in rounds of as many slots as fit, while one warp
+// per head reads the slots' m / l and forms the weights e^(m - M) and the sum
+// L.  Each thread then owns float4 columns of the G x 128 result and sums its
+// weighted columns from shared memory.  Returns after a consumer barrier, with
+// every thread's region accesses ordered before later bulk copies.
+template <int G, typename T>
+__device__ __forceinline__ void merge_bulk(const DecodeParams& p, const PendingMerge& e,
+                                           uint8_t* region, uint32_t region_bytes, float* s_w,
+                                           uint64_t* bar, uint32_t& phase,
+                                           volatile int* s_flags) {
+    constexpr int NT = kConsumerWarps * 32;
+    constexpr uint32_t kSlotBytesG = G * kHeadDim * sizeof(float);
+    constexpr int kCols = G * 32;                          // float4 columns of the result
+    constexpr int kColThreads = kCols < NT ? kCols : NT;   // threads per slot subset
+    constexpr int kSubsets = NT / kColThreads;             // slot subsets (G < 4)
+    constexpr int kColsPerThread = kCols / kColThreads;    // 2 for G = 8
+    const int t = threadIdx.x;
+    const int warp = t >> 5;
+    const int lane = t & 31;
+    const size_t base = ((size_t)e.kvh * p.total_slots + e.s0) * G;
+    const float* pm = p.part_m + base;
+    const float* pl = p.part_l + base;
+    const float* pa = p.part_acc + base * kHeadDim;
+    const int per_round = (int)(region_bytes / kSlotBytesG);
+    const int rounds = (e.n + per_round - 1) / per_round;
+    const uint32_t region_u32 = smem_u32(region);
+    float* s_hl = s_w + kMergeWeights;  // [0, 8): per-head max M, [8, 16): sum L
+    PKV_CLOCK_BASE(t_merge);
+    auto issue = [&](int r) {
+        const int cn = min(per_round, e.n - r * per_round);
+        mbar_arrive_expect_tx(bar, (uint32_t)cn * kSlotBytesG);
+        bulk_copy_g2s(region_u32, pa + (size_t)r * per_round * G * kHeadDim,
+                      (uint32_t)cn * kSlotBytesG, bar);
+    };
+    if (t == 0) {
+        fence_proxy_async_global();  // the acquired partial states, for the bulk copies
+        issue(0);
+    }
+    // weights, overlapping the first copy: warp w takes heads w, w + 4.  One
+    // pass over global memory keeps a running (max, sum) per lane and parks
+    // the raw m values in s_w; the warp then combines its lanes' pairs and
+    // turns s_w into the weights e^(m - M).
+#pragma unroll 1
+    for (int g = warp; g < G; g += kConsumerWarps) {
+        float mx = kNegFltMax, ls = 0.f;
+#pragma unroll 2
+        for (int sl = lane; sl < e.n; sl += 32) {
+            const float mv = __ldcg(pm + sl * G + g);
+            const float lv = __ldcg(pl + sl * G + g);
+            s_w[sl * G + g] = mv;
+            const float mn = fmaxf(mx, mv);
+            ls = ls * fast_exp2((mx - mn) * kLog2e) + lv * fast_exp2((mv - mn) * kLog2e);
+            mx = mn;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float mo = __shfl_xor_sync(0xffffffffu, mx, off);
+            const float lo = __shfl_xor_sync(0xffffffffu, ls, off);
+            const float mn = fmaxf(mx, mo);
+            ls = ls * fast_exp2((mx - mn) * kLog2e) + lo * fast_exp2((mo - mn) * kLog2e);
+            mx = mn;
+        }
+        for (int sl = lane; sl < e.n; sl += 32)
+            s_w[sl * G + g] = fast_exp2((s_w[sl * G + g] - mx) * kLog2e);
+        if (lane == 0) {
+            s_hl[g] = mx;
+            s_hl[8 + g] = ls;
+        }
+    }
+    if (t == 0) PKV_CLOCK_STAMP(p, 20, t_merge);
+    const int sub = t / kColThreads;
+    const int c0 = t % kColThreads;
+    float4 acc[kColsPerThread];
+#pragma unroll
+    for (int c = 0; c < kColsPerThread; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    // Every consumer thread passes the same barriers whatever happens: a warp
+    // whose wait gives up only skips its arithmetic and its stores.
+    bool ok = true;
+#pragma unroll 1
+    for (int r = 0; r < rounds; ++r) {
+        if (r > 0) {
+            fence_proxy_async_smem();  // this round's reads before the next copy's writes
+            consumer_bar_sync();
+            if (t == 0) issue(r);
+        } else {
+            consumer_bar_sync();       // weights visible
+        }
+        if (ok) {
+            ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar, phase, s_flags));
+            if (!ok && lane == 0) {
+                s_flags[0] = 1;
+                raise_error(p.error, kErrTimeout);
+            }
+        }
+        phase ^= 1u;
+        if (r == 0 && t == 0) PKV_CLOCK_STAMP(p, 21, t_merge);
+        if (!ok) continue;
+        const int first = r * per_round;
+        const int cn = min(per_round, e.n - first);
+#pragma unroll 4
+        for (int sl = sub; sl < cn; sl += kSubsets) {
+            const float4* rowp = reinterpret_cast<const float4*>(region + (size_t)sl * kSlotBytesG);
+#pragma unroll
+            for (int c = 0; c < kColsPerThread; ++c) {
+                const int col = c0 + c * kColThreads;
+                const float w = s_w[(first + sl) * G + col / 32];
+                const float4 v = rowp[col];
+                acc[c].x = fmaf(w, v.x, acc[c].x);
+                acc[c].y = fmaf(w, v.y, acc[c].y);
+                acc[c].z = fmaf(w, v.z, acc[c].z);
+                acc[c].w = fmaf(w, v.w, acc[c].w);
+            }
+        }
+    }
+    if (kSubsets > 1) {
+        // G < 4: fold the slot subsets through the region (its copies have landed)
+        consumer_bar_sync();
+        float4* red = reinterpret_cast<float4*>(region);
+        if (ok && sub > 0) red[(sub - 1) * kColThreads + c0] = acc[0];
+        consumer_bar_sync();
+        if (ok && sub == 0) {
+#pragma unroll
+            for (int j = 1; j < kSubsets; ++j) {
+                const float4 v = red[(j - 1) * kColThreads + c0];
+                acc[0].x += v.x;
+                acc[0].y += v.y;
+                acc[0].z += v.z;
+                acc[0].w += v.w;
+            }
+        }
+    }
+    if (t == 0) PKV_CLOCK_STAMP(p, 22, t_merge);
+    if (ok && sub == 0) {
+#pragma unroll
+        for (int c = 0; c < kColsPerThread; ++c) {
+            const int col = c0 + c * kColThreads;
+            const int g = col / 32;
+            const int d = 4 * (col % 32);
+            const float M = s_hl[g];
+            const float L = s_hl[8 + g];
+            if (p.state_out != nullptr) {
+                float* st = p.state_out + ((size_t)e.row * p.Hq + (size_t)e.kvh * G + g) * kStateStride;
+                st[2 + d] = acc[c].x;
+                st[3 + d] = acc[c].y;
+                st[4 + d] = acc[c].z;
+                st[5 + d] = acc[c].w;
+                if (d == 0) {
+                    st[0] = M;
+                    st[1] = L;
+                }
+            } else if (e.out_row >= 0) {
+                const float inv = L > 0.f ? 1.f / L : 0.f;
+                T* o = reinterpret_cast<T*>(p.out) +
+                       ((size_t)e.out_row * p.Hq + (size_t)e.kvh * G + g) * kHeadDim + d;
+                o[0] = ElemOps<T>::from_float(acc[c].x * inv);
+                o[1] = ElemOps<T>::from_float(acc[c].y * inv);
+                o[2] = ElemOps<T>::from_float(acc[c].z * inv);
+                o[3] = ElemOps<T>::from_float(acc[c].w * inv);
+            }
+        }
+    }
+    if (t == 0) PKV_CLOCK_STAMP(p, 23, t_merge);
+    fence_proxy_async_smem();
+    consumer_bar_sync();
+}
+
 // 16 e4m3 values (elements [16c, 16c + 16) of token t, chunk q = 8t + c of a
 // row-major e4m3 stage) to fp16, stored as two 16-byte chunks of the stage's
 // swizzled 16-bit layout (lo / hi half of 64 elements, 128-byte rows).
@@ -832,18 +1110,21 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     uint8_t* smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
     uint8_t* ring = smem;
     uint8_t* s_q = ring + (size_t)NSLOTS * kSlotBytes;                    // [kDescSlots][8][128]
-    ItemDesc* s_desc = reinterpret_cast<ItemDesc*>(s_q + kDescSlots * kQSlotBytes);
+    float* s_merge = reinterpret_cast<float*>(s_q + kDescSlots * kQSlotBytes);
+    ItemDesc* s_desc = reinterpret_cast<ItemDesc*>(ring + merge_region_bytes<G, NSLOTS>());
     uint64_t* full_bar = reinterpret_cast<uint64_t*>(s_desc + kDescSlots);
     uint64_t* empty_bar = full_bar + NSLOTS;
     uint64_t* desc_full = empty_bar + NSLOTS;
     uint64_t* desc_empty = desc_full + kDescSlots;
-    uint8_t* s_flag_bytes = reinterpret_cast<uint8_t*>(desc_empty + kDescSlots);
+    uint64_t* merge_bar = desc_empty + kDescSlots;
+    uint8_t* s_flag_bytes = reinterpret_cast<uint8_t*>(merge_bar + 2);
     // [0] abort, [1] last task of a row, [2] a peer exchange gave up
     volatile int* s_flags = reinterpret_cast<volatile int*>(s_flag_bytes);
     float* s_mstat = reinterpret_cast<float*>(s_flag_bytes + 64);
     float* s_lstat = s_mstat + 2 * kConsumerWarps * 8;
-    float* s_merge = s_lstat + 2 * kConsumerWarps * 8;
-    float* s_mw = s_merge + 2 * DecodeSmem<G>::kMergeFloats;  // merge weights + stats
+    float* s_mw = s_lstat + 2 * kConsumerWarps * 8;  // merge weights + stats
+    PendingMerge* s_pend = reinterpret_cast<PendingMerge*>(s_mw + mw_floats<G>());
+    static_assert(merge_region_bytes<G, NSLOTS>() % 16 == 0, "bulk-copy destination alignment");
     // [G][130] sharded own state lives in the half of the combine double
     // buffer that the item's own combine loop does not read: half 1 after a
     // merge (whose shared sums use half 0), else the half opposite `buf`.
@@ -853,8 +1134,13 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     const int lane = threadIdx.x & 31;
     // Launched behind a stage-in kernel (programmatic dependent launch), the
     // CTA starts early and waits here for its metadata; otherwise a no-op.
+    PKV_CLOCK_BASE(t_entry);
     griddep_wait();
     if (threadIdx.x == 0) PKV_STAMP(p, 0);
+    if (threadIdx.x == kConsumerWarps * 32) {
+        PKV_CLOCK_STAMP(p, 12, t_entry);
+        PKV_STAMP_VALUE(p, 28, clock64());
+    }
     // The producer resolves its schedule and its first item before the
     // CTA-wide barrier, so those reads overlap the barrier setup.
     AutoCursor acur;
@@ -872,9 +1158,15 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                        ? (p.num_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
                        : 0;
         }
-        if (lane == 0) PKV_STAMP(p, 1);
+        if (lane == 0) {
+            PKV_STAMP(p, 1);
+            PKV_CLOCK_STAMP(p, 13, t_entry);
+        }
         if (mine > 0) first_item = producer_next<BOX_ROWS>(p, 0, lane, first_pid0, acur);
-        if (lane == 0) s_my_items = mine;
+        if (lane == 0) {
+            s_my_items = mine;
+            PKV_CLOCK_STAMP(p, 14, t_entry);
+        }
     }
 
     if (threadIdx.x == 0) {
@@ -886,6 +1178,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
             mbar_init(&desc_full[s], 33);  // 32 lanes' Q copies + the descriptor store
             mbar_init(&desc_empty[s], kConsumerWarps);
         }
+        mbar_init(merge_bar, 1);  // end-of-CTA merge: thread 0's expect_tx + bulk bytes
         s_flags[0] = 0;
         s_flags[1] = 0;
         s_flags[2] = 0;
@@ -893,6 +1186,8 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     }
     __syncthreads();
     const int my_items = s_my_items;
+    if (threadIdx.x == kConsumerWarps * 32) PKV_CLOCK_STAMP(p, 15, t_entry);
+    if (threadIdx.x == 0) PKV_CLOCK_STAMP(p, 24, t_entry);
 
     if (warp == kConsumerWarps) {
         // ============================ producer warp ============================
@@ -955,6 +1250,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                     d.out_row = cur.out_row;
                     d.noop = cur.noop ? 1 : 0;
                     mbar_arrive(&desc_full[e]);
+                    if (s == 0) PKV_CLOCK_STAMP(p, 16, t_entry);
                 }
             }
 
@@ -988,7 +1284,10 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                         y = (pid * p.Hkv + it.kvh) * p.page_size + (tok % p.page_size);
                     }
                 }
-                if (s == 0 && base == 0 && lane == 0) PKV_STAMP(p, 2);
+                if (s == 0 && base == 0 && lane == 0) {
+                    PKV_STAMP(p, 2);
+                    PKV_CLOCK_STAMP(p, 17, t_entry);
+                }
                 const int stages_here = min(kStagesPerBatch, n_stages - base / kBoxesPerStage);
                 for (int st = 0; st < stages_here; ++st) {
                     const uint32_t slot = gstage % NSLOTS;
@@ -1051,7 +1350,10 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                                 cp_async_16(dst + kStageTokens * kHeadDim, p.v_pages + off, nbytes, policy);
                             }
                             cp_async_mbar_arrive_noinc(&full_bar[slot]);
-                            if (gstage == 0 && lane == 0) PKV_STAMP(p, 3);
+                            if (gstage == 0 && lane == 0) {
+                                PKV_STAMP(p, 3);
+                                PKV_CLOCK_STAMP(p, 18, t_entry);
+                            }
                             ++gstage;
                             continue;
                         }
@@ -1070,7 +1372,10 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                         }
                         cp_async_mbar_arrive_noinc(&full_bar[slot]);
                     }
-                    if (gstage == 0 && lane == 0) PKV_STAMP(p, 3);
+                    if (gstage == 0 && lane == 0) {
+                        PKV_STAMP(p, 3);
+                        PKV_CLOCK_STAMP(p, 18, t_entry);
+                    }
                     ++gstage;
                 }
                 if (!fetched) {
@@ -1114,6 +1419,10 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     const unsigned xg_epoch = p.xg_world > 0 ? ld_relaxed_gpu_u32(p.xg_counters) : 0u;
     const bool state_mode = p.state_out != nullptr;
     const bool xg_mode = p.xg_world > 0;
+    long long stamp_tokens = 0;  // diagnostic build: tokens this CTA streamed
+    int n_pend = 0;              // deferred merges (uniform across consumer threads)
+    int pend_old = 0;            // thread 0: result of the latest deferred counter add
+    uint32_t merge_phase = 0u;
 
     for (int s = 0; s < my_items; ++s) {
         if (s == my_items - 1) griddep_launch_dependents();
@@ -1160,6 +1469,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&desc_empty[e]);
+            if (s == 0 && threadIdx.x == 0) PKV_CLOCK_STAMP(p, 25, t_entry);
         } else {
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) qf[ks][0] = qf[ks][1] = 0u;
@@ -1188,7 +1498,10 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                 }
             }
             if (aborted) break;
-            if (gs == 0 && threadIdx.x == 0) PKV_STAMP(p, 4);
+            if (gs == 0 && threadIdx.x == 0) {
+                PKV_STAMP(p, 4);
+                PKV_CLOCK_STAMP(p, 26, t_entry);
+            }
 
             const int t0 = it.tok_begin + j * kStageTokens;
             const int valid = min(kStageTokens, it.tok_end - t0);
@@ -1302,8 +1615,10 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty_bar[slot]);
+            if (gs == 0 && threadIdx.x == 0) PKV_CLOCK_STAMP(p, 27, t_entry);
         }
         gbase += (uint32_t)n_stages;
+        stamp_tokens += it.tok_end - it.tok_begin;
 
         // ---- combine the four warps' states of this item
 #pragma unroll
@@ -1381,7 +1696,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                     orow[d] = Ops::from_float(osum * (lsum > 0.f ? 1.f / lsum : 0.f));
                 }
             } else if (it.slot >= 0) {
-                const size_t si = (size_t)it.slot * p.Hq + (size_t)it.kvh * G + g;
+                const size_t si = ((size_t)it.kvh * p.total_slots + it.slot) * G + g;
                 p.part_acc[si * kHeadDim + d] = osum;
                 if (d == 0) {
                     p.part_m[si] = mnat;
@@ -1390,24 +1705,48 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
             }
         }
         if (xg_direct) xg_collect<G, T>(p, it.row, it.kvh, it.out_row, xs, s_flags);
-        if (!direct && it.slot >= 0) {
-            if (p.merge_counters != nullptr && !rect) {
-                // fused merge: the last task of this (row, kvh) merges all of
-                // the row's slots (reference cuh:648-716).
-                __threadfence();
+        if (!direct && it.slot >= 0 && p.merge_counters != nullptr && !rect) {
+            // fused merge: the last task of this (row, kvh) merges all of the
+            // row's slots (reference cuh:648-716)
+            int32_t* ctr = p.merge_counters + (size_t)it.row * p.Hkv + it.kvh;
+            if (!xg_mode && n_pend < kMaxPending) {
+                // Deferred to the CTA's end.  Thread 0's add releases the
+                // partial state every thread wrote before the barrier; its
+                // result is only read after the CTA's last item, so no thread
+                // waits for the round trip here.
                 consumer_bar_sync();
                 if (threadIdx.x == 0) {
-                    int32_t* ctr = p.merge_counters + (size_t)it.row * p.Hkv + it.kvh;
-                    const int old = atomicAdd(ctr, 1);
+                    if (n_pend > 0) s_pend[n_pend - 1].old = pend_old;
+                    PendingMerge& pe = s_pend[n_pend];
+                    pe.row = it.row;
+                    pe.kvh = it.kvh;
+                    pe.s0 = it.slot - it.split;
+                    pe.n = it.row_splits;
+                    pe.out_row = it.out_row;
+                    pend_old = atom_add_acq_rel_gpu(ctr, 1);
+                }
+                ++n_pend;
+            } else {
+                // immediate: the sharded exchange (its peers wait for the
+                // row), or the pending list is full
+                consumer_bar_sync();
+                if (threadIdx.x == 0) {
+                    const int old = atom_add_acq_rel_gpu(ctr, 1);
                     const int last = old == it.row_splits - 1;
                     if (last) *ctr = 0;
                     s_flags[1] = last;
                 }
                 consumer_bar_sync();
                 if (s_flags[1]) {
-                    __threadfence();
-                    if (threadIdx.x == 0) PKV_STAMP(p, 6);
+                    if (threadIdx.x == 0) {
+                        PKV_STAMP(p, 6);
+                        PKV_STAMP_VALUE(p, 11, it.row_splits);
+                    }
                     MergeSmem ms{s_mw, s_mw + kMergeChunk * 8, s_merge};
+                    const size_t sb = ((size_t)it.kvh * p.total_slots + (it.slot - it.split)) * G;
+                    const float* pm = p.part_m + sb;
+                    const float* pl = p.part_l + sb;
+                    const float* pa = p.part_acc + sb * kHeadDim;
                     const int qh0 = it.kvh * G;
                     T* o = nullptr;
                     float* st = nullptr;
@@ -1421,19 +1760,56 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                     }
                     if (xg_merge) {
                         merge_slots<G, T, kConsumerWarps, true, true>(
-                            p.part_m, p.part_l, p.part_acc, it.slot - it.split, it.row_splits,
-                            p.Hq, qh0, ms, nullptr, nullptr, xs);
+                            pm, pl, pa, 0, it.row_splits, G, 0, ms, nullptr, nullptr, xs);
                         xg_collect<G, T>(p, it.row, it.kvh, it.out_row, xs, s_flags);
                     } else {
                         merge_slots<G, T, kConsumerWarps, true, false>(
-                            p.part_m, p.part_l, p.part_acc, it.slot - it.split, it.row_splits,
-                            p.Hq, qh0, ms, o, st, xs);
+                            pm, pl, pa, 0, it.row_splits, G, 0, ms, o, st, xs);
                     }
                     consumer_bar_sync();  // merge scratch aliases the combine buffers
                 }
             }
         }
         buf ^= 1;
+    }
+    if (n_pend > 0) {
+        // the deferred merges whose "last task" this CTA was, now that the
+        // ring, the Q slots and the combine buffers are idle
+        if (threadIdx.x == 0) s_pend[n_pend - 1].old = pend_old;
+        fence_proxy_async_smem();
+        consumer_bar_sync();
+#pragma unroll 1
+        for (int k = 0; k < n_pend; ++k) {
+            const PendingMerge pe = s_pend[k];
+            if (pe.old != pe.n - 1) continue;
+            if (threadIdx.x == 0) {
+                p.merge_counters[(size_t)pe.row * p.Hkv + pe.kvh] = 0;
+                PKV_STAMP(p, 6);
+                PKV_STAMP_VALUE(p, 11, pe.n);
+            }
+            if (aborted || s_flags[0] != 0) continue;
+            if (pe.n * G <= kMergeWeights) {
+                merge_bulk<G, T>(p, pe, ring, (uint32_t)merge_region_bytes<G, NSLOTS>(), s_mw,
+                                 merge_bar, merge_phase, s_flags);
+            } else {
+                // more slots than the weight buffer holds: the chunked merge
+                MergeSmem ms{s_mw, s_mw + kMergeChunk * 8, s_merge};
+                const size_t sb = ((size_t)pe.kvh * p.total_slots + pe.s0) * G;
+                const int qh0 = pe.kvh * G;
+                T* o = (!state_mode && pe.out_row >= 0)
+                           ? reinterpret_cast<T*>(p.out) + ((size_t)pe.out_row * p.Hq + qh0) * kHeadDim
+                           : nullptr;
+                float* st = state_mode
+                                ? p.state_out + ((size_t)pe.row * p.Hq + qh0) * kStateStride
+                                : nullptr;
+                const XgSink unused{};
+                merge_slots<G, T, kConsumerWarps, true, false>(
+                    p.part_m + sb, p.part_l + sb, p.part_acc + sb * kHeadDim, 0, pe.n, G, 0, ms, o,
+                    st, unused);
+                fence_proxy_async_smem();
+                consumer_bar_sync();
+            }
+        }
     }
     if (p.xg_world > 0) {
         // the last CTA to finish advances the step number for the next launch
@@ -1448,7 +1824,14 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
             }
         }
     }
-    if (threadIdx.x == 0) PKV_STAMP(p, 7);
+    if (threadIdx.x == 0) {
+        PKV_STAMP(p, 7);
+        unsigned smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        PKV_STAMP_VALUE(p, 8, smid);
+        PKV_STAMP_VALUE(p, 9, my_items);
+        PKV_STAMP_VALUE(p, 10, stamp_tokens);
+    }
 }
 
 }  // namespace pkv
