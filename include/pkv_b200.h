@@ -316,6 +316,46 @@ pkv_status pkv_engine_destroy(pkv_engine* engine);
  * NG = 2 * sm_count / Hkv; sm_count <= 0 queries the current device. */
 size_t pkv_auto_workspace_bytes(int B, int Hq, int Hkv, int sm_count);
 
+/* NG, the number of groups of the device-side schedule (2 * sm_count / Hkv,
+ * at least 1); sm_count <= 0 queries the current device. */
+int pkv_auto_groups(int Hkv, int sm_count);
+
+/* ---- Host-planned device schedule ----
+ * The schedule pkv_paged_attention_auto derives on the device from seq_lens,
+ * computed on the host instead by pkv_build_auto_plan (same integer
+ * arithmetic): a 64-byte header, then per group of the NG groups an 80-byte
+ * entry with its first row piece, that row's q / output rows and the
+ * physical pages of the piece's first boxes.  Given a device copy of it,
+ * pkv_paged_attention_auto_planned starts its first K/V copies after one read
+ * of the entry, where the unplanned launch first reads seq_lens, derives the
+ * schedule and then reads the block table.  Upload the plan with the step's
+ * other metadata; it must describe exactly the seq_lens, block_table,
+ * q_indices and out_indices of the launch (a plan of another step gives
+ * wrong rows, never a fault: every value taken from it is range-checked, and
+ * a plan of another shape is detected and ignored with PKV_DEVERR_WORK_ITEM).
+ * No counterpart in the reference. */
+size_t pkv_auto_plan_bytes(int Hkv, int sm_count);
+
+/* seq_lens / block_table (row stride row_stride) / q_indices / out_indices
+ * (either may be NULL = identity) are HOST copies of the step's metadata;
+ * max_pages and page_size are those of the launch.  Writes plan (host,
+ * plan_bytes >= pkv_auto_plan_bytes). */
+pkv_status pkv_build_auto_plan(const int32_t* seq_lens, const int32_t* block_table, int B,
+                               int row_stride, const int32_t* q_indices,
+                               const int32_t* out_indices, int max_pages, int page_size,
+                               int Hkv, int sm_count, int32_t* plan, size_t plan_bytes);
+
+/* pkv_paged_attention_auto with a device copy of the step's plan (16-byte
+ * aligned, plan_bytes >= pkv_auto_plan_bytes(Hkv, 0)). */
+pkv_status pkv_paged_attention_auto_planned(
+    const void* q_source, const void* k_pages, const void* v_pages,
+    const int32_t* block_table, const int32_t* seq_lens,
+    const int32_t* q_indices, const int32_t* out_indices, void* output,
+    void* workspace, size_t workspace_bytes, int32_t* merge_counters, const void* plan,
+    size_t plan_bytes, int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim,
+    int physical_pages, int page_size, int max_pages,
+    pkv_dtype dtype, void* stream);
+
 /* Capacity of the scratch array used by
  * pkv_paged_attention_workqueue_noalloc (bytes of fp32 partial states). */
 #define PKV_NOALLOC_SCRATCH_BYTES (8u << 20)

@@ -117,6 +117,16 @@ SIGNATURES = {
          c_int, c_int, c_int, c_int, c_int, _P],
     ),
     "pkv_auto_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "pkv_auto_groups": (c_int, [c_int, c_int]),
+    "pkv_auto_plan_bytes": (c_size_t, [c_int, c_int]),
+    "pkv_build_auto_plan": (
+        c_int, [_I32P, _I32P, c_int, c_int, _I32P, _I32P, c_int, c_int, c_int, c_int, _I32P,
+                c_size_t]),
+    "pkv_paged_attention_auto_planned": (
+        c_int,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, _P, c_size_t, c_int, c_int, c_int,
+         c_int, c_int, c_int, c_int, c_int, c_int, c_int, _P],
+    ),
     "pkv_paged_attention_auto_state": (
         c_int,
         [_P, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, c_int, c_int, c_int, c_int, c_int,

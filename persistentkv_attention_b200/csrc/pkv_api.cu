@@ -685,6 +685,16 @@ pkv_status pkv_paged_attention_workqueue(
                             stream);
 }
 
+int pkv_auto_groups(int Hkv, int sm_count) {
+    if (Hkv <= 0) return 0;
+    if (sm_count <= 0) {
+        DeviceState* ds = nullptr;
+        if (current_device(&ds) != PKV_OK) return 0;
+        sm_count = ds->sm_count;
+    }
+    return auto_groups_for(sm_count, Hkv);
+}
+
 size_t pkv_auto_workspace_bytes(int B, int Hq, int Hkv, int sm_count) {
     if (B <= 0 || Hq <= 0 || Hkv <= 0) return 0;
     if (sm_count <= 0) {
@@ -736,7 +746,7 @@ pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* 
                        void* workspace, size_t workspace_bytes, int32_t* merge_counters,
                        int q_rows, int out_rows, void* stream,
                        const pkv_exchange* xg = nullptr, bool pdl = false,
-                       const float* kv8_scales = nullptr);
+                       const float* kv8_scales = nullptr, const void* plan = nullptr);
 
 }  // namespace
 
@@ -770,6 +780,27 @@ pkv_status pkv_paged_attention_auto_state(
                        workspace_bytes, merge_counters, q_rows, B, stream);
 }
 
+pkv_status pkv_paged_attention_auto_planned(
+    const void* q_source, const void* k_pages, const void* v_pages, const int32_t* block_table,
+    const int32_t* seq_lens, const int32_t* q_indices, const int32_t* out_indices, void* output,
+    void* workspace, size_t workspace_bytes, int32_t* merge_counters, const void* plan,
+    size_t plan_bytes, int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim,
+    int physical_pages, int page_size, int max_pages, pkv_dtype dtype, void* stream) {
+    Common c{q_source, k_pages, v_pages, block_table, B, Hq, Hkv, head_dim,
+             physical_pages, page_size, max_pages, dtype};
+    if (output == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "output must be a CUDA tensor");
+    if (plan == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "plan must be a device pointer");
+    // the kernel reads the header and its group's entry before it checks them
+    const size_t need = pkv_auto_plan_bytes(Hkv, 0);
+    if (need == 0 || plan_bytes < need) {
+        return fail(PKV_ERR_INVALID_ARGUMENT, "plan holds %zu bytes but %zu are needed",
+                    plan_bytes, need);
+    }
+    return auto_common(c, seq_lens, q_indices, out_indices, output, nullptr, workspace,
+                       workspace_bytes, merge_counters, q_rows, out_rows, stream, nullptr, false,
+                       nullptr, plan);
+}
+
 }  // extern "C"
 
 namespace {
@@ -778,7 +809,7 @@ pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* 
                        const int32_t* out_indices, void* output, float* state_out,
                        void* workspace, size_t workspace_bytes, int32_t* merge_counters,
                        int q_rows, int out_rows, void* stream, const pkv_exchange* xg,
-                       bool pdl, const float* kv8_scales) {
+                       bool pdl, const float* kv8_scales, const void* plan) {
     const int B = c.B, Hq = c.Hq, Hkv = c.Hkv;
     const int max_pages = c.max_pages, page_size = c.page_size;
     pkv_status st = check_common(c);
@@ -820,6 +851,11 @@ pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* 
     partition_workspace(ls.dp, workspace, slots);
     ls.merge = merge_counters == nullptr;
     if (xg != nullptr) xg_fill(ls.dp, *xg);
+    if (plan != nullptr) {
+        if (reinterpret_cast<uintptr_t>(plan) & 15u)
+            return fail(PKV_ERR_MISALIGNED, "plan must be 16-byte aligned");
+        ls.dp.plan = static_cast<const int32_t*>(plan);
+    }
     ls.pdl = pdl;
     if (kv8_scales != nullptr) {
         ls.kv8 = true;
@@ -962,11 +998,12 @@ pkv_status auto_after_stage(const void* q_source, const void* k_pages, const voi
                             void* workspace, size_t workspace_bytes, int32_t* merge_counters,
                             int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim,
                             int physical_pages, int page_size, int max_pages, pkv_dtype dtype,
-                            void* stream) {
+                            void* stream, const void* plan) {
     Common c{q_source, k_pages, v_pages, block_table, B, Hq, Hkv, head_dim,
              physical_pages, page_size, max_pages, dtype};
     return auto_common(c, seq_lens, nullptr, nullptr, output, nullptr, workspace,
-                       workspace_bytes, merge_counters, q_rows, out_rows, stream, nullptr, true);
+                       workspace_bytes, merge_counters, q_rows, out_rows, stream, nullptr, true,
+                       nullptr, plan);
 }
 
 }  // namespace pkv_internal

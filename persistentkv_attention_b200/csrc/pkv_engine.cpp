@@ -36,7 +36,7 @@ pkv_status auto_after_stage(const void* q_source, const void* k_pages, const voi
                             void* workspace, size_t workspace_bytes, int32_t* merge_counters,
                             int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim,
                             int physical_pages, int page_size, int max_pages, pkv_dtype dtype,
-                            void* stream);
+                            void* stream, const void* plan);
 }  // namespace pkv_internal
 
 namespace {
@@ -80,10 +80,12 @@ struct pkv_engine {
     void* d_ws;
     size_t ws_bytes;
     int32_t* d_counters;
-    // pinned staging [seq_lens (max_batch, 16-byte padded) | block table
-    // max_batch rows of max_pages] int32, read by the stage-in kernel; the same
-    // layout on the device, so a captured step serves every row width
+    // pinned staging [seq_lens (max_batch, 16-byte padded) | host plan of the
+    // device schedule (16-byte padded) | block table max_batch rows of
+    // max_pages] int32, read by the stage-in kernel; the same layout on the
+    // device, so a captured step serves every row width
     size_t sl_words;
+    size_t plan_words;
     int32_t* h_meta[kStaging];
     int32_t* dh_meta[kStaging];    // the same buffers as the device addresses them
     cudaEvent_t staged[kStaging];  // the launch that read staging buffer i has finished
@@ -122,8 +124,9 @@ pkv_status pkv_engine_create(const void* k_pages, const void* v_pages, int physi
     e->elem = 2;
     cudaGetDevice(&e->device);
     e->sl_words = align_up((size_t)max_batch, 4);
-    const size_t meta_bytes =
-        align_up((e->sl_words + (size_t)max_batch * max_pages) * sizeof(int32_t), 16);
+    e->plan_words = align_up(pkv_auto_plan_bytes(Hkv, 0) / sizeof(int32_t), 4);
+    const size_t meta_bytes = align_up(
+        (e->sl_words + e->plan_words + (size_t)max_batch * max_pages) * sizeof(int32_t), 16);
     const size_t q_bytes = (size_t)max_batch * Hq * kHeadDim * e->elem;
     e->ws_bytes = pkv_auto_workspace_bytes(max_batch, Hq, Hkv, 0);
     const size_t ctr_bytes = (size_t)max_batch * Hkv * sizeof(int32_t);
@@ -208,11 +211,17 @@ pkv_status pkv_engine_step_host(pkv_engine* e, const int32_t* seq_lens,
     }
     int32_t* h = e->h_meta[i];
     std::memcpy(h, seq_lens, (size_t)B * sizeof(int32_t));
-    int32_t* rows = h + e->sl_words;
+    // the schedule, planned here from the host rows (the device starts from it)
+    pkv_status pst = pkv_build_auto_plan(seq_lens, block_table, B, row_pages, nullptr, nullptr,
+                                         e->max_pages, e->page_size, e->hkv, 0,
+                                         h + e->sl_words, e->plan_words * sizeof(int32_t));
+    if (pst != PKV_OK) return efail(pst, "planning the step failed");
+    int32_t* rows = h + e->sl_words + e->plan_words;
     for (int r = 0; r < B; ++r)
         std::memcpy(rows + (size_t)r * e->max_pages, block_table + (size_t)r * row_pages,
                     (size_t)row_pages * sizeof(int32_t));
-    const size_t meta_bytes = (e->sl_words + (size_t)B * e->max_pages) * sizeof(int32_t);
+    const size_t meta_bytes =
+        (e->sl_words + e->plan_words + (size_t)B * e->max_pages) * sizeof(int32_t);
     const size_t q_bytes = (size_t)B * e->hq * kHeadDim * e->elem;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
 
@@ -223,9 +232,10 @@ pkv_status pkv_engine_step_host(pkv_engine* e, const int32_t* seq_lens,
         if (st != PKV_OK) return st;
         // nothing between the two launches: the decode starts behind the stage-in
         return pkv_internal::auto_after_stage(
-            e->d_q, e->k_pages, e->v_pages, e->d_meta + e->sl_words, e->d_meta, e->mapped[1],
-            e->d_ws, e->ws_bytes, e->d_counters, B, B, B, e->hq, e->hkv, kHeadDim,
-            e->physical_pages, e->page_size, e->max_pages, e->dtype, stream);
+            e->d_q, e->k_pages, e->v_pages, e->d_meta + e->sl_words + e->plan_words, e->d_meta,
+            e->mapped[1], e->d_ws, e->ws_bytes, e->d_counters, B, B, B, e->hq, e->hkv, kHeadDim,
+            e->physical_pages, e->page_size, e->max_pages, e->dtype, stream,
+            e->d_meta + e->sl_words);
     };
     StepGraph* g = nullptr;
     for (auto& x : e->graphs) {

@@ -29,32 +29,39 @@
 
 namespace pkv {
 
+// Kernel parameters live in the constant bank, and the first read of each of
+// its lines misses all the way to memory: the fields that the schedule and
+// the first item read come first, in four 32-byte lines that the kernel
+// touches together at entry (decode_params_touch).
 struct DecodeParams {
-    const void* q;                 // [q_rows, Hq, 128]
-    void* out;                     // [out_rows, Hq, 128] or null (state mode)
-    float* state_out;              // [B, Hq, 130] combined states, or null
-    const int32_t* block_table;    // [B, max_pages]
+    const int32_t* plan;           // host-built schedule of the device-side route, or null
     const int32_t* seq_lens;       // [B] or null (every row has `context`)
+    const int32_t* block_table;    // [B, max_pages]
     const int32_t* q_indices;      // [B] or null
     const int32_t* out_indices;    // [B] or null
+    const uint8_t* k_pages;        // pool bases (cp.async load path)
+    const uint8_t* v_pages;
+    const void* q;                 // [q_rows, Hq, 128]
+    unsigned* error;               // device error word
+    int32_t* merge_counters;       // [B, Hkv] for the fused merge, or null
+    int B, q_rows, out_rows, Hq;
+    int Hkv, num_pages, page_size, max_pages;
+    int auto_groups;   // > 0: device-side schedule over auto_groups x Hkv CTAs
+    int total_slots;
+    float scale_log2;  // softmax scale * log2(e) (times the K scale for e4m3 pools)
+    float v_scale;     // e4m3 pools: V scale, applied to each item's state
+    // ---- read later (item ends, merges, other routes)
+    void* out;                     // [out_rows, Hq, 128] or null (state mode)
+    float* state_out;              // [B, Hq, 130] combined states, or null
     const int32_t* work_items;     // [T, 5] or null (rectangular grid)
     const int32_t* split_offsets;  // [B + 1] (work queue)
-    int32_t* merge_counters;       // [B, Hkv] for the fused merge, or null
     // partial states, [Hkv][total_slots][G] (m, l) and [Hkv][total_slots][G][128]
     // (acc): the slots of one (row, KV head) are one contiguous block
     float* part_m;
     float* part_l;
     float* part_acc;
-    const uint8_t* k_pages;        // pool bases (cp.async load path)
-    const uint8_t* v_pages;
-    unsigned* error;               // device error word
     unsigned long long* stamps;    // [grid][kStampsPerCta] phase stamps (diagnostic build) or null
-    int B, q_rows, out_rows, Hq, Hkv;
-    int num_pages, page_size, max_pages;
-    int context, num_splits, num_items, total_slots;
-    int auto_groups;   // > 0: device-side schedule over auto_groups x Hkv CTAs
-    float scale_log2;  // softmax scale * log2(e) (times the K scale for e4m3 pools)
-    float v_scale;     // e4m3 pools: V scale, applied to each item's state
+    int context, num_splits, num_items;
     // Sequence-sharded decode with the state exchange fused in (xg_world > 0):
     // rank r's gather buffer of LL words [2 parities][world][xg_bcap][Hq][130],
     // mapped into this process for every rank, and this rank's
@@ -63,6 +70,14 @@ struct DecodeParams {
     unsigned* xg_counters;
     int xg_world, xg_rank, xg_bcap;
 };
+
+// Reads one word of each of the first six 32-byte lines of the parameter
+// block together, so their constant-cache misses overlap instead of
+// surfacing one by one along the schedule's dependent chain.
+__device__ __forceinline__ void decode_params_touch(const DecodeParams& p) {
+    asm volatile("" ::"l"(p.plan), "l"(p.q_indices), "l"(p.q), "r"(p.B), "r"(p.auto_groups),
+                 "l"(p.state_out));
+}
 
 // Phase stamps (diagnostic build, PKV_PHASE_STAMPS): per CTA, written by one
 // thread each -- %globaltimer values
@@ -713,6 +728,96 @@ __device__ __forceinline__ Item auto_item(const DecodeParams& p, AutoCursor& c, 
     return it;
 }
 
+// ------------------------------------------------------------ host plan
+// The device-side schedule computed on the host (pkv_build_auto_plan): a
+// header {magic, NG, B, T} padded to 16 words, then per group g of the NG
+// groups kPlanEntryWords words {first row, one past its last row, tile prefix
+// and slot prefix of the first row, its length, first and last group of the
+// first row, its q row and output row, then the physical pages of the first
+// kPlanPages boxes of the group's first piece (-1 past its end)}.  With a plan
+// the producer issues its first K/V copies after one read of 80 bytes,
+// instead of reading seq_lens, deriving the schedule and reading the block
+// table first.  Every value it takes from the plan is range-checked.
+constexpr int32_t kPlanMagic = 0x504B5650;
+constexpr int kPlanHeaderWords = 16;
+constexpr int kPlanEntryWords = 20;
+constexpr int kPlanPages = 8;
+
+// Whole-warp.  Fills the cursor, the first item and this lane's page id of
+// the first batch (kPlanPages boxes) from the group's plan entry; returns
+// false (and raises PKV_DEVERR_WORK_ITEM) when the plan does not belong to
+// this launch, and the caller derives the schedule itself.
+template <int BOX_ROWS>
+__device__ __forceinline__ bool plan_init(const DecodeParams& p, int lane, AutoCursor& c,
+                                          Item& it, int& pid0, bool report) {
+    const int g = (int)blockIdx.x / p.Hkv;
+    const int32_t* ent = p.plan + kPlanHeaderWords + (size_t)g * kPlanEntryWords;
+    int v = 0;
+    if (lane < 4) {
+        v = __ldg(p.plan + lane);
+    } else if (lane < 4 + kPlanEntryWords) {
+        v = __ldg(ent + (lane - 4));
+    }
+    auto word = [&](int i) { return __shfl_sync(0xffffffffu, v, i); };
+    const int page_word = __shfl_sync(0xffffffffu, v, 4 + 9 + (lane & (kPlanPages - 1)));
+    if (lane == 0 && v != -12345) PKV_STAMP_VALUE(p, 29, clock64());  // the plan words are in
+    const long long T = word(3);
+    const int row = word(4), row_end = word(5), P = word(6), O = word(7);
+    const long long limit = (long long)p.max_pages * p.page_size;
+    const bool ok = word(0) == kPlanMagic && word(1) == p.auto_groups && word(2) == p.B && T >= 0 &&
+                    row < p.B && row_end <= p.B && (row < 0 || (row_end > row && P >= 0 && O >= 0));
+    if (!ok) {
+        if (report) raise_error(p.error, kErrWorkItem);
+        return false;
+    }
+    if (lane == 0) PKV_STAMP_VALUE(p, 30, clock64());
+    c.NG = p.auto_groups;
+    c.g = g;
+    c.kvh = (int)blockIdx.x % p.Hkv;
+    c.T = T;
+    c.sd.init(T, c.NG);
+    c.b = row;
+    c.b_end = row < 0 ? row : row_end;
+    c.P = P;
+    c.O = O;
+    if (row < 0) return true;
+    int seq = word(8);
+    seq = seq < 0 ? 0 : ((long long)seq > limit ? (int)limit : seq);
+    const int n = (seq + kTileTokens - 1) / kTileTokens;
+    const int gf = word(9), gl = word(10), qr = word(11), orow = word(12);
+    long long tb = 0, te = 0;
+    if (n > 0) {
+        const long long s0 = auto_group_start(c.g, c.sd);
+        const long long s1 = auto_group_start(c.g + 1, c.sd);
+        tb = (s0 > c.P ? s0 : c.P) - c.P;
+        te = ((c.P + n) < s1 ? (c.P + n) : s1) - c.P;
+    }
+    long long t_end = te * kTileTokens;
+    if (t_end > seq) t_end = seq;
+    it.noop = false;
+    it.row = row;
+    it.kvh = c.kvh;
+    it.tok_begin = (int)(tb * kTileTokens);
+    it.tok_end = (int)(t_end > it.tok_begin ? t_end : it.tok_begin);
+    it.split = c.g - gf;
+    it.row_splits = gl - gf + 1;
+    it.slot = c.O + it.split;
+    if (it.split < 0 || it.row_splits < 1 || it.slot >= p.total_slots) {
+        if (report) raise_error(p.error, kErrSlot);
+        it.slot = -1;
+        it.row_splits = 2;
+    }
+    it.q_row = (qr >= 0 && qr < p.q_rows) ? qr : -1;
+    if (it.q_row < 0 && report) raise_error(p.error, kErrIndex);
+    it.out_row = (orow >= 0 && orow < p.out_rows) ? orow : -1;
+    if (it.out_row < 0 && report && p.out != nullptr) raise_error(p.error, kErrIndex);
+    pid0 = (lane < kPlanPages && it.tok_begin + lane * BOX_ROWS < it.tok_end) ? page_word : -1;
+    c.P += n;
+    c.O += it.row_splits;
+    c.b += 1;
+    return true;
+}
+
 template <int G>
 struct DecodeSmem {
     static constexpr int kMergeStride = kHeadDim + 4;  // padded: conflict-free combine
@@ -1101,7 +1206,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     static_assert(BOX_ROWS == 8 || BOX_ROWS == 16, "box rows must be 8 or 16");
     static_assert(!KV8 || (LOAD == kLoadCpAsync && sizeof(T) == 2), "e4m3 K/V: cp.async only");
     constexpr int kBoxesPerStage = kStageTokens / BOX_ROWS;
-    constexpr int kStagesPerBatch = 32 / kBoxesPerStage;
+    static_assert(kPlanPages % kBoxesPerStage == 0, "a plan's first batch is whole stages");
     constexpr int kBoxBytes = BOX_ROWS * kHalfRowBytes;
     using Ops = ElemOps<T>;
 
@@ -1135,6 +1240,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     // Launched behind a stage-in kernel (programmatic dependent launch), the
     // CTA starts early and waits here for its metadata; otherwise a no-op.
     PKV_CLOCK_BASE(t_entry);
+    decode_params_touch(p);
     griddep_wait();
     if (threadIdx.x == 0) PKV_STAMP(p, 0);
     if (threadIdx.x == kConsumerWarps * 32) {
@@ -1147,10 +1253,17 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     acur.b = acur.b_end = 0;
     Item first_item;
     int first_pid0 = -1;
+    int first_width = 32;  // boxes of the producer's first batch
     __shared__ int s_my_items;
     if (warp == kConsumerWarps) {
         int mine;
-        if (p.auto_groups > 0) {
+        const bool planned = p.auto_groups > 0 && p.plan != nullptr &&
+                             plan_init<BOX_ROWS>(p, lane, acur, first_item, first_pid0, lane == 0);
+        if (planned) {
+            // the plan's first item is built: the cursor stands on the next row
+            mine = acur.b >= 0 ? acur.b_end - (acur.b - 1) : 0;
+            first_width = kPlanPages;
+        } else if (p.auto_groups > 0) {
             acur = auto_init(p, lane);
             mine = acur.b >= 0 ? acur.b_end - acur.b : 0;
         } else {
@@ -1162,7 +1275,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
             PKV_STAMP(p, 1);
             PKV_CLOCK_STAMP(p, 13, t_entry);
         }
-        if (mine > 0) first_item = producer_next<BOX_ROWS>(p, 0, lane, first_pid0, acur);
+        if (mine > 0 && !planned) first_item = producer_next<BOX_ROWS>(p, 0, lane, first_pid0, acur);
         if (lane == 0) {
             s_my_items = mine;
             PKV_CLOCK_STAMP(p, 14, t_entry);
@@ -1269,12 +1382,15 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
             Item nxt = it;
             int nxt_pid0 = -1;
             int pid_next = pid0;
-            for (int base = 0; base < n_boxes && !aborted; base += 32) {
+            // the first batch of a planned launch is the plan's kPlanPages
+            // boxes; every other batch is 32 boxes, one per lane
+            int width = s == 0 ? first_width : 32;
+            for (int base = 0; base < n_boxes && !aborted; base += width, width = 32) {
                 const int box = base + lane;
                 const int tok = it.tok_begin + box * BOX_ROWS;
                 const int pid = pid_next;
-                if (base + 32 < n_boxes) pid_next = fetch_page(base + 32 + lane);
-                bool ok = box < n_boxes && tok < it.tok_end;
+                if (base + width < n_boxes) pid_next = fetch_page(base + width + lane);
+                bool ok = lane < width && box < n_boxes && tok < it.tok_end;
                 int y = 0;
                 if (ok) {
                     if (pid < 0 || pid >= p.num_pages) {
@@ -1288,7 +1404,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                     PKV_STAMP(p, 2);
                     PKV_CLOCK_STAMP(p, 17, t_entry);
                 }
-                const int stages_here = min(kStagesPerBatch, n_stages - base / kBoxesPerStage);
+                const int stages_here = min(width / kBoxesPerStage, n_stages - base / kBoxesPerStage);
                 for (int st = 0; st < stages_here; ++st) {
                     const uint32_t slot = gstage % NSLOTS;
                     if (gstage >= (uint32_t)NSLOTS) {

@@ -367,3 +367,109 @@ pkv_status pkv_build_workqueue(const pkv_router_params* p, const int32_t* seq_le
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ host plan
+// The device-side schedule of pkv_paged_attention_auto computed on the host,
+// with the same integer arithmetic as the kernel (pkv_kernels.cuh:
+// auto_init / auto_item): the 32-token tiles of all rows, concatenated in row
+// order, are cut into NG equal groups; group g's entry records its first row
+// piece and the pages of that piece's first boxes.
+namespace {
+constexpr int32_t kPlanMagic = 0x504B5650;
+constexpr int kPlanHeaderWords = 16;
+constexpr int kPlanEntryWords = 20;
+constexpr int kPlanPages = 8;
+}  // namespace
+
+extern "C" {
+
+int pkv_auto_groups(int Hkv, int sm_count);
+
+size_t pkv_auto_plan_bytes(int Hkv, int sm_count) {
+    const int ng = pkv_auto_groups(Hkv, sm_count);
+    if (ng <= 0) return 0;
+    return (size_t)(kPlanHeaderWords + (size_t)ng * kPlanEntryWords) * sizeof(int32_t);
+}
+
+pkv_status pkv_build_auto_plan(const int32_t* seq_lens, const int32_t* block_table, int B,
+                               int row_stride, const int32_t* q_indices,
+                               const int32_t* out_indices, int max_pages, int page_size, int Hkv,
+                               int sm_count, int32_t* plan, size_t plan_bytes) {
+    if (seq_lens == nullptr || block_table == nullptr || plan == nullptr || B <= 0 ||
+        row_stride <= 0 || max_pages <= 0 || page_size <= 0 || page_size % 8 != 0 || Hkv <= 0)
+        return PKV_ERR_INVALID_ARGUMENT;
+    const int NG = pkv_auto_groups(Hkv, sm_count);
+    if (NG <= 0) return PKV_ERR_NO_DEVICE;
+    if (plan_bytes < pkv_auto_plan_bytes(Hkv, sm_count)) return PKV_ERR_CAPACITY;
+    const long long limit = (long long)max_pages * page_size;
+    std::vector<long long> P(B), O(B);
+    std::vector<int> n(B), gf(B), gl(B), seq(B);
+    long long T = 0;
+    for (int b = 0; b < B; ++b) {
+        if (seq_lens[b] < 0 || seq_lens[b] > limit) return PKV_ERR_INVALID_ARGUMENT;
+        seq[b] = seq_lens[b];
+        n[b] = tiles_of(seq[b]);
+        P[b] = T;
+        T += n[b];
+    }
+    if (T >= (1ll << 31)) return PKV_ERR_UNSUPPORTED;
+    auto group_of = [&](long long x) { return (int)(((x + 1) * NG - 1) / T); };
+    auto group_start = [&](int g) { return (long long)g * T / NG; };
+    long long o = 0;
+    for (int b = 0; b < B; ++b) {
+        if (T == 0) {
+            gf[b] = gl[b] = 0;
+        } else {
+            const long long first = n[b] > 0 ? P[b] : (P[b] < T ? P[b] : T - 1);
+            const long long last = n[b] > 0 ? P[b] + n[b] - 1 : first;
+            gf[b] = group_of(first);
+            gl[b] = group_of(last);
+        }
+        O[b] = o;
+        o += gl[b] - gf[b] + 1;
+    }
+    if (o >= (1ll << 31)) return PKV_ERR_UNSUPPORTED;
+    const int box_rows = page_size % 16 == 0 ? 16 : 8;
+    std::memset(plan, 0, (size_t)kPlanHeaderWords * sizeof(int32_t));
+    plan[0] = kPlanMagic;
+    plan[1] = NG;
+    plan[2] = B;
+    plan[3] = (int32_t)T;
+    int b_lo = 0;  // rows are visited in order: first row whose last group is >= g
+    for (int g = 0; g < NG; ++g) {
+        int32_t* e = plan + kPlanHeaderWords + (size_t)g * kPlanEntryWords;
+        for (int i = 0; i < kPlanEntryWords; ++i) e[i] = -1;
+        while (b_lo < B && gl[b_lo] < g) ++b_lo;
+        if (b_lo >= B) continue;
+        int b_hi = -1;
+        for (int b = b_lo; b < B && gf[b] <= g; ++b) b_hi = b;
+        const int b = b_lo;
+        e[0] = b;
+        e[1] = b_hi >= b ? b_hi + 1 : b;
+        e[2] = (int32_t)P[b];
+        e[3] = (int32_t)O[b];
+        e[4] = seq[b];
+        e[5] = gf[b];
+        e[6] = gl[b];
+        e[7] = q_indices != nullptr ? q_indices[b] : b;
+        e[8] = out_indices != nullptr ? out_indices[b] : b;
+        if (n[b] > 0) {
+            const long long s0 = group_start(g), s1 = group_start(g + 1);
+            const long long tb = std::max(s0, P[b]) - P[b];
+            const long long te = std::min(P[b] + n[b], s1) - P[b];
+            const long long tok0 = tb * PKV_TILE_TOKENS;
+            const long long tok1 = std::min<long long>(te * PKV_TILE_TOKENS, seq[b]);
+            for (int i = 0; i < kPlanPages; ++i) {
+                const long long tok = tok0 + (long long)i * box_rows;
+                if (tok >= tok1) break;
+                const long long slot = tok / page_size;
+                e[9 + i] = (slot < max_pages && slot < row_stride)
+                               ? block_table[(size_t)b * row_stride + slot]
+                               : -1;
+            }
+        }
+    }
+    return PKV_OK;
+}
+
+}  // extern "C"

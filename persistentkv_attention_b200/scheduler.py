@@ -134,3 +134,35 @@ class Router:
             _native.check(status)
             break
         return WorkQueue(items[: n_items.value], offsets, int(n_slots.value))
+
+
+def auto_groups(hkv: int, sm_count: int) -> int:
+    """NG, the group count of the device-side schedule (``pkv_auto_groups``)."""
+    return int(_native.load().pkv_auto_groups(int(hkv), int(sm_count)))
+
+
+def plan_words(hkv: int, sm_count: int) -> int:
+    """int32 words of a host plan (``pkv_auto_plan_bytes`` / 4)."""
+    return int(_native.load().pkv_auto_plan_bytes(int(hkv), int(sm_count))) // 4
+
+
+def build_auto_plan(seq_lens, block_rows, max_pages: int, page_size: int, hkv: int,
+                    sm_count: int, q_indices=None, out_indices=None,
+                    out: np.ndarray | None = None) -> np.ndarray:
+    """Host plan of the device-side schedule for one step (``pkv_build_auto_plan``):
+    the group entries ``pkv_paged_attention_auto_planned`` starts from.  ``block_rows``
+    is the host block table [B, width]; ``max_pages`` the launch's row count."""
+    lens = _i32(seq_lens)
+    rows = np.ascontiguousarray(block_rows, dtype=np.int32)
+    b = lens.size
+    words = plan_words(hkv, sm_count)
+    plan = out if out is not None else np.empty(words, dtype=np.int32)
+    if plan.dtype != np.int32 or plan.size < words or not plan.flags.c_contiguous:
+        raise RuntimeError("plan buffer must be contiguous int32 with room for the plan")
+    qi = None if q_indices is None else _i32(q_indices)
+    oi = None if out_indices is None else _i32(out_indices)
+    _native.check(_native.load().pkv_build_auto_plan(
+        _ptr(lens), _ptr(rows), b, rows.shape[1], None if qi is None else _ptr(qi),
+        None if oi is None else _ptr(oi), int(max_pages), int(page_size), int(hkv),
+        int(sm_count), _ptr(plan), plan.size * 4))
+    return plan

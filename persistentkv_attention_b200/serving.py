@@ -33,7 +33,7 @@ import torch
 
 from . import ops
 from .ops import _stream
-from .scheduler import Router
+from .scheduler import Router, build_auto_plan, plan_words
 
 HEAD_DIM = 128
 
@@ -47,6 +47,7 @@ class HostPlan:
     total_slots: int
     bucket: int
     tokens: int                # sum of seq_lens
+    plan_words: int = 0        # host plan of the device-side schedule (0: none)
 
     def views(self, t: torch.Tensor):
         """Splits a (host or device) copy of the buffer into its fields."""
@@ -59,6 +60,9 @@ class HostPlan:
             o += size
         out["block_table"] = out["block_table"].view(b, mp)
         out["work_items"] = out["work_items"].view(n, 5)
+        if self.plan_words:
+            o = -(-o // 4) * 4                 # the plan starts 16-byte aligned
+            out["plan"] = t[o:o + self.plan_words]
         return out
 
     @property
@@ -79,8 +83,9 @@ class StepPlan:
         return self.host.batch
 
 
-def _staging_size(batch: int, max_pages: int, items: int) -> int:
-    return batch * max_pages + 4 * batch + 1 + 5 * items
+def _staging_size(batch: int, max_pages: int, items: int, plan_words: int = 0) -> int:
+    words = batch * max_pages + 4 * batch + 1 + 5 * items
+    return (-(-words // 4) * 4 + plan_words) if plan_words else words
 
 
 class DecodeEngine:
@@ -88,9 +93,12 @@ class DecodeEngine:
 
     def __init__(self, k_pages: torch.Tensor, v_pages: torch.Tensor, hq: int,
                  router: Router | None = None, policy: str = "device", fused: bool = True,
-                 requested_splits: int = 0, kv_scales: tuple[float, float] | None = None):
+                 requested_splits: int = 0, kv_scales: tuple[float, float] | None = None,
+                 use_plan: bool = True):
         """``kv_scales`` = (k_scale, v_scale) for ``torch.float8_e4m3fn`` pools
-        (q and output are then fp16; device schedule only)."""
+        (q and output are then fp16; device schedule only).  ``use_plan``: with
+        the device schedule, each step carries a host plan of the schedule
+        (``scheduler.build_auto_plan``) uploaded with its other metadata."""
         self.k_pages = k_pages
         self.v_pages = v_pages
         self.hq = hq
@@ -109,6 +117,8 @@ class DecodeEngine:
         self.policy = policy
         self.fused = fused
         self.requested_splits = requested_splits
+        self.sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self.use_plan = use_plan and policy == "device" and not self.kv8
         self._workspace = torch.empty(0, device=self.device, dtype=torch.float32)
         self._counters = torch.zeros(0, device=self.device, dtype=torch.int32)
         # buffers replaced by a larger one stay alive: captured graphs may
@@ -132,12 +142,13 @@ class DecodeEngine:
             items, offsets, n_items = queue.work_items, queue.split_offsets, queue.num_items
             total_slots = queue.total_slots
         mp = block_rows.shape[1]
-        size = _staging_size(b, mp, n_items)
+        pw = plan_words(self.hkv, self.sm_count) if self.use_plan else 0
+        size = _staging_size(b, mp, n_items, pw)
         if out is None or out.numel() < size:
             out = torch.empty(size, dtype=torch.int32, pin_memory=True)
         buf = out[:size]
         plan = HostPlan(buf, b, mp, n_items, total_slots, int(seq.max(initial=1)),
-                        int(seq.sum()))
+                        int(seq.sum()), pw)
         v = plan.views(buf)
         v["block_table"].numpy()[:] = block_rows
         v["seq_lens"].numpy()[:] = seq
@@ -146,6 +157,10 @@ class DecodeEngine:
         v["split_offsets"].numpy()[:] = offsets
         if items is not None:
             v["work_items"].numpy()[:] = items
+        if pw:
+            build_auto_plan(seq, block_rows, mp, self.page_size, self.hkv, self.sm_count,
+                            q_indices=v["q_indices"].numpy(), out_indices=v["out_indices"].numpy(),
+                            out=v["plan"].numpy())
         return plan
 
     def _auto_groups(self) -> int:
@@ -197,7 +212,7 @@ class DecodeEngine:
             ops.paged_attention_auto(
                 q_source, self.k_pages, self.v_pages, f["block_table"], f["seq_lens"], out,
                 self._workspace, f["q_indices"], f["out_indices"],
-                counters if self.fused else None)
+                counters if self.fused else None, plan=f.get("plan"))
             return
         ops.paged_attention_workqueue(
             q_source, self.k_pages, self.v_pages, f["block_table"], f["seq_lens"],
@@ -373,7 +388,10 @@ class StepGraph:
         self._out = torch.zeros(out_rows + 1, hq, HEAD_DIM, dtype=engine.dtype, device=dev)
         self.out = self._out[:out_rows]
         b, mp = max_batch, max_pages
-        self._words = b * mp + 3 * b
+        # [block table | seq_lens | q_indices | out_indices | host plan (16-byte aligned)]
+        self._plan_off = -(-(b * mp + 3 * b) // 4) * 4
+        self._plan_words = plan_words(engine.hkv, engine.sm_count)
+        self._words = self._plan_off + self._plan_words
         self._dev = torch.zeros(self._words, dtype=torch.int32, device=dev)
         self._ws = torch.empty(ops.auto_workspace_bytes(b, hq, engine.hkv) // 4,
                                dtype=torch.float32, device=dev)
@@ -381,7 +399,8 @@ class StepGraph:
         bt = self._dev[: b * mp].view(b, mp)
         sl = self._dev[b * mp: b * mp + b]
         qi = self._dev[b * mp + b: b * mp + 2 * b]
-        oi = self._dev[b * mp + 2 * b:]
+        oi = self._dev[b * mp + 2 * b: b * mp + 3 * b]
+        plan = self._dev[self._plan_off:]
         self._stage = [torch.zeros(self._words, dtype=torch.int32).pin_memory() for _ in range(2)]
         self._done = [torch.cuda.Event() for _ in range(2)]
         self._graphs = []
@@ -392,7 +411,7 @@ class StepGraph:
             def run(i=i):
                 self._dev.copy_(self._stage[i], non_blocking=True)
                 ops.paged_attention_auto(self.q, engine.k_pages, engine.v_pages, bt, sl,
-                                         self._out, self._ws, qi, oi, self._counters)
+                                         self._out, self._ws, qi, oi, self._counters, plan=plan)
 
             with torch.cuda.stream(self._stream):
                 run()  # first call outside capture (kernel attributes, maps)
@@ -419,9 +438,12 @@ class StepGraph:
         qi = v[b * mp + b: b * mp + 2 * b]
         qi[:] = 0
         qi[:n] = np.arange(n) if q_indices is None else q_indices
-        oi = v[b * mp + 2 * b:]
+        oi = v[b * mp + 2 * b: b * mp + 3 * b]
         oi[:] = self.out_rows            # the spare row
         oi[:n] = np.arange(n) if out_indices is None else out_indices
+        build_auto_plan(v[b * mp: b * mp + b], bt, mp, self.engine.page_size, self.engine.hkv,
+                        self.engine.sm_count, q_indices=qi, out_indices=oi,
+                        out=v[self._plan_off:])
 
     def step(self, seq_lens, block_rows: np.ndarray, q_indices=None, out_indices=None) -> None:
         """Queues one decode step on the graph's stream (``self.q`` -> ``self.out``),

@@ -474,8 +474,11 @@ def test_native_host_step():
         h2d, d2h = engine.step_host(c.seq_lens[:b], c.block_table[:b], q_host, out_host, scratch)
         torch.cuda.current_stream().synchronize()
         nat = scratch["native"]
-        # staged metadata: lengths (padded to 16 bytes), then b rows of the engine's width
-        meta = (-(-nat.max_batch // 4) * 4 + b * nat.max_pages) * 4
+        # staged metadata: lengths (padded to 16 bytes), the host plan of the
+        # schedule (padded to 16 bytes), then b rows of the engine's width
+        from persistentkv_attention_b200.scheduler import plan_words
+        pw = -(-plan_words(8, torch.cuda.get_device_properties(0).multi_processor_count) // 4) * 4
+        meta = (-(-nat.max_batch // 4) * 4 + pw + b * nat.max_pages) * 4
         assert h2d == meta + b * 32 * 128 * 2
         assert d2h == b * 32 * 128 * 2
         assert_close(out_host[:b], want[:b], "f16", f"native step B{b}")
@@ -654,3 +657,53 @@ def test_gather_modes_bit_identical(g, dtype, page):
         a, b = results[("cpasync", route)][rows], results[("tma", route)][rows]
         assert torch.equal(a, b), f"{route}: gathers differ"
         assert_close(results[("tma", route)], want, dtype, f"tma {route}")
+
+
+@pytest.mark.parametrize("g,dtype,page", [(4, "f16", 16), (1, "f16", 8), (8, "bf16", 32),
+                                          (2, "bf16", 16)])
+def test_planned_schedule_bit_identical(g, dtype, page):
+    """A host plan of the device schedule (pkv_paged_attention_auto_planned)
+    gives the same bits as the schedule the kernel derives itself, and a plan
+    of another batch shape is detected, ignored and flagged."""
+    from persistentkv_attention_b200.scheduler import build_auto_plan
+
+    lens = [0] + EDGE_LENS + [9000, 4096]
+    c = make_case(lens, hq=32, hkv=32 // g, page_size=page, dtype=dtype, seed=400 + g,
+                  indexed=True)
+    d = c.cuda()
+    want = c.oracle()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    plan = torch.from_numpy(build_auto_plan(c.seq_lens, c.block_table, c.block_table.shape[1],
+                                            page, c.hkv, sms, q_indices=c.q_indices,
+                                            out_indices=c.out_indices)).cuda()
+    outs = []
+    for pl in (None, plan):
+        for fused in (True, False):
+            ws = torch.empty(ops.auto_workspace_bytes(len(lens), 32, c.hkv) // 4, device="cuda")
+            out = torch.full((c.out_rows, 32, 128), float("nan"), device="cuda",
+                             dtype=d["q_source"].dtype)
+            ctr = torch.zeros(len(lens), c.hkv, device="cuda", dtype=torch.int32)
+            ops.paged_attention_auto(d["q_source"], d["k_pages"], d["v_pages"], d["block_table"],
+                                     d["seq_lens"], out, ws, d["q_indices"], d["out_indices"],
+                                     ctr if fused else None, plan=pl)
+            torch.cuda.synchronize()
+            assert (ctr == 0).all()
+            outs.append(out)
+    rows = torch.from_numpy(c.out_indices).long().cuda()
+    # same merge (fused: 0, 2; separate kernel: 1, 3), planned or derived schedule
+    assert torch.equal(outs[2][rows], outs[0][rows]), "planned and derived schedules differ"
+    assert torch.equal(outs[3][rows], outs[1][rows]), "planned and derived schedules differ"
+    assert_close(outs[2], want, dtype, "planned")
+    assert_close(outs[3], want, dtype, "planned, separate merge")
+    # a plan built for one row fewer: ignored (the kernel derives its schedule) and flagged
+    bad = torch.from_numpy(build_auto_plan(c.seq_lens[:-1], c.block_table[:-1],
+                                           c.block_table.shape[1], page, c.hkv, sms)).cuda()
+    ws = torch.empty(ops.auto_workspace_bytes(len(lens), 32, c.hkv) // 4, device="cuda")
+    out = torch.full((c.out_rows, 32, 128), float("nan"), device="cuda", dtype=d["q_source"].dtype)
+    ops.paged_attention_auto(d["q_source"], d["k_pages"], d["v_pages"], d["block_table"],
+                             d["seq_lens"], out, ws, d["q_indices"], d["out_indices"],
+                             torch.zeros(len(lens), c.hkv, device="cuda", dtype=torch.int32),
+                             plan=bad)
+    torch.cuda.synchronize()
+    assert _native.device_error(clear=True) & 0x4
+    assert torch.equal(out[rows], outs[0][rows])

@@ -177,9 +177,16 @@ def test_step_graph_staging_layout():
 
     from persistentkv_attention_b200.serving import StepGraph
 
+    from types import SimpleNamespace
+
+    from persistentkv_attention_b200.scheduler import plan_words
+
     sg = StepGraph.__new__(StepGraph)
     sg.max_batch, sg.max_pages, sg.q_rows, sg.out_rows = 4, 5, 6, 7
-    sg._words = 4 * 5 + 3 * 4
+    sg.engine = SimpleNamespace(page_size=16, hkv=8, sm_count=148)
+    sg._plan_off = 4 * 5 + 3 * 4
+    sg._plan_words = plan_words(8, 148)
+    sg._words = sg._plan_off + sg._plan_words
     sg._stage = [torch.full((sg._words,), -9, dtype=torch.int32)]
     rows = np.array([[3, 4], [7, 8]], np.int32)
     sg._fill(0, np.array([20, 9], np.int32), rows, np.array([5, 2]), np.array([1, 0]))
@@ -190,6 +197,8 @@ def test_step_graph_staging_layout():
     assert v[20:24].tolist() == [20, 9, 0, 0]
     assert v[24:28].tolist() == [5, 2, 0, 0]
     assert v[28:32].tolist() == [1, 0, 7, 7]
+    # the host plan of the device schedule over all four rows (two of length 0)
+    assert v[32:36].tolist() == [0x504B5650, 37, 4, 2]   # T: one tile per nonempty row
     try:
         sg._fill(0, np.zeros(5, np.int32), np.zeros((5, 2), np.int32), None, None)
     except RuntimeError as e:
