@@ -81,6 +81,7 @@ DTYPES = {"f16": torch.float16, "bf16": torch.bfloat16}
 D = 128
 SEED = 20260622
 FLUSH_BYTES = 256 << 20
+LAYERS = 8            # model layers of the back-to-back measurement
 # tolerance of the reference (benchmark_serving_trace.py:37-38); bf16 outputs
 # add one bf16 rounding of the value (2^-8 relative), since they are stored in bf16
 MAX_ERR = 2e-3
@@ -336,7 +337,7 @@ class Config:
     distinct step, and its timed run."""
 
     def __init__(self, name, args, dev, stream, rank, hkv=None, dtype="f16", kv_fp8=False,
-                 steps=None):
+                 steps=None, groups=0, layers=1):
         from persistentkv_attention_b200.serving import DecodeEngine
 
         self.name = name
@@ -350,6 +351,11 @@ class Config:
         self.kv_fp8 = kv_fp8
         tdt = DTYPES[dtype]
         k_pages, v_pages, q_pool = make_inputs(w, physical, self.hkv, tdt, dev, rank)
+        self.layers = layers
+        # layers > 1: that many distinct K/V pools (one per model layer), each
+        # step decodes every layer back to back in one graph
+        extra = [make_inputs(w, physical, self.hkv, tdt, dev, rank + 1000 * (i + 1))[:2]
+                 for i in range(layers - 1)]
         self.kv_elem = 2
         if kv_fp8:
             # e4m3 cache with per-tensor scales; the pools kept here hold the
@@ -362,7 +368,10 @@ class Config:
             self.kv_elem = 1
             self.engine = DecodeEngine(k8, v8, HQ, fused=not args.no_fused, kv_scales=scales)
         else:
-            self.engine = DecodeEngine(k_pages, v_pages, HQ, fused=not args.no_fused)
+            self.engine = DecodeEngine(k_pages, v_pages, HQ, fused=not args.no_fused,
+                                       groups=groups)
+        self.layer_engines = [DecodeEngine(k, v, HQ, fused=not args.no_fused, groups=groups)
+                              for k, v in extra]
         self.k_pages, self.v_pages, self.q_pool = k_pages, v_pages, q_pool
         self.stream = stream
         self.plans, self.graphs, self.outs = [], [], []
@@ -372,7 +381,23 @@ class Config:
         for p in self.plans:
             o = torch.empty(p.batch, HQ, D, dtype=tdt, device=dev)
             self.outs.append(o)
-            self.graphs.append(self.engine.capture(p, q_pool, o, stream))
+            if layers == 1:
+                self.graphs.append(self.engine.capture(p, q_pool, o, stream))
+                continue
+            # one graph per step holding every layer's decode (same metadata,
+            # each layer its own pool, workspace and output)
+            outs_l = [torch.empty_like(o) for _ in self.layer_engines]
+            for e, ol in zip(self.layer_engines, outs_l):
+                e.reserve(p.batch, p.host.total_slots)
+                e.run(p, q_pool, ol)
+            self.engine.run(p, q_pool, o)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(g, stream=stream):
+                    self.engine.run(p, q_pool, o)
+                    for e, ol in zip(self.layer_engines, outs_l):
+                        e.run(p, q_pool, ol)
+            self.graphs.append(g)
         torch.cuda.synchronize()
         self.sched = [i % n_distinct for i in range(self.warmup + self.steps_timed)]
 
@@ -395,7 +420,8 @@ class Config:
                     self.graphs[j].replay()
                     ev[i][1].record(self.stream)
             barrier()
-        self.times_ms = [a.elapsed_time(b) for a, b in ev]
+        # per layer: one layer's decode is one step of the metric
+        self.times_ms = [a.elapsed_time(b) / self.layers for a, b in ev]
         self.tokens = sum(self.plans[j].batch for j in self.sched[self.warmup:])
         self.bytes_alg = sum(kv_bytes(self.trace_steps[j], self.hkv, self.kv_elem)
                              for j in self.sched[self.warmup:])
@@ -422,6 +448,11 @@ class Config:
             raise SystemExit(f"correctness gate failed on {self.name}: max abs error {err:.3e}")
         return err
 
+    def groups_used(self):
+        """Group counts of the device schedule over the timed steps."""
+        used = sorted({self.plans[j].host.groups for j in self.sched[self.warmup:]})
+        return ",".join(str(g) for g in used)
+
     def summary(self, peak):
         total_ms = sum(self.times_ms)
         per_step_bytes = self.bytes_alg / self.steps_timed
@@ -431,10 +462,12 @@ class Config:
                 "steps": self.steps_timed, "value": self.tokens / (total_ms / 1000.0),
                 "unit": "tokens/s", "ms_per_step": total_ms / self.steps_timed,
                 "us_per_step_median": 1000.0 * statistics.median(self.times_ms),
+                "groups": self.groups_used(),
                 "kv_bytes_per_step": per_step_bytes, "hbm_gbs": achieved,
                 "frac_of_measured_peak": achieved / peak, "frac_of_8tbs": achieved / 8000.0}
 
     def release(self):
+        self.layer_engines = []
         self.graphs.clear()
         self.plans.clear()
         self.outs.clear()
@@ -580,6 +613,21 @@ def run_engine_arm(args) -> None:
         cfg.release()
         _native.set_gather_mode(args.gather)
         per_config[f"{args.workload}@gather={args.gather}"] = main_summary
+        # back to back: one interval covers a step of LAYERS model layers, each
+        # with its own K/V pool (inputs far larger than L2, no flush between
+        # the layers), reported per layer
+        for name in (args.workload, "long_b1"):
+            cfg = Config(name, args, dev, stream, rank, hkv=args.hkv or None, dtype=args.dtype,
+                         steps=min(args.steps, 10), layers=LAYERS)
+            cfg.timed(flush, barrier, clocks)
+            err = cfg.gate()
+            per_config[f"{name}@{LAYERS} layers back to back"] = dict(
+                cfg.summary(peak), correctness_max_abs_err=err,
+                timing=f"one CUDA-event interval per step of {LAYERS} layers (distinct pools, "
+                       f"{LAYERS} decode launches back to back), divided by {LAYERS}; L2 "
+                       "flushed before each step")
+            cfg.release()
+            torch.cuda.empty_cache()
         code = _native.device_error(clear=True)
         if code:
             raise RuntimeError(f"device error: {_native.describe_device_error(code)}")
@@ -621,7 +669,9 @@ def run_engine_arm(args) -> None:
             "l2": "flushed before every step outside the timed intervals: 256 MiB write, "
                   "then 256 MiB read (no dirty lines left for the timed step)",
             "merge": "fused last-task merge" if not args.no_fused else "PDL merge kernel",
-            "schedule": "device-side equal-token groups (no host work queue)",
+            "schedule": "device-side equal-token groups from a host plan uploaded with the "
+                        "step's metadata; group count per step from the calibrated router "
+                        f"(used: {main.groups_used()})",
             "gather": args.gather,
         },
         "hbm_gbs": achieved, "hbm_frac_of_8tbs": achieved / 8000.0,
@@ -846,6 +896,43 @@ def run_seq_shard_arm(args) -> None:
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------------------ group sweep
+SWEEP_GROUPS = (37, 32, 28, 24, 18, 14, 9, 6)
+
+
+def run_group_sweep(args) -> None:
+    """Step time of each config under each group count of the device schedule
+    (host plans), one B200: the measurements the router's B200 constants are
+    fitted to (persistentkv_attention_b200.calibrate)."""
+    from persistentkv_attention_b200 import _native
+    from persistentkv_attention_b200.scheduler import auto_groups
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    _native.set_gather_mode(args.gather)
+    flush = L2Flush(dev)
+    stream = torch.cuda.Stream(dev)
+    clocks = ClockSampler(0)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    out = {"sm_count": sms, "hkv": 8, "hq": HQ, "steps": args.steps, "configs": {}}
+    for name in ("single_b1", "uniform_8k", "bimodal_32k", "long_b1", "zipf_b64"):
+        res = {}
+        lens = None
+        for g in SWEEP_GROUPS:
+            if g > auto_groups(8, sms):
+                continue
+            cfg = Config(name, args, dev, stream, 0, steps=args.steps, groups=g)
+            cfg.timed(flush, barrier=torch.cuda.synchronize, clocks=clocks)
+            if lens is None:
+                lens = [list(cfg.trace_steps[j].lengths) for j in cfg.sched[cfg.warmup:]]
+            res[str(g)] = [1000.0 * t for t in cfg.times_ms]
+            cfg.release()
+            torch.cuda.empty_cache()
+        out["configs"][name] = {"lengths": lens, "us": res}
+    out["clocks"] = clocks.summary()
+    print(json.dumps(out), flush=True)
+
+
 # ------------------------------------------------------------------ phase stamps
 PHASES = [("launch_spread", 0, None), ("schedule", 0, 1), ("first_pages", 1, 2),
           ("first_issue", 2, 3), ("first_data", 3, 4), ("stream", 4, 5),
@@ -955,6 +1042,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-per-config", action="store_true",
                     help="time only --workload (no per_config / seq_shard sub-objects)")
+    ap.add_argument("--sweep-groups", action="store_true",
+                    help="time every config under several group counts (router calibration)")
     ap.add_argument("--phase-stamps", action="store_true",
                     help="diagnostic build: print per-phase CTA timings instead of the bench line")
     ap.add_argument("--seq-shard", action="store_true",
@@ -971,6 +1060,8 @@ def main() -> None:
     if args.phase_stamps:
         os.environ["PKV_LIB_VARIANT"] = "stamps"
         run_phase_stamps(args)
+    elif args.sweep_groups:
+        run_group_sweep(args)
     elif args.impl == "reference":
         run_reference_arm(args)
     elif args.seq_shard:

@@ -338,21 +338,26 @@ size_t pkv_auto_plan_bytes(int Hkv, int sm_count);
 
 /* seq_lens / block_table (row stride row_stride) / q_indices / out_indices
  * (either may be NULL = identity) are HOST copies of the step's metadata;
- * max_pages and page_size are those of the launch.  Writes plan (host,
- * plan_bytes >= pkv_auto_plan_bytes). */
+ * max_pages and page_size are those of the launch; groups is the schedule's
+ * group count, in [1, pkv_auto_groups(Hkv, sm_count)] (0 = that maximum; a
+ * router may choose fewer, see pkv_choose_groups), and the launch must use
+ * the same.  Writes plan (host, plan_bytes >= pkv_auto_plan_bytes). */
 pkv_status pkv_build_auto_plan(const int32_t* seq_lens, const int32_t* block_table, int B,
                                int row_stride, const int32_t* q_indices,
                                const int32_t* out_indices, int max_pages, int page_size,
-                               int Hkv, int sm_count, int32_t* plan, size_t plan_bytes);
+                               int Hkv, int sm_count, int groups, int32_t* plan,
+                               size_t plan_bytes);
 
 /* pkv_paged_attention_auto with a device copy of the step's plan (16-byte
- * aligned, plan_bytes >= pkv_auto_plan_bytes(Hkv, 0)). */
+ * aligned, plan_bytes >= pkv_auto_plan_bytes(Hkv, 0)) built for `groups`
+ * groups (0 = the maximum); the workspace is that of pkv_paged_attention_auto. */
 pkv_status pkv_paged_attention_auto_planned(
     const void* q_source, const void* k_pages, const void* v_pages,
     const int32_t* block_table, const int32_t* seq_lens,
     const int32_t* q_indices, const int32_t* out_indices, void* output,
     void* workspace, size_t workspace_bytes, int32_t* merge_counters, const void* plan,
-    size_t plan_bytes, int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim,
+    size_t plan_bytes, int groups, int B, int q_rows, int out_rows, int Hq, int Hkv,
+    int head_dim,
     int physical_pages, int page_size, int max_pages,
     pkv_dtype dtype, void* stream);
 
@@ -473,6 +478,14 @@ typedef struct pkv_router_params {
     int tasks_per_cta;      /* tasks per resident CTA slot (balanced policy)   */
     int max_splits;         /* cap on splits per row (balanced policy)         */
     int min_tiles_per_task; /* lower bound on task size (balanced policy)      */
+    /* Step-time model of the device-side schedule with NG groups (used by
+     * pkv_choose_groups): fixed_us + KV bytes / min(read_gbps,
+     * NG * hkv * cta_gbps) + (merge_us + merge_piece_us * n) when the most
+     * split row has n >= 2 pieces. */
+    double dev_fixed_us;    /* launch, schedule and first copies               */
+    double dev_cta_gbps;    /* what one decode CTA streams on its own          */
+    double dev_merge_us;    /* end-of-CTA merge of a split row ...             */
+    double dev_merge_piece_us; /* ... plus this per piece                      */
 } pkv_router_params;
 
 /* Fills p with the reference constants (benchmark_serving_trace.py:33-43). */
@@ -514,6 +527,14 @@ double pkv_estimate_route_ms(const pkv_router_params* p, const int32_t* lengths,
  * Writes the chosen splits and estimated milliseconds if non-NULL. */
 pkv_route pkv_choose_route(const pkv_router_params* p, const int32_t* lengths,
                            int n, int* splits_out, double* est_ms_out);
+
+/* Group count NG of the device-side schedule for one step: the NG in
+ * [max(1, NG_max / 8), NG_max] (NG_max = pkv_auto_groups(hkv, sm_count)) that
+ * minimises the dev_* step-time model; writes the modelled microseconds.  No
+ * counterpart in the reference, whose router picks split counts for its
+ * host-built queues. */
+int pkv_choose_groups(const pkv_router_params* p, const int32_t* lengths, int n,
+                      double* est_us_out);
 
 /* Builds the compact work queue of one decode step, following
  * compile_persistentkv_metadata (benchmark_serving_trace.py:686-703):

@@ -77,6 +77,10 @@ class RouterParams(ctypes.Structure):
         ("tasks_per_cta", c_int),
         ("max_splits", c_int),
         ("min_tiles_per_task", c_int),
+        ("dev_fixed_us", c_double),
+        ("dev_cta_gbps", c_double),
+        ("dev_merge_us", c_double),
+        ("dev_merge_piece_us", c_double),
     ]
 
 
@@ -120,12 +124,12 @@ SIGNATURES = {
     "pkv_auto_groups": (c_int, [c_int, c_int]),
     "pkv_auto_plan_bytes": (c_size_t, [c_int, c_int]),
     "pkv_build_auto_plan": (
-        c_int, [_I32P, _I32P, c_int, c_int, _I32P, _I32P, c_int, c_int, c_int, c_int, _I32P,
-                c_size_t]),
+        c_int, [_I32P, _I32P, c_int, c_int, _I32P, _I32P, c_int, c_int, c_int, c_int, c_int,
+                _I32P, c_size_t]),
     "pkv_paged_attention_auto_planned": (
         c_int,
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, _P, c_size_t, c_int, c_int, c_int,
-         c_int, c_int, c_int, c_int, c_int, c_int, c_int, _P],
+         c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, _P],
     ),
     "pkv_paged_attention_auto_state": (
         c_int,
@@ -180,6 +184,7 @@ SIGNATURES = {
     "pkv_estimate_route_ms": (c_double, [POINTER(RouterParams), _I32P, c_int, c_int, c_int]),
     "pkv_choose_route": (
         c_int, [POINTER(RouterParams), _I32P, c_int, POINTER(c_int), POINTER(c_double)]),
+    "pkv_choose_groups": (c_int, [POINTER(RouterParams), _I32P, c_int, POINTER(c_double)]),
     "pkv_build_workqueue": (
         c_int,
         [POINTER(RouterParams), _I32P, c_int, c_int, c_int, c_int, _I32P, c_int, _I32P,

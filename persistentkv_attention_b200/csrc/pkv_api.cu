@@ -746,7 +746,8 @@ pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* 
                        void* workspace, size_t workspace_bytes, int32_t* merge_counters,
                        int q_rows, int out_rows, void* stream,
                        const pkv_exchange* xg = nullptr, bool pdl = false,
-                       const float* kv8_scales = nullptr, const void* plan = nullptr);
+                       const float* kv8_scales = nullptr, const void* plan = nullptr,
+                       int groups = 0);
 
 }  // namespace
 
@@ -784,8 +785,9 @@ pkv_status pkv_paged_attention_auto_planned(
     const void* q_source, const void* k_pages, const void* v_pages, const int32_t* block_table,
     const int32_t* seq_lens, const int32_t* q_indices, const int32_t* out_indices, void* output,
     void* workspace, size_t workspace_bytes, int32_t* merge_counters, const void* plan,
-    size_t plan_bytes, int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim,
-    int physical_pages, int page_size, int max_pages, pkv_dtype dtype, void* stream) {
+    size_t plan_bytes, int groups, int B, int q_rows, int out_rows, int Hq, int Hkv,
+    int head_dim, int physical_pages, int page_size, int max_pages, pkv_dtype dtype,
+    void* stream) {
     Common c{q_source, k_pages, v_pages, block_table, B, Hq, Hkv, head_dim,
              physical_pages, page_size, max_pages, dtype};
     if (output == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "output must be a CUDA tensor");
@@ -798,7 +800,7 @@ pkv_status pkv_paged_attention_auto_planned(
     }
     return auto_common(c, seq_lens, q_indices, out_indices, output, nullptr, workspace,
                        workspace_bytes, merge_counters, q_rows, out_rows, stream, nullptr, false,
-                       nullptr, plan);
+                       nullptr, plan, groups);
 }
 
 }  // extern "C"
@@ -809,7 +811,7 @@ pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* 
                        const int32_t* out_indices, void* output, float* state_out,
                        void* workspace, size_t workspace_bytes, int32_t* merge_counters,
                        int q_rows, int out_rows, void* stream, const pkv_exchange* xg,
-                       bool pdl, const float* kv8_scales, const void* plan) {
+                       bool pdl, const float* kv8_scales, const void* plan, int groups) {
     const int B = c.B, Hq = c.Hq, Hkv = c.Hkv;
     const int max_pages = c.max_pages, page_size = c.page_size;
     pkv_status st = check_common(c);
@@ -821,8 +823,13 @@ pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* 
     DeviceState* ds = nullptr;
     st = current_device(&ds);
     if (st != PKV_OK) return st;
-    const int NG = auto_groups_for(ds->sm_count, Hkv);
-    const long long slots = (long long)B + NG;
+    const int NG_max = auto_groups_for(ds->sm_count, Hkv);
+    if (groups < 0 || groups > NG_max) {
+        return fail(PKV_ERR_INVALID_ARGUMENT, "groups=%d outside [1, %d] (0 = %d)", groups, NG_max,
+                    NG_max);
+    }
+    const int NG = groups > 0 ? groups : NG_max;
+    const long long slots = (long long)B + NG_max;  // the workspace holds the widest schedule
     const size_t need = (size_t)slots * Hq * (kHeadDim + 2) * sizeof(float);
     if (workspace == nullptr) return fail(PKV_ERR_WORKSPACE, "auto route requires workspace");
     if (workspace_bytes < need) {

@@ -213,7 +213,7 @@ pkv_status pkv_engine_step_host(pkv_engine* e, const int32_t* seq_lens,
     std::memcpy(h, seq_lens, (size_t)B * sizeof(int32_t));
     // the schedule, planned here from the host rows (the device starts from it)
     pkv_status pst = pkv_build_auto_plan(seq_lens, block_table, B, row_pages, nullptr, nullptr,
-                                         e->max_pages, e->page_size, e->hkv, 0,
+                                         e->max_pages, e->page_size, e->hkv, 0, 0,
                                          h + e->sl_words, e->plan_words * sizeof(int32_t));
     if (pst != PKV_OK) return efail(pst, "planning the step failed");
     int32_t* rows = h + e->sl_words + e->plan_words;

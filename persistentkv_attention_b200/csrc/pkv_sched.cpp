@@ -80,6 +80,11 @@ void pkv_router_params_reference(pkv_router_params* p) {
     p->tasks_per_cta = 1;
     p->max_splits = 48;
     p->min_tiles_per_task = 1;
+    // the reference has no device-side schedule: the model is the B200 one
+    p->dev_fixed_us = 16.0;
+    p->dev_cta_gbps = 30.0;
+    p->dev_merge_us = 1.5;
+    p->dev_merge_piece_us = 0.1;
 }
 
 void pkv_router_params_b200(pkv_router_params* p) {
@@ -89,8 +94,8 @@ void pkv_router_params_b200(pkv_router_params* p) {
     p->head_dim = 128;
     p->elem_bytes = 2;
     p->sm_count = 148;          // B200: 2 dies x 74 SMs
-    p->read_gbps = 6556.5;      // measured STREAM-style copy on this pool's B200s
-    p->launch_us = 2.5;         // graph-replayed launch + PDL-overlapped merge
+    p->read_gbps = 6350.0;      // decode streaming rate fitted to the group sweep below
+    p->launch_us = 6.0;         // CUDA-event interval of an empty graph launch after an L2 flush
     p->min_ctas_per_sm = 2.0;   // 2 resident 160-thread decode CTAs per SM
     p->supported_g = 0;         // every G in {1,2,4,8} runs the split routes
     p->min_split_len = 0;
@@ -98,6 +103,15 @@ void pkv_router_params_b200(pkv_router_params* p) {
     p->tasks_per_cta = 1;       // one task per resident CTA slot measured fastest
     p->max_splits = 256;
     p->min_tiles_per_task = 4;   // 128 tokens: 8 ring stages, two per consumer warp
+    // Least-squares fit (persistentkv_attention_b200/calibrate.py) of the
+    // step times of configs 1-5 under 8 group counts each, one B200, L2
+    // flushed before every step (profiles/router_sweep_b200.json): 2.5% RMS
+    // relative error.  Launch and merge cost are not separable in that data
+    // (every single-row step is split), so they share the fixed cost.
+    p->dev_fixed_us = 7.87;
+    p->dev_cta_gbps = 23.0;
+    p->dev_merge_us = 7.87;
+    p->dev_merge_piece_us = 0.056;
 }
 
 int pkv_choose_workqueue_row_splits(const pkv_router_params* p, int length, int active_count,
@@ -394,13 +408,16 @@ size_t pkv_auto_plan_bytes(int Hkv, int sm_count) {
 pkv_status pkv_build_auto_plan(const int32_t* seq_lens, const int32_t* block_table, int B,
                                int row_stride, const int32_t* q_indices,
                                const int32_t* out_indices, int max_pages, int page_size, int Hkv,
-                               int sm_count, int32_t* plan, size_t plan_bytes) {
+                               int sm_count, int groups, int32_t* plan, size_t plan_bytes) {
     if (seq_lens == nullptr || block_table == nullptr || plan == nullptr || B <= 0 ||
         row_stride <= 0 || max_pages <= 0 || page_size <= 0 || page_size % 8 != 0 || Hkv <= 0)
         return PKV_ERR_INVALID_ARGUMENT;
-    const int NG = pkv_auto_groups(Hkv, sm_count);
-    if (NG <= 0) return PKV_ERR_NO_DEVICE;
-    if (plan_bytes < pkv_auto_plan_bytes(Hkv, sm_count)) return PKV_ERR_CAPACITY;
+    const int NG_max = pkv_auto_groups(Hkv, sm_count);
+    if (NG_max <= 0) return PKV_ERR_NO_DEVICE;
+    if (groups < 0 || groups > NG_max) return PKV_ERR_INVALID_ARGUMENT;
+    const int NG = groups > 0 ? groups : NG_max;
+    if (plan_bytes < (size_t)(kPlanHeaderWords + (size_t)NG * kPlanEntryWords) * sizeof(int32_t))
+        return PKV_ERR_CAPACITY;
     const long long limit = (long long)max_pages * page_size;
     std::vector<long long> P(B), O(B);
     std::vector<int> n(B), gf(B), gl(B), seq(B);
@@ -470,6 +487,51 @@ pkv_status pkv_build_auto_plan(const int32_t* seq_lens, const int32_t* block_tab
         }
     }
     return PKV_OK;
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int pkv_choose_groups(const pkv_router_params* p, const int32_t* lengths, int n,
+                      double* est_us_out) {
+    if (p == nullptr || lengths == nullptr || n <= 0 || p->hkv <= 0) return 0;
+    const int ng_max = std::max(1, (2 * std::max(1, p->sm_count)) / p->hkv);
+    long long T = 0;
+    double bytes = 0.0;
+    std::vector<int> tiles(n);
+    for (int i = 0; i < n; ++i) {
+        const int len = std::max(0, (int)lengths[i]);
+        tiles[i] = tiles_of(len);
+        T += tiles[i];
+        bytes += (double)len * p->hkv * p->head_dim * 2.0 * p->elem_bytes;
+    }
+    int best = ng_max;
+    double best_us = 1e300;
+    for (int ng = ng_max; ng >= std::max(1, ng_max / 8); --ng) {
+        // most pieces of one row: the groups its first and last tile fall in
+        int pieces = 1;
+        if (T > 0) {
+            long long P = 0;
+            for (int i = 0; i < n; ++i) {
+                if (tiles[i] > 0) {
+                    const long long gf = ((P + 1) * ng - 1) / T;
+                    const long long gl = ((P + tiles[i]) * ng - 1) / T;
+                    pieces = std::max(pieces, (int)(gl - gf + 1));
+                }
+                P += tiles[i];
+            }
+        }
+        const double gbps = std::min(p->read_gbps, (double)ng * p->hkv * p->dev_cta_gbps);
+        double us = p->dev_fixed_us + bytes / (gbps * 1e3);
+        if (pieces >= 2) us += p->dev_merge_us + p->dev_merge_piece_us * pieces;
+        if (us < best_us) {
+            best_us = us;
+            best = ng;
+        }
+    }
+    if (est_us_out) *est_us_out = best_us;
+    return best;
 }
 
 }  // extern "C"

@@ -279,7 +279,7 @@ def paged_attention_workqueue_state(q_source, k_pages, v_pages, block_table, seq
 
 def paged_attention_auto(q_source, k_pages, v_pages, block_table, seq_lens, output, workspace,
                          q_indices=None, out_indices=None, merge_counters=None,
-                         plan=None) -> None:
+                         plan=None, groups: int = 0) -> None:
     """Paged decode with the device-side schedule (no work queue, no host builder).
 
     Row b attends to ``seq_lens[b]`` tokens of ``block_table[b]``, reads
@@ -288,7 +288,8 @@ def paged_attention_auto(q_source, k_pages, v_pages, block_table, seq_lens, outp
     ``[B, Hkv]``) selects the fused merge.  ``workspace`` needs
     ``auto_workspace_bytes(B, Hq, Hkv)`` bytes.  ``plan`` (optional) is a
     device int32 copy of ``scheduler.build_auto_plan`` for exactly this step's
-    metadata: the kernel then starts from it instead of deriving the schedule.
+    metadata: the kernel then starts from it instead of deriving the schedule;
+    ``groups`` is the group count the plan was built for (0: the maximum).
     No counterpart in the reference.
     """
     _check_tensor(q_source, "q_source", tuple(_DTYPES), 3)
@@ -325,7 +326,8 @@ def paged_attention_auto(q_source, k_pages, v_pages, block_table, seq_lens, outp
         _native.check(lib.pkv_paged_attention_auto_planned(
             q_source.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), block_table.data_ptr(),
             seq_lens.data_ptr(), ptrs[0], ptrs[1], output.data_ptr(), ws_ptr, ws_bytes, ctr,
-            plan.data_ptr(), plan.numel() * 4, b, q_source.size(0), output.size(0), hq, hkv, d,
+            plan.data_ptr(), plan.numel() * 4, int(groups), b, q_source.size(0), output.size(0),
+            hq, hkv, d,
             physical_pages,
             k_pages.size(2), block_table.size(1), _DTYPES[q_source.dtype], _stream()))
         return

@@ -110,6 +110,15 @@ class Router:
                                            ctypes.byref(splits), ctypes.byref(ms))
         return ROUTE_NAMES[route], int(splits.value), float(ms.value)
 
+    def choose_groups(self, lengths) -> tuple[int, float]:
+        """Group count of the device-side schedule for one step and its modelled
+        microseconds (``pkv_choose_groups``)."""
+        arr = _i32(lengths)
+        us = ctypes.c_double(0.0)
+        ng = self._lib.pkv_choose_groups(ctypes.byref(self.params), _ptr(arr), arr.size,
+                                         ctypes.byref(us))
+        return int(ng), float(us.value)
+
     # ---- work-queue builder (benchmark_serving_trace.py:686-703, clamped)
     def build_workqueue(self, seq_lens, active_count: int | None = None,
                         policy: str = "balanced", requested_splits: int = 0,
@@ -148,10 +157,11 @@ def plan_words(hkv: int, sm_count: int) -> int:
 
 def build_auto_plan(seq_lens, block_rows, max_pages: int, page_size: int, hkv: int,
                     sm_count: int, q_indices=None, out_indices=None,
-                    out: np.ndarray | None = None) -> np.ndarray:
+                    out: np.ndarray | None = None, groups: int = 0) -> np.ndarray:
     """Host plan of the device-side schedule for one step (``pkv_build_auto_plan``):
     the group entries ``pkv_paged_attention_auto_planned`` starts from.  ``block_rows``
-    is the host block table [B, width]; ``max_pages`` the launch's row count."""
+    is the host block table [B, width]; ``max_pages`` the launch's row count;
+    ``groups`` the schedule's group count (0: the maximum)."""
     lens = _i32(seq_lens)
     rows = np.ascontiguousarray(block_rows, dtype=np.int32)
     b = lens.size
@@ -164,5 +174,5 @@ def build_auto_plan(seq_lens, block_rows, max_pages: int, page_size: int, hkv: i
     _native.check(_native.load().pkv_build_auto_plan(
         _ptr(lens), _ptr(rows), b, rows.shape[1], None if qi is None else _ptr(qi),
         None if oi is None else _ptr(oi), int(max_pages), int(page_size), int(hkv),
-        int(sm_count), _ptr(plan), plan.size * 4))
+        int(sm_count), int(groups), _ptr(plan), plan.size * 4))
     return plan

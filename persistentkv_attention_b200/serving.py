@@ -48,6 +48,7 @@ class HostPlan:
     bucket: int
     tokens: int                # sum of seq_lens
     plan_words: int = 0        # host plan of the device-side schedule (0: none)
+    groups: int = 0            # the plan's group count (0: the maximum)
 
     def views(self, t: torch.Tensor):
         """Splits a (host or device) copy of the buffer into its fields."""
@@ -94,11 +95,14 @@ class DecodeEngine:
     def __init__(self, k_pages: torch.Tensor, v_pages: torch.Tensor, hq: int,
                  router: Router | None = None, policy: str = "device", fused: bool = True,
                  requested_splits: int = 0, kv_scales: tuple[float, float] | None = None,
-                 use_plan: bool = True):
+                 use_plan: bool = True, groups: int | str = "router"):
         """``kv_scales`` = (k_scale, v_scale) for ``torch.float8_e4m3fn`` pools
         (q and output are then fp16; device schedule only).  ``use_plan``: with
         the device schedule, each step carries a host plan of the schedule
-        (``scheduler.build_auto_plan``) uploaded with its other metadata."""
+        (``scheduler.build_auto_plan``) uploaded with its other metadata.
+        ``groups``: the device schedule's group count -- "router" (default) the
+        router's choice per step (``Router.choose_groups``), 0 the maximum (two
+        CTAs per SM), an int a fixed count; without a plan it is the maximum."""
         self.k_pages = k_pages
         self.v_pages = v_pages
         self.hq = hq
@@ -119,6 +123,11 @@ class DecodeEngine:
         self.requested_splits = requested_splits
         self.sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.use_plan = use_plan and policy == "device" and not self.kv8
+        if not self.use_plan:
+            if groups not in (0, "router"):
+                raise RuntimeError("a group count other than the maximum needs the host plan")
+            groups = 0
+        self.groups = groups
         self._workspace = torch.empty(0, device=self.device, dtype=torch.float32)
         self._counters = torch.zeros(0, device=self.device, dtype=torch.int32)
         # buffers replaced by a larger one stay alive: captured graphs may
@@ -147,8 +156,13 @@ class DecodeEngine:
         if out is None or out.numel() < size:
             out = torch.empty(size, dtype=torch.int32, pin_memory=True)
         buf = out[:size]
+        groups = 0
+        if pw and self.groups == "router":
+            groups = self.router.choose_groups(seq)[0]
+        elif pw:
+            groups = int(self.groups)
         plan = HostPlan(buf, b, mp, n_items, total_slots, int(seq.max(initial=1)),
-                        int(seq.sum()), pw)
+                        int(seq.sum()), pw, groups)
         v = plan.views(buf)
         v["block_table"].numpy()[:] = block_rows
         v["seq_lens"].numpy()[:] = seq
@@ -160,7 +174,7 @@ class DecodeEngine:
         if pw:
             build_auto_plan(seq, block_rows, mp, self.page_size, self.hkv, self.sm_count,
                             q_indices=v["q_indices"].numpy(), out_indices=v["out_indices"].numpy(),
-                            out=v["plan"].numpy())
+                            out=v["plan"].numpy(), groups=groups)
         return plan
 
     def _auto_groups(self) -> int:
@@ -212,7 +226,7 @@ class DecodeEngine:
             ops.paged_attention_auto(
                 q_source, self.k_pages, self.v_pages, f["block_table"], f["seq_lens"], out,
                 self._workspace, f["q_indices"], f["out_indices"],
-                counters if self.fused else None, plan=f.get("plan"))
+                counters if self.fused else None, plan=f.get("plan"), groups=plan.host.groups)
             return
         ops.paged_attention_workqueue(
             q_source, self.k_pages, self.v_pages, f["block_table"], f["seq_lens"],

@@ -707,3 +707,39 @@ def test_planned_schedule_bit_identical(g, dtype, page):
     torch.cuda.synchronize()
     assert _native.device_error(clear=True) & 0x4
     assert torch.equal(out[rows], outs[0][rows])
+
+
+@pytest.mark.parametrize("groups", [1, 6, 18, 36])
+def test_planned_fewer_groups(groups):
+    """A plan for fewer groups than the maximum (a router's choice): a grid of
+    groups x Hkv CTAs, same result as the oracle; the engine's router route."""
+    from persistentkv_attention_b200.scheduler import build_auto_plan
+    from persistentkv_attention_b200.serving import DecodeEngine
+
+    lens = [0, 33, 9000, 4096, 700, 12000, 1]
+    c = make_case(lens, seed=500 + groups, indexed=True)
+    d = c.cuda()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    plan = torch.from_numpy(build_auto_plan(c.seq_lens, c.block_table, c.block_table.shape[1],
+                                            16, 8, sms, q_indices=c.q_indices,
+                                            out_indices=c.out_indices, groups=groups)).cuda()
+    for fused in (True, False):
+        ws = torch.empty(ops.auto_workspace_bytes(len(lens), 32, 8) // 4, device="cuda")
+        out = torch.full((c.out_rows, 32, 128), float("nan"), device="cuda", dtype=torch.float16)
+        ctr = torch.zeros(len(lens), 8, device="cuda", dtype=torch.int32)
+        ops.paged_attention_auto(d["q_source"], d["k_pages"], d["v_pages"], d["block_table"],
+                                 d["seq_lens"], out, ws, d["q_indices"], d["out_indices"],
+                                 ctr if fused else None, plan=plan, groups=groups)
+        torch.cuda.synchronize()
+        assert (ctr == 0).all()
+        assert_close(out, c.oracle(), "f16", f"groups={groups} fused={fused}")
+    engine = DecodeEngine(d["k_pages"], d["v_pages"], 32, groups="router")
+    step = engine.upload(engine.plan_step(c.seq_lens, c.block_table,
+                                          q_indices=np.arange(len(lens))))
+    assert 1 <= step.host.groups <= 37
+    out = torch.full((len(lens), 32, 128), float("nan"), device="cuda", dtype=torch.float16)
+    engine.run(step, d["q_source"], out)
+    torch.cuda.synchronize()
+    want = po.paged_decode(c.q_source.float().numpy(), c.k_pages.float().numpy(),
+                           c.v_pages.float().numpy(), c.block_table, seq_lens=c.seq_lens)
+    assert_close(out, want, "f16", "router groups")
