@@ -864,6 +864,11 @@ pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* 
         ls.dp.plan = static_cast<const int32_t*>(plan);
     }
     ls.pdl = pdl;
+    // The lean kernel: a host plan, the fused merge deferred to the CTA's end
+    // (a row's NG * G merge weights fit the CTA's buffer), output rows.
+    ls.lean = plan != nullptr && state_out == nullptr && xg == nullptr &&
+              merge_counters != nullptr && output != nullptr && kv8_scales == nullptr &&
+              NG * (Hq / Hkv) <= pkv::kMergeWeights;
     if (kv8_scales != nullptr) {
         ls.kv8 = true;
         ls.dp.scale_log2 *= kv8_scales[0];

@@ -1197,7 +1197,15 @@ __device__ __forceinline__ void expand_e4m3_chunk(uint8_t* half_base, int q, uin
 // each consumer warp expands its stage to the 16-bit layout in place and the
 // math below is unchanged (the K scale is folded into scale_log2, the V scale
 // is applied to each item's state).  q and output stay 16-bit.
-template <int G, typename T, int BOX_ROWS, int NSLOTS, int LOAD, bool KV8 = false>
+// LEAN: the engine's step route only -- device-side schedule from a host
+// plan, fused merge deferred to the CTA's end (merge_bulk), output rows
+// written directly; no work queue, rectangular grid, state output or peer
+// exchange.  The host dispatches it only when those conditions hold
+// (pkv_api.cu).  Compiling the other routes out shortens the code the CTA
+// runs once per launch (schedule, first item, item ends, merge), whose
+// instruction fetches miss every cache after an L2 flush.
+template <int G, typename T, int BOX_ROWS, int NSLOTS, int LOAD, bool KV8 = false,
+          bool LEAN = false>
 __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     pkv_decode_kernel(const __grid_constant__ DecodeParams p,
                       const __grid_constant__ CUtensorMap tmap_k,
@@ -1205,6 +1213,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     static_assert(G == 1 || G == 2 || G == 4 || G == 8, "G must be 1, 2, 4 or 8");
     static_assert(BOX_ROWS == 8 || BOX_ROWS == 16, "box rows must be 8 or 16");
     static_assert(!KV8 || (LOAD == kLoadCpAsync && sizeof(T) == 2), "e4m3 K/V: cp.async only");
+    static_assert(!(LEAN && KV8), "the lean route serves 16-bit pools");
     constexpr int kBoxesPerStage = kStageTokens / BOX_ROWS;
     static_assert(kPlanPages % kBoxesPerStage == 0, "a plan's first batch is whole stages");
     constexpr int kBoxBytes = BOX_ROWS * kHalfRowBytes;
@@ -1257,13 +1266,15 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     __shared__ int s_my_items;
     if (warp == kConsumerWarps) {
         int mine;
-        const bool planned = p.auto_groups > 0 && p.plan != nullptr &&
-                             plan_init<BOX_ROWS>(p, lane, acur, first_item, first_pid0, lane == 0);
+        const bool planned =
+            LEAN ? plan_init<BOX_ROWS>(p, lane, acur, first_item, first_pid0, lane == 0)
+                 : (p.auto_groups > 0 && p.plan != nullptr &&
+                    plan_init<BOX_ROWS>(p, lane, acur, first_item, first_pid0, lane == 0));
         if (planned) {
             // the plan's first item is built: the cursor stands on the next row
             mine = acur.b >= 0 ? acur.b_end - (acur.b - 1) : 0;
             first_width = kPlanPages;
-        } else if (p.auto_groups > 0) {
+        } else if (LEAN || p.auto_groups > 0) {
             acur = auto_init(p, lane);
             mine = acur.b >= 0 ? acur.b_end - acur.b : 0;
         } else {
@@ -1275,7 +1286,12 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
             PKV_STAMP(p, 1);
             PKV_CLOCK_STAMP(p, 13, t_entry);
         }
-        if (mine > 0 && !planned) first_item = producer_next<BOX_ROWS>(p, 0, lane, first_pid0, acur);
+        if (mine > 0 && !planned) {
+            // a plan that is not this launch's (flagged) falls back to the
+            // schedule derived on the device
+            first_item = LEAN ? auto_item<BOX_ROWS>(p, acur, lane, lane == 0, first_pid0)
+                              : producer_next<BOX_ROWS>(p, 0, lane, first_pid0, acur);
+        }
         if (lane == 0) {
             s_my_items = mine;
             PKV_CLOCK_STAMP(p, 14, t_entry);
@@ -1496,10 +1512,13 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                 }
                 if (!fetched) {
                     fetched = true;
-                    nxt = producer_next<BOX_ROWS>(p, s + 1, lane, nxt_pid0, acur);
+                    nxt = LEAN ? auto_item<BOX_ROWS>(p, acur, lane, lane == 0, nxt_pid0)
+                               : producer_next<BOX_ROWS>(p, s + 1, lane, nxt_pid0, acur);
                 }
             }
-            if (!fetched) nxt = producer_next<BOX_ROWS>(p, s + 1, lane, nxt_pid0, acur);
+            if (!fetched)
+                nxt = LEAN ? auto_item<BOX_ROWS>(p, acur, lane, lane == 0, nxt_pid0)
+                           : producer_next<BOX_ROWS>(p, s + 1, lane, nxt_pid0, acur);
             cur = nxt;
             pid0 = nxt_pid0;
         }
@@ -1532,9 +1551,9 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     bool aborted = false;
     // step number of a sharded launch: advanced only after every CTA of the
     // launch has finished, so all CTAs read the same value here
-    const unsigned xg_epoch = p.xg_world > 0 ? ld_relaxed_gpu_u32(p.xg_counters) : 0u;
-    const bool state_mode = p.state_out != nullptr;
-    const bool xg_mode = p.xg_world > 0;
+    const unsigned xg_epoch = (!LEAN && p.xg_world > 0) ? ld_relaxed_gpu_u32(p.xg_counters) : 0u;
+    const bool state_mode = !LEAN && p.state_out != nullptr;
+    const bool xg_mode = !LEAN && p.xg_world > 0;
     long long stamp_tokens = 0;  // diagnostic build: tokens this CTA streamed
     int n_pend = 0;              // deferred merges (uniform across consumer threads)
     int pend_old = 0;            // thread 0: result of the latest deferred counter add
@@ -1768,7 +1787,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
         consumer_bar_sync();
         if (threadIdx.x == 0) PKV_STAMP(p, 5);
 
-        const bool rect = p.work_items == nullptr && p.auto_groups == 0;
+        const bool rect = !LEAN && p.work_items == nullptr && p.auto_groups == 0;
         const bool direct = it.row_splits == 1;
         const bool write_direct_out = direct && !state_mode && !xg_mode && it.out_row >= 0 &&
                                       (!rect || it.tok_end > it.tok_begin);
@@ -1821,7 +1840,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
             }
         }
         if (xg_direct) xg_collect<G, T>(p, it.row, it.kvh, it.out_row, xs, s_flags);
-        if (!direct && it.slot >= 0 && p.merge_counters != nullptr && !rect) {
+        if (!direct && it.slot >= 0 && (LEAN || p.merge_counters != nullptr) && !rect) {
             // fused merge: the last task of this (row, kvh) merges all of the
             // row's slots (reference cuh:648-716)
             int32_t* ctr = p.merge_counters + (size_t)it.row * p.Hkv + it.kvh;
@@ -1842,6 +1861,10 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                     pend_old = atom_add_acq_rel_gpu(ctr, 1);
                 }
                 ++n_pend;
+            } else if constexpr (LEAN) {
+                // a group holds at most two split rows (its first and its
+                // last), so the pending list never fills on this route
+                if (threadIdx.x == 0) raise_error(p.error, kErrSlot);
             } else {
                 // immediate: the sharded exchange (its peers wait for the
                 // row), or the pending list is full
@@ -1907,6 +1930,9 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
             if (pe.n * G <= kMergeWeights) {
                 merge_bulk<G, T>(p, pe, ring, (uint32_t)merge_region_bytes<G, NSLOTS>(), s_mw,
                                  merge_bar, merge_phase, s_flags);
+            } else if constexpr (LEAN) {
+                // the host dispatches this route only when NG * G fits
+                if (threadIdx.x == 0) raise_error(p.error, kErrSlot);
             } else {
                 // more slots than the weight buffer holds: the chunked merge
                 MergeSmem ms{s_mw, s_mw + kMergeChunk * 8, s_merge};
@@ -1927,7 +1953,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
             }
         }
     }
-    if (p.xg_world > 0) {
+    if (!LEAN && p.xg_world > 0) {
         // the last CTA to finish advances the step number for the next launch
         consumer_bar_sync();
         if (threadIdx.x == 0) {

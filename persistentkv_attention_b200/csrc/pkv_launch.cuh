@@ -29,6 +29,7 @@ struct LaunchSpec {
     bool merge;        // run the separate merge kernel after decode (pkv_api.cu)
     bool pdl = false;  // decode may launch early behind the previous kernel (it waits on it)
     bool kv8 = false;  // e4m3 K/V pools (cp.async producer)
+    bool lean = false; // the planned step route (pkv_decode_kernel's LEAN form)
     int load = pkv::kLoadCpAsync;  // gather: pkv::kLoadTma or pkv::kLoadCpAsync
     int G;
     int box_rows;
@@ -43,11 +44,11 @@ struct LaunchSpec {
 // diagnostics).
 extern thread_local int t_last_grid;
 
-template <int G, typename T, int BR, int LOAD, bool KV8>
+template <int G, typename T, int BR, int LOAD, bool KV8, bool LEAN>
 pkv_status launch_typed(const LaunchSpec& ls, const CUtensorMap& tk, const CUtensorMap& tv,
                         cudaStream_t stream) {
     using namespace pkv;
-    auto kern = pkv_decode_kernel<G, T, BR, kSlots, LOAD, KV8>;
+    auto kern = pkv_decode_kernel<G, T, BR, kSlots, LOAD, KV8, LEAN>;
     const size_t smem = decode_smem_bytes<G, kSlots>();
     // the device schedule's grid (2 CTAs per SM) must be resident in one wave
     static_assert(decode_fits_two_per_sm<G, kSlots>(), "decode CTA too large for 2 per SM");
@@ -113,8 +114,9 @@ pkv_status launch_typed(const LaunchSpec& ls, const CUtensorMap& tk, const CUten
     return ok();
 }
 
-// The four G values of one (dtype, box rows, gather, e4m3) configuration;
-// defined (and instantiated) in the pkv_inst_*.cu files.
+// The four G values of one (dtype, box rows, gather, e4m3) configuration,
+// each in its general and (16-bit pools) its lean form; defined (and
+// instantiated) in the pkv_inst_*.cu files.
 template <typename T, int BR, int LOAD, bool KV8>
 pkv_status launch_g(const LaunchSpec& ls, const CUtensorMap& tk, const CUtensorMap& tv,
                     cudaStream_t s);
@@ -123,11 +125,16 @@ pkv_status launch_g(const LaunchSpec& ls, const CUtensorMap& tk, const CUtensorM
     template <>                                                                                   \
     pkv_status launch_g<T, BR, LOAD, KV8>(const LaunchSpec& ls, const CUtensorMap& tk,          \
                                           const CUtensorMap& tv, cudaStream_t s) {              \
+        const bool lean = ls.lean && !KV8;                                                        \
         switch (ls.G) {                                                                           \
-            case 1: return launch_typed<1, T, BR, LOAD, KV8>(ls, tk, tv, s);                     \
-            case 2: return launch_typed<2, T, BR, LOAD, KV8>(ls, tk, tv, s);                     \
-            case 4: return launch_typed<4, T, BR, LOAD, KV8>(ls, tk, tv, s);                     \
-            case 8: return launch_typed<8, T, BR, LOAD, KV8>(ls, tk, tv, s);                     \
+            case 1: return lean ? launch_typed<1, T, BR, LOAD, KV8, !KV8>(ls, tk, tv, s)          \
+                                : launch_typed<1, T, BR, LOAD, KV8, false>(ls, tk, tv, s);        \
+            case 2: return lean ? launch_typed<2, T, BR, LOAD, KV8, !KV8>(ls, tk, tv, s)          \
+                                : launch_typed<2, T, BR, LOAD, KV8, false>(ls, tk, tv, s);        \
+            case 4: return lean ? launch_typed<4, T, BR, LOAD, KV8, !KV8>(ls, tk, tv, s)          \
+                                : launch_typed<4, T, BR, LOAD, KV8, false>(ls, tk, tv, s);        \
+            case 8: return lean ? launch_typed<8, T, BR, LOAD, KV8, !KV8>(ls, tk, tv, s)          \
+                                : launch_typed<8, T, BR, LOAD, KV8, false>(ls, tk, tv, s);        \
             default: return fail_fmt(PKV_ERR_UNSUPPORTED, "unsupported G=%d", ls.G);             \
         }                                                                                         \
     }
