@@ -101,7 +101,9 @@ def test_bf16_quantize_round_to_nearest_even():
 def test_torch_repack_forms_match_numpy_oracle():
     """The repack + SDPA forms (benchmark_torch_paged_sdpa.py:90-109) agree
     with the numpy oracle: torch's fp32 SDPA (the CPU baseline) to fp32
-    rounding, the float64 checker to 1e-12."""
+    rounding, the float64 checker to 1e-9 (the numpy oracle keeps the
+    reference's ``/(l + 1e-8)`` normalisation, the torch checker divides by l:
+    they differ by o * 1e-8 / l, l >= 1)."""
     import torch
 
     rng = np.random.default_rng(11)
@@ -114,7 +116,7 @@ def test_torch_repack_forms_match_numpy_oracle():
     want = po.paged_decode(q, kp, vp, table, seq_lens=seq)
     got64 = po.torch_paged_decode(torch.from_numpy(q), torch.from_numpy(kp),
                                   torch.from_numpy(vp), table, seq)
-    assert np.abs(got64.numpy() - want).max() < 1e-12
+    assert np.abs(got64.numpy() - want).max() < 1e-9
     kt, vt = torch.from_numpy(kp), torch.from_numpy(vp)
     for r in (0, 2):
         n = int(seq[r])
