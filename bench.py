@@ -337,7 +337,7 @@ class Config:
     distinct step, and its timed run."""
 
     def __init__(self, name, args, dev, stream, rank, hkv=None, dtype="f16", kv_fp8=False,
-                 steps=None, groups=0, layers=1):
+                 steps=None, groups="router", layers=1):
         from persistentkv_attention_b200.serving import DecodeEngine
 
         self.name = name
@@ -486,7 +486,7 @@ def e2e_measure(cfg, flush, barrier, args):
     host_rows = []
     for p, state in zip(cfg.plans, cfg.trace_steps):
         v = p.host.views(p.host.buf)
-        host_rows.append((list(state.lengths), v["block_table"].numpy().copy(),
+        host_rows.append((np.asarray(state.lengths, np.int32), v["block_table"].numpy().copy(),
                           torch.stack([q_host[r] for r in state.active_ids]).pin_memory()))
     engine.reserve_host(scratch, max(len(r[0]) for r in host_rows),
                         max(r[1].shape[1] for r in host_rows))

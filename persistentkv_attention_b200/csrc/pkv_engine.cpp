@@ -70,7 +70,7 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 struct pkv_engine {
     const void* k_pages;
     const void* v_pages;
-    int physical_pages, hq, hkv, page_size, max_batch, max_pages, device;
+    int physical_pages, hq, hkv, page_size, max_batch, max_pages, device, sm_count;
     pkv_dtype dtype;
     size_t elem;
     // device: staged metadata, staged q rows, workspace, merge counters
@@ -123,6 +123,11 @@ pkv_status pkv_engine_create(const void* k_pages, const void* v_pages, int physi
     e->dtype = dtype;
     e->elem = 2;
     cudaGetDevice(&e->device);
+    if (cudaDeviceGetAttribute(&e->sm_count, cudaDevAttrMultiProcessorCount, e->device) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        e->sm_count = 0;  // the planner asks the current device itself
+    }
     e->sl_words = align_up((size_t)max_batch, 4);
     e->plan_words = align_up(pkv_auto_plan_bytes(Hkv, 0) / sizeof(int32_t), 4);
     const size_t meta_bytes = align_up(
@@ -213,7 +218,7 @@ pkv_status pkv_engine_step_host(pkv_engine* e, const int32_t* seq_lens,
     std::memcpy(h, seq_lens, (size_t)B * sizeof(int32_t));
     // the schedule, planned here from the host rows (the device starts from it)
     pkv_status pst = pkv_build_auto_plan(seq_lens, block_table, B, row_pages, nullptr, nullptr,
-                                         e->max_pages, e->page_size, e->hkv, 0, 0,
+                                         e->max_pages, e->page_size, e->hkv, e->sm_count, 0,
                                          h + e->sl_words, e->plan_words * sizeof(int32_t));
     if (pst != PKV_OK) return efail(pst, "planning the step failed");
     int32_t* rows = h + e->sl_words + e->plan_words;

@@ -419,8 +419,18 @@ pkv_status pkv_build_auto_plan(const int32_t* seq_lens, const int32_t* block_tab
     if (plan_bytes < (size_t)(kPlanHeaderWords + (size_t)NG * kPlanEntryWords) * sizeof(int32_t))
         return PKV_ERR_CAPACITY;
     const long long limit = (long long)max_pages * page_size;
-    std::vector<long long> P(B), O(B);
-    std::vector<int> n(B), gf(B), gl(B), seq(B);
+    // per-row scratch, kept by the calling thread: a step's plan is built on
+    // the host call's critical path, so no allocation once the batch fits
+    thread_local std::vector<long long> P, O;
+    thread_local std::vector<int> n, gf, gl, seq;
+    if ((int)P.size() < B) {
+        P.resize(B);
+        O.resize(B);
+        n.resize(B);
+        gf.resize(B);
+        gl.resize(B);
+        seq.resize(B);
+    }
     long long T = 0;
     for (int b = 0; b < B; ++b) {
         if (seq_lens[b] < 0 || seq_lens[b] > limit) return PKV_ERR_INVALID_ARGUMENT;
