@@ -361,10 +361,15 @@ class NativeEngine:
 
     def step(self, seq: np.ndarray, rows: np.ndarray, q_host: torch.Tensor,
              out_host: torch.Tensor) -> tuple[int, int]:
-        self._check(self._step(
-            self._ptr, seq.ctypes.data, rows.ctypes.data, rows.shape[0], rows.shape[1],
-            q_host.data_ptr(), out_host.data_ptr(), _stream(), self._h2d_ref, self._d2h_ref))
-        return int(self._h2d.value), int(self._d2h.value)
+        # the arrays' addresses through the array interface: ``ndarray.ctypes``
+        # builds a helper object per access, a measurable share of a step
+        st = self._step(
+            self._ptr, seq.__array_interface__["data"][0], rows.__array_interface__["data"][0],
+            rows.shape[0], rows.shape[1], q_host.data_ptr(), out_host.data_ptr(), _stream(),
+            self._h2d_ref, self._d2h_ref)
+        if st != 0:
+            self._check(st)
+        return self._h2d.value, self._d2h.value
 
     def close(self) -> None:
         if self._ptr:
