@@ -1018,6 +1018,20 @@ def run_phase_stamps(args) -> None:
             "median_over_steps": {".".join(k): med(k) for k in keys}}
         cfg.release()
         torch.cuda.empty_cache()
+    # the floor under any step: the event interval of a (nearly) empty one-CTA
+    # kernel launched after the same flush
+    floor = []
+    with torch.cuda.stream(stream):
+        for i in range(20):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            flush(i)
+            a.record(stream)
+            torch.cuda._sleep(0)
+            b.record(stream)
+            floor.append((a, b))
+    torch.cuda.synchronize()
+    report["empty_launch_floor_us"] = float(np.median([1000.0 * a.elapsed_time(b)
+                                                       for a, b in floor]))
     print(json.dumps(report, indent=1), flush=True)
 
 
