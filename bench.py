@@ -4,7 +4,8 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
                     [--impl engine|reference] [--trace-file FILE]
                     [--hkv 32|8|4] [--dtype f16|bf16] [--kv-fp8]
-                    [--gather cpasync|tma] [--no-per-config] [--phase-stamps]
+                    [--gather cpasync|tma] [--math mma|fma] [--no-per-config]
+                    [--phase-stamps]
                     [--seq-shard [--exchange fused|nccl]]
 
 A step is one continuous-batching decode step of a seeded synthetic trace
@@ -26,9 +27,11 @@ Reported (one JSON line on rank 0):
               the split of one step into host call, interval and decode;
   roofline    algorithmic K/V bytes per step / step interval vs the measured
               HBM copy bandwidth;
-  per_config  configs 1 and 3-5 (and the default config with the other
-              gather) measured in the same run, same timing method, each
-              with its correctness gate on every row of one step;
+  per_config  configs 1 and 3-5, the default config with the other gather,
+              the default config and config 5 with CUDA-core math (fp32 FMA
+              instead of mma.sync), and 8 model layers back to back, measured
+              in the same run, same timing method, each with its correctness
+              gate on every row of one step;
   cpu_baseline the reference's torch CPU repack + SDPA path
               (tests/benchmark_torch_paged_sdpa.py:90-109) on the host cores,
               bounded sample, with the reference's own cpu_gqa_attention
@@ -546,6 +549,7 @@ def run_engine_arm(args) -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
     _native.set_gather_mode(args.gather)
+    _native.set_math_mode(args.math)
     flush = L2Flush(dev)
     stream = torch.cuda.Stream(dev)
     clocks = ClockSampler(local)
@@ -613,6 +617,22 @@ def run_engine_arm(args) -> None:
         cfg.release()
         _native.set_gather_mode(args.gather)
         per_config[f"{args.workload}@gather={args.gather}"] = main_summary
+        # tensor cores (mma.sync) against CUDA cores (fp32 FMA) for the
+        # consumer math at G = 4, on the latency-bound default config and the
+        # streaming-bound config 5
+        if args.math == "mma" and args.dtype == "f16" and not args.kv_fp8 and \
+                (args.hkv or 8) == 8:
+            _native.set_math_mode("fma")
+            for name in (args.workload, "zipf_b64"):
+                cfg = Config(name, args, dev, stream, rank, dtype=args.dtype,
+                             steps=min(args.steps, 20))
+                cfg.timed(flush, barrier, clocks)
+                err = cfg.gate()
+                per_config[f"{name}@math=fma"] = dict(cfg.summary(peak),
+                                                      correctness_max_abs_err=err)
+                cfg.release()
+                torch.cuda.empty_cache()
+            _native.set_math_mode("mma")
         # back to back: one interval covers a step of LAYERS model layers, each
         # with its own K/V pool (inputs far larger than L2, no flush between
         # the layers), reported per layer
@@ -673,6 +693,7 @@ def run_engine_arm(args) -> None:
                         "step's metadata; group count per step from the calibrated router "
                         f"(used: {main.groups_used()})",
             "gather": args.gather,
+            "math": args.math,
         },
         "hbm_gbs": achieved, "hbm_frac_of_8tbs": achieved / 8000.0,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -1053,6 +1074,9 @@ def main() -> None:
     ap.add_argument("--gather", choices=["cpasync", "tma"], default="cpasync",
                     help="decode gather of 16-bit pools (pkv_set_gather_mode)")
     ap.add_argument("--no-fused", action="store_true", help="separate PDL merge kernel")
+    ap.add_argument("--math", choices=["mma", "fma"], default="mma",
+                    help="consumer math: tensor cores (mma.sync) or CUDA cores (fp32 FMA; lean "
+                         "fp16 route at G = 4)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-per-config", action="store_true",
                     help="time only --workload (no per_config / seq_shard sub-objects)")

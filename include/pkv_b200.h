@@ -91,6 +91,24 @@ typedef enum pkv_gather {
 pkv_status pkv_set_gather_mode(pkv_gather mode);
 pkv_gather pkv_get_gather_mode(void);
 
+/* Where the decode kernel's consumer warps do the QK and PV products.  The
+ * north star allows tensor cores only where they beat CUDA cores at G >= 4;
+ * this switch measures that.  The reference uses WMMA for G == 4 and scalar
+ * FMA loops otherwise (kernels/persistentkv_attention.cuh:422-449, :519-598). */
+typedef enum pkv_math {
+    /* mma.sync.m16n8k16 tiles, fp32 accumulation (the default, every route). */
+    PKV_MATH_MMA = 0,
+    /* fp32 FMA on CUDA cores.  Served by the lean fp16 cp.async route at
+     * G = 4 (the engine's step route: host plan, fused merge, output rows);
+     * every other launch keeps the tensor-core path. */
+    PKV_MATH_FMA = 1
+} pkv_math;
+
+/* Selects the math of every later eligible decode launch in this process;
+ * launches already captured in a CUDA graph keep theirs. */
+pkv_status pkv_set_math_mode(pkv_math mode);
+pkv_math pkv_get_math_mode(void);
+
 /* Diagnostic build only (libpkv_b200_stamps.so, compiled with
  * PKV_PHASE_STAMPS): copies the per-CTA %globaltimer stamps of the last
  * decode launch on this thread -- PKV_STAMPS_PER_CTA values per CTA:

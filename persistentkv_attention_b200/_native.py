@@ -94,6 +94,8 @@ SIGNATURES = {
     "pkv_last_error_message": (c_char_p, []),
     "pkv_set_gather_mode": (c_int, [c_int]),
     "pkv_get_gather_mode": (c_int, []),
+    "pkv_set_math_mode": (c_int, [c_int]),
+    "pkv_get_math_mode": (c_int, []),
     "pkv_phase_stamps": (c_int, [POINTER(ctypes.c_uint64), c_int, POINTER(c_int)]),
     "pkv_paged_attention": (
         c_int,
@@ -254,6 +256,20 @@ def set_gather_mode(mode: str) -> None:
 def gather_mode() -> str:
     value = load().pkv_get_gather_mode()
     return {v: k for k, v in GATHER_MODES.items()}[value]
+
+
+MATH_MODES = {"mma": 0, "fma": 1}
+
+
+def set_math_mode(mode: str) -> None:
+    """Consumer math of later decode launches: "mma" (tensor cores, the
+    default) or "fma" (CUDA cores; lean fp16 cp.async route at G = 4)."""
+    check(load().pkv_set_math_mode(MATH_MODES[mode]))
+
+
+def math_mode() -> str:
+    value = load().pkv_get_math_mode()
+    return {v: k for k, v in MATH_MODES.items()}[value]
 
 
 def phase_stamps(max_ctas: int = 4096):

@@ -64,6 +64,7 @@ pkv_status ok_status() {
 static_assert((int)PKV_GATHER_TMA == kLoadTma && (int)PKV_GATHER_CP_ASYNC == kLoadCpAsync,
               "gather enum values are the kernel's LOAD template values");
 std::atomic<int> g_gather_mode{PKV_GATHER_DEFAULT};
+std::atomic<int> g_math_mode{PKV_MATH_MMA};
 
 }  // namespace
 
@@ -349,6 +350,7 @@ pkv_status launch(LaunchSpec& ls, void* stream_ptr) {
     ls.dp.stamps = ds->stamps;
     ls.sm_count = ds->sm_count;
     ls.load = ls.kv8 ? kLoadCpAsync : g_gather_mode.load(std::memory_order_relaxed);
+    ls.fma = g_math_mode.load(std::memory_order_relaxed) == PKV_MATH_FMA;
     CUtensorMap tk, tv;
     std::memset(&tk, 0, sizeof(tk));
     std::memset(&tv, 0, sizeof(tv));
@@ -584,6 +586,17 @@ pkv_status pkv_set_gather_mode(pkv_gather mode) {
 
 pkv_gather pkv_get_gather_mode(void) {
     return (pkv_gather)g_gather_mode.load(std::memory_order_relaxed);
+}
+
+pkv_status pkv_set_math_mode(pkv_math mode) {
+    if (mode != PKV_MATH_MMA && mode != PKV_MATH_FMA)
+        return fail(PKV_ERR_INVALID_ARGUMENT, "unknown math mode %d", (int)mode);
+    g_math_mode.store((int)mode, std::memory_order_relaxed);
+    return ok_status();
+}
+
+pkv_math pkv_get_math_mode(void) {
+    return (pkv_math)g_math_mode.load(std::memory_order_relaxed);
 }
 
 pkv_status pkv_phase_stamps(uint64_t* out, int max_ctas, int* n_ctas) {

@@ -25,6 +25,8 @@
 //    resident grid; every wait is bounded and every index is checked.
 #pragma once
 
+#include <type_traits>
+
 #include "pkv_device.cuh"
 
 namespace pkv {
@@ -1169,6 +1171,105 @@ __device__ __forceinline__ void merge_bulk(const DecodeParams& p, const PendingM
     consumer_bar_sync();
 }
 
+// ------------------------------------------------------- CUDA-core stage (G = 4)
+// The same 16-token stage as the mma.sync path, on the FMA pipes only, for
+// the tensor-core versus CUDA-core comparison (pkv_set_math_mode).  Lane l
+// owns dims 4l .. 4l + 3 (one 8-byte part of a 16-byte chunk of one
+// swizzled half-row).  S: each lane forms its 4-dim partial products for
+// all 16 tokens x 4 heads, then a reduce-scatter across the warp leaves lane
+// l the full scores of token l >> 1, heads 2 (l & 1) and 2 (l & 1) + 1.
+// Online softmax on those; P.V: each lane accumulates its 4 dims of the 4
+// heads over the 16 tokens, the probabilities broadcast by shuffles.
+struct FmaState {
+    float q[4][4];    // this lane's 4 dims of the 4 heads
+    float m[2];       // running max (log2 domain) of the lane's two heads
+    float l[2];       // partial sum over the lane's tokens, reduced at item end
+    float acc[4][4];  // [head][dim]
+};
+
+__device__ __forceinline__ float2 half2_to_float2(uint32_t x) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&x));
+}
+
+__device__ __forceinline__ void fma_stage(FmaState& f, const uint8_t* sbase, int lane, int valid,
+                                          float scale_log2) {
+    const int fh = lane >> 4;
+    const int fc = (lane >> 1) & 7;
+    const uint8_t* kb = sbase + fh * (kStageTokens * kHalfRowBytes) + (lane & 1) * 8;
+    const uint8_t* vb = kb + 2 * kStageTokens * kHalfRowBytes;
+    float part[64];  // [token][head]
+#pragma unroll
+    for (int t = 0; t < kStageTokens; ++t) {
+        const uint2 kr = *reinterpret_cast<const uint2*>(kb + t * kHalfRowBytes + ((fc ^ (t & 7)) << 4));
+        const float2 k01 = half2_to_float2(kr.x);
+        const float2 k23 = half2_to_float2(kr.y);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            part[t * 4 + g] = fmaf(f.q[g][3], k23.y,
+                                   fmaf(f.q[g][2], k23.x, fmaf(f.q[g][1], k01.y, f.q[g][0] * k01.x)));
+        }
+    }
+#pragma unroll
+    for (int lvl = 0; lvl < 5; ++lvl) {
+        const int off = 16 >> lvl;
+        const int half = 32 >> lvl;
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float send = upper ? part[i] : part[i + half];
+            const float keep = upper ? part[i + half] : part[i];
+            part[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+    }
+    const bool tok_ok = (lane >> 1) < valid;
+    const float sc0 = tok_ok ? part[0] * scale_log2 : -INFINITY;
+    const float sc1 = tok_ok ? part[1] * scale_log2 : -INFINITY;
+    float mx0 = sc0, mx1 = sc1;
+#pragma unroll
+    for (int off = 2; off < 32; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float mn0 = fmaxf(f.m[0], mx0);
+    const float mn1 = fmaxf(f.m[1], mx1);
+    const float c0 = fast_exp2(f.m[0] - mn0);
+    const float c1 = fast_exp2(f.m[1] - mn1);
+    f.m[0] = mn0;
+    f.m[1] = mn1;
+    const float p0 = fast_exp2(sc0 - mn0);
+    const float p1 = fast_exp2(sc1 - mn1);
+    f.l[0] = f.l[0] * c0 + p0;
+    f.l[1] = f.l[1] * c1 + p1;
+    // the other pair of heads' corrections sit in the neighbouring lane
+    const float o0 = __shfl_xor_sync(0xffffffffu, c0, 1);
+    const float o1 = __shfl_xor_sync(0xffffffffu, c1, 1);
+    const bool odd = (lane & 1) != 0;
+    const float corr[4] = {odd ? o0 : c0, odd ? o1 : c1, odd ? c0 : o0, odd ? c1 : o1};
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) f.acc[g][j] *= corr[g];
+    }
+#pragma unroll
+    for (int t = 0; t < kStageTokens; ++t) {
+        const float pa = __shfl_sync(0xffffffffu, p0, 2 * t);
+        const float pb = __shfl_sync(0xffffffffu, p1, 2 * t);
+        const float pc = __shfl_sync(0xffffffffu, p0, 2 * t + 1);
+        const float pd = __shfl_sync(0xffffffffu, p1, 2 * t + 1);
+        const uint2 vr = *reinterpret_cast<const uint2*>(vb + t * kHalfRowBytes + ((fc ^ (t & 7)) << 4));
+        const float2 v01 = half2_to_float2(vr.x);
+        const float2 v23 = half2_to_float2(vr.y);
+        const float pt[4] = {pa, pb, pc, pd};
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            f.acc[g][0] = fmaf(pt[g], v01.x, f.acc[g][0]);
+            f.acc[g][1] = fmaf(pt[g], v01.y, f.acc[g][1]);
+            f.acc[g][2] = fmaf(pt[g], v23.x, f.acc[g][2]);
+            f.acc[g][3] = fmaf(pt[g], v23.y, f.acc[g][3]);
+        }
+    }
+}
+
 // 16 e4m3 values (elements [16c, 16c + 16) of token t, chunk q = 8t + c of a
 // row-major e4m3 stage) to fp16, stored as two 16-byte chunks of the stage's
 // swizzled 16-bit layout (lo / hi half of 64 elements, 128-byte rows).
@@ -1204,8 +1305,10 @@ __device__ __forceinline__ void expand_e4m3_chunk(uint8_t* half_base, int q, uin
 // (pkv_api.cu).  Compiling the other routes out shortens the code the CTA
 // runs once per launch (schedule, first item, item ends, merge), whose
 // instruction fetches miss every cache after an L2 flush.
+// FMA: the consumer warps compute on CUDA cores (fma_stage) instead of
+// mma.sync; lean fp16 cp.async route at G = 4 only (pkv_set_math_mode).
 template <int G, typename T, int BOX_ROWS, int NSLOTS, int LOAD, bool KV8 = false,
-          bool LEAN = false>
+          bool LEAN = false, bool FMA = false>
 __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     pkv_decode_kernel(const __grid_constant__ DecodeParams p,
                       const __grid_constant__ CUtensorMap tmap_k,
@@ -1214,6 +1317,9 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     static_assert(BOX_ROWS == 8 || BOX_ROWS == 16, "box rows must be 8 or 16");
     static_assert(!KV8 || (LOAD == kLoadCpAsync && sizeof(T) == 2), "e4m3 K/V: cp.async only");
     static_assert(!(LEAN && KV8), "the lean route serves 16-bit pools");
+    static_assert(!FMA || (G == 4 && LEAN && !KV8 && LOAD == kLoadCpAsync &&
+                           std::is_same<T, __half>::value),
+                  "the CUDA-core stage serves the lean fp16 cp.async route at G = 4");
     constexpr int kBoxesPerStage = kStageTokens / BOX_ROWS;
     static_assert(kPlanPages % kBoxesPerStage == 0, "a plan's first batch is whole stages");
     constexpr int kBoxBytes = BOX_ROWS * kHalfRowBytes;
@@ -1570,6 +1676,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
         it.row_splits = 2;
         it.q_row = it.out_row = -1;
         uint32_t qf[8][2];
+        FmaState fst;
         if (!aborted) {
             bool ok = mbar_wait_bounded(&desc_full[e], (s / kDescSlots) & 1, s_flags);
             ok = __all_sync(0xffffffffu, ok) && s_flags[0] == 0;
@@ -1602,6 +1709,19 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                 qf[ks][0] = tq < G ? qrow[(16 * ks + tc) / 2] : 0u;
                 qf[ks][1] = tq < G ? qrow[(16 * ks + 8 + tc) / 2] : 0u;
             }
+            if constexpr (FMA) {
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    const uint2 qv = *reinterpret_cast<const uint2*>(s_q + e * kQSlotBytes +
+                                                                    g * kRowBytes + lane * 8);
+                    const float2 a = half2_to_float2(qv.x);
+                    const float2 b = half2_to_float2(qv.y);
+                    fst.q[g][0] = a.x;
+                    fst.q[g][1] = a.y;
+                    fst.q[g][2] = b.x;
+                    fst.q[g][3] = b.y;
+                }
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&desc_empty[e]);
             if (s == 0 && threadIdx.x == 0) PKV_CLOCK_STAMP(p, 25, t_entry);
@@ -1617,6 +1737,12 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
         float acc[8][4];
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+        if constexpr (FMA) {
+            fst.m[0] = fst.m[1] = -INFINITY;
+            fst.l[0] = fst.l[1] = 0.f;
+#pragma unroll
+            for (int g = 0; g < 4; ++g) fst.acc[g][0] = fst.acc[g][1] = fst.acc[g][2] = fst.acc[g][3] = 0.f;
+        }
 
         for (int j = warp; j < n_stages; j += kConsumerWarps) {
             const uint32_t gs = gbase + (uint32_t)j;
@@ -1682,6 +1808,9 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                 __syncwarp();
             }
 
+            if constexpr (FMA) {
+                fma_stage(fst, sbase, lane, valid, p.scale_log2);
+            } else {
             // ---- S^T[16 tok x 8 heads] = K[16 x 128] . Q^T
             float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -1748,6 +1877,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                 Ops::mma(acc[mt], a, pb0, pb1);
                 if constexpr (Ops::kSplitP) Ops::mma(acc[mt], a, pl0, pl1);
             }
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty_bar[slot]);
             if (gs == 0 && threadIdx.x == 0) PKV_CLOCK_STAMP(p, 27, t_entry);
@@ -1756,15 +1886,37 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
         stamp_tokens += it.tok_end - it.tok_begin;
 
         // ---- combine the four warps' states of this item
+        float* mbuf = s_merge + buf * DecodeSmem<G>::kMergeFloats;
+        float* mstat = s_mstat + buf * kConsumerWarps * 8;
+        float* lstat = s_lstat + buf * kConsumerWarps * 8;
+        if constexpr (FMA) {
+            // a head's partial sums sit in the 16 lanes of one parity
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+#pragma unroll
+                for (int off = 2; off < 32; off <<= 1)
+                    fst.l[h] += __shfl_xor_sync(0xffffffffu, fst.l[h], off);
+            }
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+#pragma unroll
+                for (int j2 = 0; j2 < 4; ++j2)
+                    mbuf[(warp * G + g) * DecodeSmem<G>::kMergeStride + 4 * lane + j2] = fst.acc[g][j2];
+            }
+            if (lane < 2) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    mstat[warp * 8 + 2 * lane + h] = fst.m[h];
+                    lstat[warp * 8 + 2 * lane + h] = fst.l[h];
+                }
+            }
+        } else {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 4);
             l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 8);
             l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 16);
         }
-        float* mbuf = s_merge + buf * DecodeSmem<G>::kMergeFloats;
-        float* mstat = s_mstat + buf * kConsumerWarps * 8;
-        float* lstat = s_lstat + buf * kConsumerWarps * 8;
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
 #pragma unroll
@@ -1783,6 +1935,7 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                     lstat[warp * 8 + g] = l_run[h];
                 }
             }
+        }
         }
         consumer_bar_sync();
         if (threadIdx.x == 0) PKV_STAMP(p, 5);

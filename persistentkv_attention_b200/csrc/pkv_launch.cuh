@@ -30,6 +30,7 @@ struct LaunchSpec {
     bool pdl = false;  // decode may launch early behind the previous kernel (it waits on it)
     bool kv8 = false;  // e4m3 K/V pools (cp.async producer)
     bool lean = false; // the planned step route (pkv_decode_kernel's LEAN form)
+    bool fma = false;  // CUDA-core consumer math where the route allows it (PKV_MATH_FMA)
     int load = pkv::kLoadCpAsync;  // gather: pkv::kLoadTma or pkv::kLoadCpAsync
     int G;
     int box_rows;
@@ -44,11 +45,11 @@ struct LaunchSpec {
 // diagnostics).
 extern thread_local int t_last_grid;
 
-template <int G, typename T, int BR, int LOAD, bool KV8, bool LEAN>
+template <int G, typename T, int BR, int LOAD, bool KV8, bool LEAN, bool FMA = false>
 pkv_status launch_typed(const LaunchSpec& ls, const CUtensorMap& tk, const CUtensorMap& tv,
                         cudaStream_t stream) {
     using namespace pkv;
-    auto kern = pkv_decode_kernel<G, T, BR, kSlots, LOAD, KV8, LEAN>;
+    auto kern = pkv_decode_kernel<G, T, BR, kSlots, LOAD, KV8, LEAN, FMA>;
     const size_t smem = decode_smem_bytes<G, kSlots>();
     // the device schedule's grid (2 CTAs per SM) must be resident in one wave
     static_assert(decode_fits_two_per_sm<G, kSlots>(), "decode CTA too large for 2 per SM");
@@ -126,6 +127,10 @@ pkv_status launch_g(const LaunchSpec& ls, const CUtensorMap& tk, const CUtensorM
     pkv_status launch_g<T, BR, LOAD, KV8>(const LaunchSpec& ls, const CUtensorMap& tk,          \
                                           const CUtensorMap& tv, cudaStream_t s) {              \
         const bool lean = ls.lean && !KV8;                                                        \
+        if constexpr (std::is_same<T, __half>::value && LOAD == pkv::kLoadCpAsync && !KV8) {      \
+            if (ls.fma && lean && ls.G == 4)                                                      \
+                return launch_typed<4, T, BR, LOAD, KV8, true, true>(ls, tk, tv, s);              \
+        }                                                                                         \
         switch (ls.G) {                                                                           \
             case 1: return lean ? launch_typed<1, T, BR, LOAD, KV8, !KV8>(ls, tk, tv, s)          \
                                 : launch_typed<1, T, BR, LOAD, KV8, false>(ls, tk, tv, s);        \

@@ -143,6 +143,21 @@ def test_gather_mode_switch(lib):
         _native.set_gather_mode(prev)
 
 
+def test_math_mode_switch(lib):
+    """Tensor-core and CUDA-core consumer math are selectable at run time;
+    unknown modes are refused; the default is the tensor-core path."""
+    prev = _native.math_mode()
+    assert prev == "mma"
+    try:
+        for mode in ("fma", "mma"):
+            _native.set_math_mode(mode)
+            assert _native.math_mode() == mode
+        assert lib.pkv_set_math_mode(3) == _native.PKV_ERR_INVALID_ARGUMENT
+        assert b"math mode" in lib.pkv_last_error_message()
+    finally:
+        _native.set_math_mode(prev)
+
+
 def test_phase_stamps_only_in_the_diagnostic_build(lib):
     import os
 

@@ -743,3 +743,48 @@ def test_planned_fewer_groups(groups):
     want = po.paged_decode(c.q_source.float().numpy(), c.k_pages.float().numpy(),
                            c.v_pages.float().numpy(), c.block_table, seq_lens=c.seq_lens)
     assert_close(out, want, "f16", "router groups")
+
+
+@pytest.mark.parametrize("page", [16, 8, 32])
+def test_cuda_core_math_matches_oracle(page):
+    """The CUDA-core consumer math (pkv_set_math_mode(PKV_MATH_FMA): fp32 FMA
+    instead of mma.sync) on the lean route it serves -- host plan, fused merge,
+    G = 4, fp16 -- against the float64 oracle, and against the tensor-core
+    result of the same launch within the same tolerance; other routes keep
+    the tensor-core path under that mode."""
+    from persistentkv_attention_b200.scheduler import build_auto_plan
+
+    lens = [0] + EDGE_LENS + [9000, 4096]
+    c = make_case(lens, hq=32, hkv=8, page_size=page, seed=800 + page, indexed=True)
+    d = c.cuda()
+    want = c.oracle()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    plan = torch.from_numpy(build_auto_plan(c.seq_lens, c.block_table, c.block_table.shape[1],
+                                            page, 8, sms, q_indices=c.q_indices,
+                                            out_indices=c.out_indices)).cuda()
+    outs = {}
+    prev = _native.math_mode()
+    try:
+        for mode in ("mma", "fma"):
+            _native.set_math_mode(mode)
+            for planned in (True, False):
+                ws = torch.empty(ops.auto_workspace_bytes(len(lens), 32, 8) // 4, device="cuda")
+                out = torch.full((c.out_rows, 32, 128), float("nan"), device="cuda",
+                                 dtype=torch.float16)
+                ctr = torch.zeros(len(lens), 8, device="cuda", dtype=torch.int32)
+                ops.paged_attention_auto(d["q_source"], d["k_pages"], d["v_pages"],
+                                         d["block_table"], d["seq_lens"], out, ws,
+                                         d["q_indices"], d["out_indices"], ctr,
+                                         plan=plan if planned else None)
+                torch.cuda.synchronize()
+                assert (ctr == 0).all()
+                assert _native.device_error(clear=True) == 0
+                assert_close(out, want, "f16", f"math={mode} planned={planned}")
+                outs[(mode, planned)] = out
+    finally:
+        _native.set_math_mode(prev)
+    rows = torch.from_numpy(c.out_indices).long().cuda()
+    diff = (outs[("fma", True)][rows].float() - outs[("mma", True)][rows].float()).abs().max()
+    assert diff.item() < MAX_ERR
+    # without a plan the launch is not the lean route: the tensor-core path, same bits
+    assert torch.equal(outs[("fma", False)][rows], outs[("mma", False)][rows])
