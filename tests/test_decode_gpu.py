@@ -455,6 +455,30 @@ def test_sharded_fused_exchange_single_rank():
     finally:
         torch.cuda.synchronize()
         x.close()
+    # Many short rows: CTAs whose group holds many rows exchange one row
+    # after another within the launch.
+    x = ops.Exchange(1, 0, 32, 32, 8)
+    try:
+        lens = [1 + i for i in range(20)] + [3000, 5, 7, 9000]
+        c = make_case(lens, seed=81, indexed=True)
+        d = c.cuda()
+        b = len(lens)
+        bt, sl = pdist.shard_rows(c.block_table, c.seq_lens, 16, 1, 0)
+        out = torch.full((c.out_rows, 32, 128), float("nan"), device="cuda", dtype=torch.float16)
+        counters = torch.zeros(b, 8, device="cuda", dtype=torch.int32)
+        for _ in range(2):
+            ops.paged_attention_sharded(
+                d["q_source"], d["k_pages"], d["v_pages"], torch.from_numpy(bt).cuda(),
+                torch.from_numpy(sl).cuda(), out,
+                torch.empty(ops.auto_workspace_bytes(b, 32, 8) // 4, device="cuda"), counters, x,
+                d["q_indices"], d["out_indices"])
+        torch.cuda.synchronize()
+        assert (counters == 0).all()
+        assert _native.device_error(clear=True) == 0
+        assert_close(out, c.oracle(), "f16", "sharded x1, many rows")
+    finally:
+        torch.cuda.synchronize()
+        x.close()
 
 
 def test_native_host_step():
