@@ -259,6 +259,19 @@ pkv_status pkv_paged_attention_sharded(
     int physical_pages, int page_size, int max_pages,
     pkv_dtype dtype, void* stream);
 
+/* pkv_paged_attention_sharded with a device copy of this rank's host plan
+ * (pkv_build_auto_plan over this rank's block_table / seq_lens, the
+ * launch's q_indices / out_indices and `groups`); the plan's rules are those
+ * of pkv_paged_attention_auto_planned.  No counterpart in the reference. */
+pkv_status pkv_paged_attention_sharded_planned(
+    const void* q_source, const void* k_pages, const void* v_pages,
+    const int32_t* block_table, const int32_t* seq_lens,
+    const int32_t* q_indices, const int32_t* out_indices, void* output,
+    void* workspace, size_t workspace_bytes, int32_t* merge_counters,
+    pkv_exchange* exchange, const void* plan, size_t plan_bytes, int groups,
+    int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim,
+    int physical_pages, int page_size, int max_pages, pkv_dtype dtype, void* stream);
+
 /* ---- e4m3 (FP8) K/V cache ----
  * pkv_paged_attention_auto over pools of e4m3 values (one byte per element,
  * [P][Hkv][page][128]) with per-tensor scales: K = k_scale * e4m3 value,

@@ -162,6 +162,11 @@ SIGNATURES = {
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, _P, c_int, c_int, c_int, c_int,
          c_int, c_int, c_int, c_int, c_int, c_int, _P],
     ),
+    "pkv_paged_attention_sharded_planned": (
+        c_int,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, _P, _P, c_size_t, c_int, c_int, c_int,
+         c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, _P],
+    ),
     "pkv_paged_attention_workqueue_noalloc": (
         c_int,
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int,

@@ -1208,18 +1208,26 @@ pkv_status pkv_exchange_destroy(pkv_exchange* x) {
     return ok_status();
 }
 
-pkv_status pkv_paged_attention_sharded(
+static pkv_status sharded_common(
     const void* q_source, const void* k_pages, const void* v_pages, const int32_t* block_table,
     const int32_t* seq_lens, const int32_t* q_indices, const int32_t* out_indices, void* output,
     void* workspace, size_t workspace_bytes, int32_t* merge_counters, pkv_exchange* exchange,
     int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim, int physical_pages,
-    int page_size, int max_pages, pkv_dtype dtype, void* stream) {
+    int page_size, int max_pages, pkv_dtype dtype, void* stream, const void* plan, size_t plan_bytes,
+    int groups) {
     if (exchange == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "exchange must not be null");
     if (!exchange->connected)
         return fail(PKV_ERR_INVALID_ARGUMENT, "exchange is not connected to its peers");
     if (output == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "output must be a CUDA tensor");
     if (merge_counters == nullptr)
         return fail(PKV_ERR_INVALID_ARGUMENT, "sharded decode requires merge_counters");
+    if (plan != nullptr) {
+        const size_t need = pkv_auto_plan_bytes(Hkv, 0);
+        if (need == 0 || plan_bytes < need) {
+            return fail(PKV_ERR_INVALID_ARGUMENT, "plan holds %zu bytes but %zu are needed",
+                        plan_bytes, need);
+        }
+    }
     if (B > exchange->bcap)
         return fail(PKV_ERR_CAPACITY, "batch %d exceeds the exchange's capacity %d", B,
                     exchange->bcap);
@@ -1233,7 +1241,34 @@ pkv_status pkv_paged_attention_sharded(
     Common c{q_source, k_pages, v_pages, block_table, B, Hq, Hkv, head_dim,
              physical_pages, page_size, max_pages, dtype};
     return auto_common(c, seq_lens, q_indices, out_indices, output, nullptr, workspace,
-                       workspace_bytes, merge_counters, q_rows, out_rows, stream, exchange);
+                       workspace_bytes, merge_counters, q_rows, out_rows, stream, exchange, false,
+                       nullptr, plan, groups);
+}
+
+pkv_status pkv_paged_attention_sharded(
+    const void* q_source, const void* k_pages, const void* v_pages, const int32_t* block_table,
+    const int32_t* seq_lens, const int32_t* q_indices, const int32_t* out_indices, void* output,
+    void* workspace, size_t workspace_bytes, int32_t* merge_counters, pkv_exchange* exchange,
+    int B, int q_rows, int out_rows, int Hq, int Hkv, int head_dim, int physical_pages,
+    int page_size, int max_pages, pkv_dtype dtype, void* stream) {
+    return sharded_common(q_source, k_pages, v_pages, block_table, seq_lens, q_indices,
+                          out_indices, output, workspace, workspace_bytes, merge_counters, exchange,
+                          B, q_rows, out_rows, Hq, Hkv, head_dim, physical_pages, page_size,
+                          max_pages, dtype, stream, nullptr, 0, 0);
+}
+
+pkv_status pkv_paged_attention_sharded_planned(
+    const void* q_source, const void* k_pages, const void* v_pages, const int32_t* block_table,
+    const int32_t* seq_lens, const int32_t* q_indices, const int32_t* out_indices, void* output,
+    void* workspace, size_t workspace_bytes, int32_t* merge_counters, pkv_exchange* exchange,
+    const void* plan, size_t plan_bytes, int groups, int B, int q_rows, int out_rows, int Hq,
+    int Hkv, int head_dim, int physical_pages, int page_size, int max_pages, pkv_dtype dtype,
+    void* stream) {
+    if (plan == nullptr) return fail(PKV_ERR_INVALID_ARGUMENT, "plan must be a device pointer");
+    return sharded_common(q_source, k_pages, v_pages, block_table, seq_lens, q_indices,
+                          out_indices, output, workspace, workspace_bytes, merge_counters, exchange,
+                          B, q_rows, out_rows, Hq, Hkv, head_dim, physical_pages, page_size,
+                          max_pages, dtype, stream, plan, plan_bytes, groups);
 }
 
 }  // extern "C"

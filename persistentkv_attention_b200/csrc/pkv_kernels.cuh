@@ -1655,9 +1655,22 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
     uint32_t gbase = 0;
     int buf = 0;
     bool aborted = false;
-    // step number of a sharded launch: advanced only after every CTA of the
-    // launch has finished, so all CTAs read the same value here
+    // Step number of a sharded launch.  Every CTA's consumers read it here,
+    // then thread 0 counts the CTA as having read it (acquire-release: the
+    // reads come first); the CTA that counts last advances it for the next
+    // launch, which starts only after this one has finished.  Counting at
+    // entry keeps fences and atomics off the CTAs' exit path.
     const unsigned xg_epoch = (!LEAN && p.xg_world > 0) ? ld_relaxed_gpu_u32(p.xg_counters) : 0u;
+    if (!LEAN && p.xg_world > 0) {
+        consumer_bar_sync();
+        if (threadIdx.x == 0) {
+            const int seen = atom_add_acq_rel_gpu(reinterpret_cast<int32_t*>(p.xg_counters + 1), 1);
+            if (seen == (int)gridDim.x - 1) {
+                p.xg_counters[1] = 0u;
+                atomicAdd(p.xg_counters, 1u);
+            }
+        }
+    }
     const bool state_mode = !LEAN && p.state_out != nullptr;
     const bool xg_mode = !LEAN && p.xg_world > 0;
     long long stamp_tokens = 0;  // diagnostic build: tokens this CTA streamed
@@ -2103,19 +2116,6 @@ __global__ void __launch_bounds__(kThreads, PKV_MIN_CTAS_PER_SM)
                     st, unused);
                 fence_proxy_async_smem();
                 consumer_bar_sync();
-            }
-        }
-    }
-    if (!LEAN && p.xg_world > 0) {
-        // the last CTA to finish advances the step number for the next launch
-        consumer_bar_sync();
-        if (threadIdx.x == 0) {
-            __threadfence();
-            const unsigned done = atomicAdd(p.xg_counters + 1, 1u);
-            if (done == gridDim.x - 1) {
-                p.xg_counters[1] = 0u;
-                __threadfence();
-                atomicAdd(p.xg_counters, 1u);
             }
         }
     }

@@ -421,11 +421,13 @@ def exchange_bytes(world: int, max_batch: int, hq: int, hkv: int) -> int:
 
 def paged_attention_sharded(q_source, k_pages, v_pages, block_table, seq_lens, output, workspace,
                             merge_counters, exchange: Exchange, q_indices=None,
-                            out_indices=None) -> None:
+                            out_indices=None, plan=None, groups: int = 0) -> None:
     """One step of sequence-sharded decode with the state exchange fused into
     the kernel: ``block_table`` / ``seq_lens`` hold this rank's page range of
     every row; every rank gets the merged ``output``.  All ranks must call it
-    with the same batch, in the same order.  No counterpart in the reference."""
+    with the same batch, in the same order.  ``plan``: a device int32 copy of
+    this rank's host plan (``scheduler.build_auto_plan`` over the same rows,
+    indices and ``groups``).  No counterpart in the reference."""
     _check_tensor(q_source, "q_source", tuple(_DTYPES), 3)
     hkv, physical_pages = _check_kv(q_source, k_pages, v_pages, k_pages.size(2))
     _check_tensor(block_table, "block_table", torch.int32, 2)
@@ -451,6 +453,15 @@ def paged_attention_sharded(q_source, k_pages, v_pages, block_table, seq_lens, o
             ptrs.append(t.data_ptr())
     _check_supported_gqa(hq, hkv)
     ws_ptr, ws_bytes = _workspace(workspace)
+    if plan is not None:
+        _check_tensor(plan, "plan", torch.int32, 1)
+        _native.check(_native.load().pkv_paged_attention_sharded_planned(
+            q_source.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), block_table.data_ptr(),
+            seq_lens.data_ptr(), ptrs[0], ptrs[1], output.data_ptr(), ws_ptr, ws_bytes,
+            merge_counters.data_ptr(), exchange.ptr, plan.data_ptr(), plan.numel() * 4,
+            int(groups), b, q_source.size(0), output.size(0), hq, hkv, d, physical_pages,
+            k_pages.size(2), block_table.size(1), _DTYPES[q_source.dtype], _stream()))
+        return
     _native.check(_native.load().pkv_paged_attention_sharded(
         q_source.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), block_table.data_ptr(),
         seq_lens.data_ptr(), ptrs[0], ptrs[1], output.data_ptr(), ws_ptr, ws_bytes,

@@ -249,7 +249,8 @@ class DecodeEngine:
         counters = self._counters[: plan.batch * self.hkv].view(plan.batch, self.hkv)
         ops.paged_attention_sharded(
             q_source, self.k_pages, self.v_pages, f["block_table"], f["seq_lens"], out,
-            self._workspace, counters, exchange, f["q_indices"], f["out_indices"])
+            self._workspace, counters, exchange, f["q_indices"], f["out_indices"],
+            plan=f.get("plan"), groups=plan.host.groups)
 
     def _step_host_native(self, seq_lens, block_rows, q_host, out_host, scratch):
         seq = np.ascontiguousarray(seq_lens, dtype=np.int32)

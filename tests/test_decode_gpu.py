@@ -430,6 +430,22 @@ def test_sharded_fused_exchange_single_rank():
             torch.cuda.synchronize()
             assert (counters == 0).all()
             assert_close(out, c.oracle(), "f16", f"sharded x1 B{b}")
+            # with this rank's host plan: the same schedule, the same bits
+            from persistentkv_attention_b200.scheduler import build_auto_plan
+
+            sms = torch.cuda.get_device_properties(0).multi_processor_count
+            plan = torch.from_numpy(build_auto_plan(sl, bt, bt.shape[1], 16, 8, sms,
+                                                    q_indices=c.q_indices,
+                                                    out_indices=c.out_indices)).cuda()
+            planned = torch.full_like(out, float("nan"))
+            ops.paged_attention_sharded(d["q_source"], d["k_pages"], d["v_pages"], bt_d, sl_d,
+                                        planned, ws, counters, x, d["q_indices"],
+                                        d["out_indices"], plan=plan)
+            torch.cuda.synchronize()
+            assert (counters == 0).all()
+            assert _native.device_error(clear=True) == 0
+            rows = torch.from_numpy(c.out_indices).long().cuda()
+            assert torch.equal(planned[rows], out[rows])
             graph = torch.cuda.CUDAGraph()
             s = torch.cuda.Stream()
             with torch.cuda.stream(s):
