@@ -212,6 +212,11 @@ def test_newer_entry_points_validate_before_touching_a_device(lib):
                                          1 << 20, FAKE, None, 1, 1, 1, 32, 8, 128, 64, 16, 4, 0,
                                          None)
     assert st == 1 and b"exchange" in lib.pkv_last_error_message()
+    # planned sharded step: the plan is checked before anything else
+    st = lib.pkv_paged_attention_sharded_planned(
+        FAKE, FAKE, FAKE, FAKE, FAKE, None, None, FAKE, FAKE, 1 << 20, FAKE, FAKE, None, 0, 0,
+        1, 1, 1, 32, 8, 128, 64, 16, 4, 0, None)
+    assert st == 1 and b"plan" in lib.pkv_last_error_message()
     # native engine: head_dim and dtype are checked first
     eng = P()
     assert lib.pkv_engine_create(FAKE, FAKE, 64, 32, 8, 64, 16, 0, 8, 32, ctypes.byref(eng)) == 2
