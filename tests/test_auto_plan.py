@@ -12,10 +12,10 @@ from persistentkv_attention_b200.scheduler import auto_groups, build_auto_plan, 
 HEADER, ENTRY, PAGES = 16, 20, 8
 
 
-def schedule(lens, table, page, hkv, sms, q_idx=None, o_idx=None):
+def schedule(lens, table, page, hkv, sms, q_idx=None, o_idx=None, groups=0):
     """The kernel's schedule (auto_init / auto_item) restated: per group the
-    entry the plan must hold."""
-    ng = max(1, (2 * sms) // hkv)
+    entry the plan must hold (``groups`` 0: the maximum group count)."""
+    ng = groups or max(1, (2 * sms) // hkv)
     b = len(lens)
     tiles = [(n + 31) // 32 for n in lens]
     prefix = np.concatenate([[0], np.cumsum(tiles)]).astype(np.int64)
@@ -92,3 +92,20 @@ def test_plan_rejects_lengths_beyond_the_table():
     with pytest.raises(_native.PkvError):
         build_auto_plan([100, 5000], np.zeros((2, 4), np.int32), 4, 16, 8, 148)
     assert lib.pkv_auto_plan_bytes(0, 148) == 0
+
+
+@pytest.mark.parametrize("groups", [1, 5, 18, 36])
+def test_plan_for_fewer_groups(groups):
+    """A router's smaller group count: the header records it and every entry
+    follows the schedule cut into that many groups."""
+    lens = [9000, 33, 4096, 1, 700, 12000, 0, 2500]
+    rng = np.random.default_rng(groups)
+    width = max((n + 15) // 16 for n in lens)
+    table = rng.integers(0, 5000, size=(len(lens), width)).astype(np.int32)
+    ng, T, entries = schedule(lens, table, 16, 8, 148, groups=groups)
+    plan = build_auto_plan(lens, table, width, 16, 8, 148, groups=groups)
+    assert list(plan[:4]) == [0x504B5650, groups, len(lens), T]
+    got = plan[HEADER:HEADER + groups * ENTRY].reshape(groups, ENTRY)
+    assert np.array_equal(got, np.asarray(entries, np.int32))
+    with pytest.raises(_native.PkvError):
+        build_auto_plan(lens, table, width, 16, 8, 148, groups=auto_groups(8, 148) + 1)
