@@ -324,7 +324,12 @@ def run_reference_arm(args) -> None:
         "ms_per_step": 1000.0 * secs / max(1, done), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fp16-quantised inputs)",
         "data": "synthetic", "config": {"workload": f"{args.workload}: {w['desc']}",
-                                        "hq": HQ, "hkv": hkv, "head_dim": D, "page_size": PAGE},
+                                        "hq": HQ, "hkv": hkv, "gqa_group": HQ // hkv,
+                                        "head_dim": D, "page_size": PAGE,
+                                        "active_per_gpu": w["max_active"],
+                                        "parallelism": "host cores: the reference's "
+                                                       "cpu_gqa_attention over (row, KV head) "
+                                                       "groups"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
                          "sample": f"{done} decode steps of the trace, (row, KV head) groups "
                                     f"in parallel"},
