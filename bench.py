@@ -399,12 +399,20 @@ class Config:
                 e.reserve(p.batch, p.host.total_slots)
                 e.run(p, q_pool, ol)
             self.engine.run(p, q_pool, o)
+            # the layers' launches chain with programmatic dependent launch, as
+            # in a model step: each starts behind the previous layer's tail
+            from persistentkv_attention_b200 import _native
+
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.stream(stream):
-                with torch.cuda.graph(g, stream=stream):
-                    self.engine.run(p, q_pool, o)
-                    for e, ol in zip(self.layer_engines, outs_l):
-                        e.run(p, q_pool, ol)
+            _native.set_dependent_launch(True)
+            try:
+                with torch.cuda.stream(stream):
+                    with torch.cuda.graph(g, stream=stream):
+                        self.engine.run(p, q_pool, o)
+                        for e, ol in zip(self.layer_engines, outs_l):
+                            e.run(p, q_pool, ol)
+            finally:
+                _native.set_dependent_launch(False)
             self.graphs.append(g)
         torch.cuda.synchronize()
         self.sched = [i % n_distinct for i in range(self.warmup + self.steps_timed)]
@@ -649,8 +657,8 @@ def run_engine_arm(args) -> None:
             per_config[f"{name}@{LAYERS} layers back to back"] = dict(
                 cfg.summary(peak), correctness_max_abs_err=err,
                 timing=f"one CUDA-event interval per step of {LAYERS} layers (distinct pools, "
-                       f"{LAYERS} decode launches back to back), divided by {LAYERS}; L2 "
-                       "flushed before each step")
+                       f"{LAYERS} decode launches back to back, chained with programmatic "
+                       f"dependent launch), divided by {LAYERS}; L2 flushed before each step")
             cfg.release()
             torch.cuda.empty_cache()
         code = _native.device_error(clear=True)

@@ -109,6 +109,16 @@ typedef enum pkv_math {
 pkv_status pkv_set_math_mode(pkv_math mode);
 pkv_math pkv_get_math_mode(void);
 
+/* enable != 0: later device-scheduled decode launches (pkv_paged_attention_auto,
+ * _auto_planned) go out with programmatic dependent launch.  Their CTAs may
+ * start while the previous kernel in the stream finishes; each waits for it
+ * (griddepcontrol.wait) before reading any input.  For a model step that
+ * chains decode launches (one per layer), this hides each launch behind the
+ * previous layer's tail.  Launches already captured in a CUDA graph keep
+ * their setting.  No counterpart in the reference. */
+pkv_status pkv_set_dependent_launch(int enable);
+int pkv_get_dependent_launch(void);
+
 /* Diagnostic build only (libpkv_b200_stamps.so, compiled with
  * PKV_PHASE_STAMPS): copies the per-CTA %globaltimer stamps of the last
  * decode launch on this thread -- PKV_STAMPS_PER_CTA values per CTA:

@@ -96,6 +96,8 @@ SIGNATURES = {
     "pkv_get_gather_mode": (c_int, []),
     "pkv_set_math_mode": (c_int, [c_int]),
     "pkv_get_math_mode": (c_int, []),
+    "pkv_set_dependent_launch": (c_int, [c_int]),
+    "pkv_get_dependent_launch": (c_int, []),
     "pkv_phase_stamps": (c_int, [POINTER(ctypes.c_uint64), c_int, POINTER(c_int)]),
     "pkv_paged_attention": (
         c_int,
@@ -275,6 +277,16 @@ def set_math_mode(mode: str) -> None:
 def math_mode() -> str:
     value = load().pkv_get_math_mode()
     return {v: k for k, v in MATH_MODES.items()}[value]
+
+
+def set_dependent_launch(enable: bool) -> None:
+    """Programmatic dependent launch for later device-scheduled decode
+    launches (``pkv_set_dependent_launch``)."""
+    check(load().pkv_set_dependent_launch(1 if enable else 0))
+
+
+def dependent_launch() -> bool:
+    return bool(load().pkv_get_dependent_launch())
 
 
 def phase_stamps(max_ctas: int = 4096):

@@ -65,6 +65,7 @@ static_assert((int)PKV_GATHER_TMA == kLoadTma && (int)PKV_GATHER_CP_ASYNC == kLo
               "gather enum values are the kernel's LOAD template values");
 std::atomic<int> g_gather_mode{PKV_GATHER_DEFAULT};
 std::atomic<int> g_math_mode{PKV_MATH_MMA};
+std::atomic<int> g_dependent_launch{0};
 
 }  // namespace
 
@@ -599,6 +600,13 @@ pkv_math pkv_get_math_mode(void) {
     return (pkv_math)g_math_mode.load(std::memory_order_relaxed);
 }
 
+pkv_status pkv_set_dependent_launch(int enable) {
+    g_dependent_launch.store(enable != 0 ? 1 : 0, std::memory_order_relaxed);
+    return ok_status();
+}
+
+int pkv_get_dependent_launch(void) { return g_dependent_launch.load(std::memory_order_relaxed); }
+
 pkv_status pkv_phase_stamps(uint64_t* out, int max_ctas, int* n_ctas) {
 #ifdef PKV_PHASE_STAMPS
     if (out == nullptr || n_ctas == nullptr || max_ctas <= 0)
@@ -876,7 +884,7 @@ pkv_status auto_common(const Common& c, const int32_t* seq_lens, const int32_t* 
             return fail(PKV_ERR_MISALIGNED, "plan must be 16-byte aligned");
         ls.dp.plan = static_cast<const int32_t*>(plan);
     }
-    ls.pdl = pdl;
+    ls.pdl = pdl || g_dependent_launch.load(std::memory_order_relaxed) != 0;
     // The lean kernel: a host plan, the fused merge deferred to the CTA's end
     // (a row's NG * G merge weights fit the CTA's buffer), output rows.
     ls.lean = plan != nullptr && state_out == nullptr && xg == nullptr &&

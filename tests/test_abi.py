@@ -158,6 +158,18 @@ def test_math_mode_switch(lib):
         _native.set_math_mode(prev)
 
 
+def test_dependent_launch_switch(lib):
+    """Programmatic dependent launch of the device-scheduled route is off by
+    default and can be switched."""
+    assert not _native.dependent_launch()
+    try:
+        _native.set_dependent_launch(True)
+        assert _native.dependent_launch()
+    finally:
+        _native.set_dependent_launch(False)
+    assert lib.pkv_get_dependent_launch() == 0
+
+
 def test_phase_stamps_only_in_the_diagnostic_build(lib):
     import os
 

@@ -828,3 +828,51 @@ def test_cuda_core_math_matches_oracle(page):
     assert diff.item() < MAX_ERR
     # without a plan the launch is not the lean route: the tensor-core path, same bits
     assert torch.equal(outs[("fma", False)][rows], outs[("mma", False)][rows])
+
+
+def test_dependent_launch_chain_in_a_graph():
+    """Decode launches chained with programmatic dependent launch (one per
+    model layer, each over its own pool, captured in one CUDA graph): each
+    waits for the previous kernel before reading, so every layer's output
+    equals its own launch run alone, and the oracle."""
+    from persistentkv_attention_b200.serving import DecodeEngine
+
+    lens = [4096, 700, 9000, 33, 2048, 1, 5000, 300]
+    cases = [make_case(lens, seed=900 + i, indexed=True) for i in range(3)]
+    dev = [c.cuda() for c in cases]
+    engines = [DecodeEngine(d["k_pages"], d["v_pages"], 32) for d in dev]
+    c0 = cases[0]
+    plans = [e.upload(e.plan_step(c0.seq_lens, c.block_table, q_indices=c0.q_indices))
+             for e, c in zip(engines, cases)]
+    q = dev[0]["q_source"]
+    alone = []
+    for e, p in zip(engines, plans):
+        o = torch.full((len(lens), 32, 128), float("nan"), device="cuda", dtype=torch.float16)
+        e.run(p, q, o)
+        alone.append(o)
+    torch.cuda.synchronize()
+    outs = [torch.full_like(a, float("nan")) for a in alone]
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    _native.set_dependent_launch(True)
+    try:
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for e, p, o in zip(engines, plans, outs):
+                    e.run(p, q, o)
+    finally:
+        _native.set_dependent_launch(False)
+    for _ in range(3):
+        for o in outs:
+            o.fill_(float("nan"))
+        g.replay()
+        torch.cuda.synchronize()
+        for a, o in zip(alone, outs):
+            assert torch.equal(a, o)
+    assert _native.device_error(clear=True) == 0
+    for c, o in zip(cases, outs):
+        # every layer reads the first case's q rows (the plans carry its q_indices)
+        want = po.paged_decode(c0.q_source.float().numpy(), c.k_pages.float().numpy(),
+                               c.v_pages.float().numpy(), c.block_table, seq_lens=c0.seq_lens,
+                               q_indices=c0.q_indices)
+        assert_close(o, want, "f16", "dependent-launch chain")
