@@ -462,14 +462,17 @@ pkv_status pkv_build_auto_plan(const int32_t* seq_lens, const int32_t* block_tab
     plan[1] = NG;
     plan[2] = B;
     plan[3] = (int32_t)T;
-    int b_lo = 0;  // rows are visited in order: first row whose last group is >= g
+    // Both bounds only move forward as g grows (gf and gl never decrease
+    // along the rows), so the plan costs O(B + NG), not O(B * NG).
+    int b_lo = 0;     // first row whose last group is >= g
+    int b_last = -1;  // last row whose first group is <= g
     for (int g = 0; g < NG; ++g) {
         int32_t* e = plan + kPlanHeaderWords + (size_t)g * kPlanEntryWords;
         for (int i = 0; i < kPlanEntryWords; ++i) e[i] = -1;
         while (b_lo < B && gl[b_lo] < g) ++b_lo;
+        while (b_last + 1 < B && gf[b_last + 1] <= g) ++b_last;
         if (b_lo >= B) continue;
-        int b_hi = -1;
-        for (int b = b_lo; b < B && gf[b] <= g; ++b) b_hi = b;
+        const int b_hi = b_last >= b_lo ? b_last : -1;
         const int b = b_lo;
         e[0] = b;
         e[1] = b_hi >= b ? b_hi + 1 : b;

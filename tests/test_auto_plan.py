@@ -109,3 +109,18 @@ def test_plan_for_fewer_groups(groups):
     assert np.array_equal(got, np.asarray(entries, np.int32))
     with pytest.raises(_native.PkvError):
         build_auto_plan(lens, table, width, 16, 8, 148, groups=auto_groups(8, 148) + 1)
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_plan_of_a_large_ragged_batch(seed):
+    """Hundreds of rows, many of them empty or shorter than a tile, against the
+    restated schedule (the builder walks rows and groups in one pass)."""
+    rng = np.random.default_rng(seed)
+    lens = rng.choice([0, 1, 17, 31, 33, 200, 1500, 7000], size=300).tolist()
+    width = max(1, max((n + 15) // 16 for n in lens))
+    table = rng.integers(0, 50000, size=(len(lens), width)).astype(np.int32)
+    for hkv in (8, 4):
+        ng, T, entries = schedule(lens, table, 16, hkv, 148)
+        plan = build_auto_plan(lens, table, width, 16, hkv, 148)
+        got = plan[HEADER:HEADER + ng * ENTRY].reshape(ng, ENTRY)
+        assert np.array_equal(got, np.asarray(entries, np.int32))
