@@ -519,20 +519,33 @@ int pkv_choose_groups(const pkv_router_params* p, const int32_t* lengths, int n,
         T += tiles[i];
         bytes += (double)len * p->hkv * p->head_dim * 2.0 * p->elem_bytes;
     }
+    // Rows by tile count, longest first, with their tile prefixes: a row of
+    // t tiles spans at most floor(t * ng / T) + 2 groups, so each candidate
+    // only visits rows until that bound cannot beat the most pieces found.
+    std::vector<long long> prefix(n);
+    std::vector<int> order(n);
+    {
+        long long P = 0;
+        for (int i = 0; i < n; ++i) {
+            prefix[i] = P;
+            P += tiles[i];
+            order[i] = i;
+        }
+        std::stable_sort(order.begin(), order.end(),
+                         [&](int a, int b) { return tiles[a] > tiles[b]; });
+    }
     int best = ng_max;
     double best_us = 1e300;
     for (int ng = ng_max; ng >= std::max(1, ng_max / 8); --ng) {
         // most pieces of one row: the groups its first and last tile fall in
         int pieces = 1;
         if (T > 0) {
-            long long P = 0;
-            for (int i = 0; i < n; ++i) {
-                if (tiles[i] > 0) {
-                    const long long gf = ((P + 1) * ng - 1) / T;
-                    const long long gl = ((P + tiles[i]) * ng - 1) / T;
-                    pieces = std::max(pieces, (int)(gl - gf + 1));
-                }
-                P += tiles[i];
+            for (int k = 0; k < n; ++k) {
+                const int i = order[k];
+                if (tiles[i] == 0 || (long long)tiles[i] * ng / T + 2 <= pieces) break;
+                const long long gf = ((prefix[i] + 1) * ng - 1) / T;
+                const long long gl = ((prefix[i] + tiles[i]) * ng - 1) / T;
+                pieces = std::max(pieces, (int)(gl - gf + 1));
             }
         }
         const double gbps = std::min(p->read_gbps, (double)ng * p->hkv * p->dev_cta_gbps);

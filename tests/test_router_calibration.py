@@ -7,6 +7,7 @@ on that file."""
 import json
 
 import numpy as np
+import pytest
 
 from persistentkv_attention_b200 import calibrate
 from persistentkv_attention_b200.scheduler import Router
@@ -47,3 +48,33 @@ def test_fit_reproduces_the_committed_constants():
     assert err ** 0.5 < 0.05
     for key in ("read_gbps", "dev_cta_gbps"):
         assert abs(fitted[key] - params[key]) <= 0.02 * params[key], key
+
+
+def _choose_groups_exhaustive(params, lengths, sms=148, hkv=8):
+    """The step-time model over every candidate group count, every row."""
+    ng_max = max(1, (2 * sms) // hkv)
+    bytes_ = float(sum(max(0, int(n)) for n in lengths)) * hkv * 128 * 2 * 2
+    best, best_us = ng_max, float("inf")
+    for ng in range(ng_max, max(1, ng_max // 8) - 1, -1):
+        s = calibrate.Sample("x", ng, 0.0, bytes_, calibrate.max_pieces(lengths, ng))
+        us = calibrate.predict(params, s, hkv)
+        if us < best_us:
+            best, best_us = ng, us
+    return best, best_us
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_choose_groups_matches_the_exhaustive_model(seed):
+    """pkv_choose_groups visits only the rows that can hold the most pieces;
+    its choice and estimate equal the model evaluated over every row."""
+    rng = np.random.default_rng(seed)
+    router = Router.b200(32, 8, sm_count=148)
+    params = _params()
+    for n in (1, 3, 8, 64, 500):
+        lens = rng.choice([0, 1, 31, 33, 512, 4096, 30000], size=n).tolist()
+        if not any(lens):
+            lens[0] = 100
+        ng, est = router.choose_groups(lens)
+        want_ng, want_us = _choose_groups_exhaustive(params, lens)
+        assert ng == want_ng, (n, ng, want_ng)
+        assert abs(est - want_us) < 1e-9 * max(1.0, want_us)
